@@ -1,0 +1,81 @@
+/*
+ * dt_attn.h -- C ABI of the sm_100a Decision Transformer attention library
+ * (libdt_attn_sm100.so).
+ *
+ * The library replaces the attention core of DecisionTransformerAttention in
+ * FujiM3/RL_for_Mario (model/model_decision_transformer.py:137-249).  Every
+ * entry point takes raw device pointers, sizes, element strides and a
+ * cudaStream_t (passed as void*), allocates no device memory, launches
+ * asynchronously on that stream and returns a status code.  On a nonzero
+ * status, dt_last_error() returns a message for the calling thread.
+ *
+ * Layout conventions (element strides; the innermost dimension, D, is
+ * contiguous):
+ *   q, o       [B, S, Hq, D]   -- the reference's q_proj(x).view(B, S, Hq, D)
+ *   k, v       [B, S, Hkv, D]  -- k_proj / v_proj views (:175-177)
+ *   cos, sin   [rows, D] fp32  -- precompute_freqs_cis tables (:93-99), already
+ *                                 sliced so that row i is the angle of token i
+ *                                 of this call (:440-443)
+ *   pad_len    [B] int32       -- number of leading padding tokens per sample
+ *                                 (left padding, attention_mask == 0 prefix)
+ */
+#ifndef DT_ATTN_H_
+#define DT_ATTN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define DT_OK 0
+#define DT_ERR_INVALID 1     /* bad pointer, size, stride or alignment */
+#define DT_ERR_UNSUPPORTED 2 /* shape / dtype / device not supported */
+#define DT_ERR_CUDA 3        /* a CUDA runtime call failed */
+#define DT_ERR_DEVICE 4      /* a kernel reported a device-side error */
+
+/* Element types. */
+#define DT_DTYPE_BF16 0
+#define DT_DTYPE_FP16 1
+#define DT_DTYPE_FP32 2
+
+/* Library version, (major << 16) | minor. */
+int dt_version(void);
+
+/* Message describing the last nonzero status returned on this thread. */
+const char* dt_last_error(void);
+
+/*
+ * Fused causal grouped-query prefill attention.
+ *
+ * Replaces, for one layer, the prefill branch of
+ * DecisionTransformerAttention.forward (model_decision_transformer.py:179-224):
+ * RoPE on q and k (apply_rotary_pos_emb, :108-117, when apply_rope != 0),
+ * repeat_kv (:121-130, never materialised here), and
+ * F.scaled_dot_product_attention with the causal mask and the additive
+ * (1 - attention_mask) * -1e9 padding mask (:206-224), scale 1/sqrt(D) unless
+ * `scale` > 0 is given.  Writes the attention output (before o_proj, :247) to o.
+ *
+ * Supported: dtype BF16 or FP16, D in {32, 64}, Hq % Hkv == 0,
+ * Hq / Hkv <= 128.  Base pointers 16-byte aligned, strides multiples of 8
+ * elements, cos/sin rows >= S.
+ */
+int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const float* cos_tab,
+                    const float* sin_tab, int cos_rows, int64_t cos_stride, const int32_t* pad_len, int B,
+                    int S, int Hq, int Hkv, int D, int64_t q_sb, int64_t q_ss, int64_t q_sh, int64_t k_sb,
+                    int64_t k_ss, int64_t k_sh, int64_t v_sb, int64_t v_ss, int64_t v_sh, int64_t o_sb,
+                    int64_t o_ss, int64_t o_sh, float scale, int apply_rope, int dtype, void* stream);
+
+/*
+ * Synchronises `stream`, then returns and clears the device status word that
+ * the kernels of this library write when a bounded wait runs out or a
+ * device-side check fails (0 = no error).  Used by tests and debugging.
+ */
+int dt_device_status(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DT_ATTN_H_ */

@@ -1,0 +1,191 @@
+// C-ABI entry points (include/dt_attn.h): argument validation, TMA tensor-map
+// encoding and kernel dispatch.  No entry point allocates device memory.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/dt_attn.h"
+#include "dt_internal.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(DT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Device status word, one per device context (static device memory).
+__device__ int g_dev_status;
+
+constexpr int kMaxDevices = 64;
+int* g_status_ptr[kMaxDevices] = {};
+int g_cc_major[kMaxDevices] = {};
+std::mutex g_dev_mu;
+
+// Resolves, once per device, the status word's device address and the
+// compute capability.
+int device_setup(int* dev_out, int** status_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(DT_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_status_ptr[dev]) {
+    int major = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_dev_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    g_cc_major[dev] = major;
+    g_status_ptr[dev] = static_cast<int*>(p);
+  }
+  *dev_out = dev;
+  *status_out = g_status_ptr[dev];
+  return DT_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 4-D map over a [B, S, H, D] tensor (dims innermost first: D, H, S, B).
+int encode_bshd(CUtensorMap* map, const void* base, bool is16, int B, int S, int H, int D, int64_t sb,
+                int64_t ss, int64_t sh, uint32_t box_h, uint32_t box_s, const char* name) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const int esz = 2;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)(sh * esz), (cuuint64_t)(ss * esz), (cuuint64_t)(sb * esz)};
+  cuuint32_t box[4] = {(cuuint32_t)D, box_h, box_s, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle swz = (D * esz == 64) ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = enc(map, is16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DT_ERR_INVALID, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name, (int)r);
+  return DT_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int dt_version(void) { return (0 << 16) | 1; }
+
+const char* dt_last_error(void) { return g_err; }
+
+int dt_device_status(void* stream) {
+  int dev = 0;
+  int* status = nullptr;
+  int rc = device_setup(&dev, &status);
+  if (rc) return -rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return -cuda_fail(e, "cudaStreamSynchronize");
+  int value = 0;
+  e = cudaMemcpyFromSymbol(&value, g_dev_status, sizeof(int));
+  if (e != cudaSuccess) return -cuda_fail(e, "cudaMemcpyFromSymbol");
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(g_dev_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return -cuda_fail(e, "cudaMemcpyToSymbol");
+  return value;
+}
+
+int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const float* cos_tab,
+                    const float* sin_tab, int cos_rows, int64_t cos_stride, const int32_t* pad_len, int B,
+                    int S, int Hq, int Hkv, int D, int64_t q_sb, int64_t q_ss, int64_t q_sh, int64_t k_sb,
+                    int64_t k_ss, int64_t k_sh, int64_t v_sb, int64_t v_ss, int64_t v_sh, int64_t o_sb,
+                    int64_t o_ss, int64_t o_sh, float scale, int apply_rope, int dtype, void* stream) {
+  if (!q || !k || !v || !o) return fail(DT_ERR_INVALID, "dt_attn_prefill: null q/k/v/o pointer");
+  if (B < 1 || S < 1 || Hq < 1 || Hkv < 1)
+    return fail(DT_ERR_INVALID, "dt_attn_prefill: sizes must be positive (B=%d S=%d Hq=%d Hkv=%d)", B, S, Hq, Hkv);
+  if (Hq % Hkv != 0)
+    return fail(DT_ERR_INVALID, "dt_attn_prefill: num_attention_heads (%d) must be divisible by "
+                                "num_key_value_heads (%d)", Hq, Hkv);
+  if (D != 32 && D != 64) return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: head_dim %d not in {32, 64}", D);
+  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
+    return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: dtype %d not supported by the tensor-core path", dtype);
+  const int R = Hq / Hkv;
+  if (R > 128) return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: group size %d > 128", R);
+  if ((long long)B * Hkv > 0x7fffffffLL) return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: B*Hkv too large");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(DT_ERR_INVALID, "dt_attn_prefill: q/k/v/o must be 16-byte aligned");
+  const int64_t strides[12] = {q_sb, q_ss, q_sh, k_sb, k_ss, k_sh, v_sb, v_ss, v_sh, o_sb, o_ss, o_sh};
+  for (int i = 0; i < 12; ++i)
+    if (strides[i] <= 0 || strides[i] % 8 != 0)
+      return fail(DT_ERR_INVALID, "dt_attn_prefill: stride #%d (%lld) must be a positive multiple of 8", i,
+                  (long long)strides[i]);
+  if (apply_rope) {
+    if (!cos_tab || !sin_tab) return fail(DT_ERR_INVALID, "dt_attn_prefill: null cos/sin with apply_rope");
+    if (cos_rows < S) return fail(DT_ERR_INVALID, "dt_attn_prefill: cos/sin have %d rows < S=%d", cos_rows, S);
+    if (!aligned16(cos_tab) || !aligned16(sin_tab) || cos_stride < D || cos_stride % 4 != 0)
+      return fail(DT_ERR_INVALID, "dt_attn_prefill: cos/sin must be 16-byte aligned with row stride >= D, %% 4");
+  }
+  int dev = 0;
+  int* status = nullptr;
+  int rc = device_setup(&dev, &status);
+  if (rc) return rc;
+  if (g_cc_major[dev] != 10)
+    return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: needs an sm_100 GPU (device %d is cc %d.x)", dev,
+                g_cc_major[dev]);
+
+  const bool bf16 = dtype == DT_DTYPE_BF16;
+  const int PT = 128 / R;
+  CUtensorMap mq, mk, mv;
+  if ((rc = encode_bshd(&mq, q, bf16, B, S, Hq, D, q_sb, q_ss, q_sh, (uint32_t)R, (uint32_t)PT, "q"))) return rc;
+  if ((rc = encode_bshd(&mk, k, bf16, B, S, Hkv, D, k_sb, k_ss, k_sh, 1, 128, "k"))) return rc;
+  if ((rc = encode_bshd(&mv, v, bf16, B, S, Hkv, D, v_sb, v_ss, v_sh, 1, 128, "v"))) return rc;
+
+  dtk::PrefillParams prm;
+  prm.o = o;
+  prm.cos = cos_tab;
+  prm.sin = sin_tab;
+  prm.pad_len = pad_len;
+  prm.status = status;
+  prm.o_sb = o_sb;
+  prm.o_ss = o_ss;
+  prm.o_sh = o_sh;
+  prm.cs_stride = (int)cos_stride;
+  prm.S = S;
+  prm.Hkv = Hkv;
+  prm.R = R;
+  prm.PT = PT;
+  const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
+  prm.scale_log2 = sc * 1.4426950408889634f;
+  prm.rope = apply_rope ? 1 : 0;
+  cudaError_t e = dtk::launch_prefill_sm100(mq, mk, mv, prm, D, bf16, B * Hkv, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dt_attn_prefill launch");
+  return DT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,112 @@
+"""GPU parity of the fused prefill kernel (dt_attn_prefill) against the CPU oracle.
+
+Inputs are drawn in float32, rounded to the kernel dtype, and the oracle sees
+the same rounded values upcast to float32.  Tolerances (written per dtype
+below) cover bf16/fp16 rounding of the rotated q/k, the probabilities and the
+output; the mean error bound catches systematic mistakes that a loose
+max-abs bound would let through.
+"""
+import pytest
+import torch
+
+from oracle import attention_prefill_ref, mask_from_pad_len, precompute_freqs_cis
+
+TOL = {torch.bfloat16: dict(atol=1.5e-2, rtol=1e-2, mean=2.5e-3),
+       torch.float16: dict(atol=4e-3, rtol=4e-3, mean=5e-4)}
+
+CASES = [
+    # B, S, Hq, Hkv, D, pads, dtype
+    (3, 24, 8, 2, 32, [0, 6, 15], torch.bfloat16),
+    (4, 192, 8, 2, 32, [0, 96, 47, 191], torch.bfloat16),
+    (6, 21, 8, 2, 32, [0, 1, 20, 21, 7, 16], torch.bfloat16),
+    (2, 1, 8, 2, 32, None, torch.bfloat16),
+    (2, 7, 8, 2, 32, [0, 3], torch.bfloat16),
+    (2, 150, 8, 2, 32, [0, 96], torch.float16),
+    (2, 768, 12, 4, 64, [0, 384], torch.bfloat16),
+    (3, 100, 12, 4, 64, [0, 5, 50], torch.float16),
+    (2, 300, 8, 8, 32, [0, 17], torch.bfloat16),
+    (2, 64, 16, 2, 32, [0, 10], torch.bfloat16),
+    (1, 255, 8, 2, 32, None, torch.bfloat16),
+    (2, 129, 4, 4, 64, [0, 128], torch.bfloat16),
+]
+
+
+def _run_case(B, S, Hq, Hkv, D, pads, dtype, seed=0, fused_layout=False, rope=True):
+    from rl_for_mario_b200.kernels import attn_prefill, device_status
+
+    g = torch.Generator().manual_seed(seed)
+    if fused_layout:
+        # q/k/v as strided views of one [B, S, Hq + 2 Hkv, D] projection output.
+        qkv = (torch.randn(B, S, Hq + 2 * Hkv, D, generator=g) * 0.5).to(dtype)
+        q32, k32, v32 = qkv.float().split([Hq, Hkv, Hkv], dim=2)
+        dev = qkv.cuda()
+        q, k, v = dev.split([Hq, Hkv, Hkv], dim=2)
+    else:
+        q32 = (torch.randn(B, S, Hq, D, generator=g) * 0.5).to(dtype).float()
+        k32 = (torch.randn(B, S, Hkv, D, generator=g) * 0.5).to(dtype).float()
+        v32 = (torch.randn(B, S, Hkv, D, generator=g) * 0.5).to(dtype).float()
+        q, k, v = (t.to(dtype).cuda() for t in (q32, k32, v32))
+    cos, sin = precompute_freqs_cis(D, S, 1e4)
+    pad_t = None if pads is None else torch.tensor(pads, dtype=torch.int32)
+    mask = None if pads is None else mask_from_pad_len(pad_t, S)
+    ref = attention_prefill_ref(q32, k32, v32, cos, sin, mask, rope=rope)
+    out = attn_prefill(q, k, v, cos.cuda(), sin.cuda(), None if pad_t is None else pad_t.cuda(),
+                       apply_rope=rope)
+    assert device_status() == 0
+    return out.float().cpu(), ref
+
+
+def _check(out, ref, dtype):
+    tol = TOL[dtype]
+    assert torch.isfinite(out).all()
+    err = (out - ref).abs()
+    bound = tol["atol"] + tol["rtol"] * ref.abs()
+    worst = (err - bound).max().item()
+    assert worst <= 0, f"max err {err.max().item():.3e} exceeds tolerance by {worst:.3e}"
+    assert err.mean().item() < tol["mean"], f"mean err {err.mean().item():.3e}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"B{c[0]}_S{c[1]}_{c[2]}x{c[3]}_D{c[4]}_{str(c[6])[6:]}")
+def test_prefill_matches_oracle(case):
+    out, ref = _run_case(*case)
+    _check(out, ref, case[6])
+
+
+@pytest.mark.gpu
+def test_prefill_strided_fused_qkv_layout():
+    out, ref = _run_case(3, 50, 8, 2, 32, [0, 9, 30], torch.bfloat16, fused_layout=True)
+    _check(out, ref, torch.bfloat16)
+
+
+@pytest.mark.gpu
+def test_prefill_without_rope():
+    out, ref = _run_case(2, 40, 8, 2, 32, [0, 12], torch.bfloat16, rope=False)
+    _check(out, ref, torch.bfloat16)
+
+
+@pytest.mark.gpu
+def test_prefill_repeatable():
+    a, _ = _run_case(2, 192, 8, 2, 32, [0, 50], torch.bfloat16, seed=5)
+    b, _ = _run_case(2, 192, 8, 2, 32, [0, 50], torch.bfloat16, seed=5)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.gpu
+def test_prefill_rejects_bad_arguments():
+    from rl_for_mario_b200._lib import DTKernelError
+    from rl_for_mario_b200.kernels import attn_prefill
+
+    q = torch.zeros(1, 8, 6, 32, dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros(1, 8, 4, 32, dtype=torch.bfloat16, device="cuda")
+    cos, sin = (t.cuda() for t in precompute_freqs_cis(32, 8))
+    with pytest.raises(DTKernelError, match="divisible"):
+        attn_prefill(q, k, k.clone(), cos, sin)
+    q = torch.zeros(1, 8, 2, 48, dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros(1, 8, 1, 48, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(DTKernelError, match="head_dim"):
+        attn_prefill(q, k, k.clone(), None, None, apply_rope=False)
+    q = torch.zeros(1, 16, 2, 32, dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros(1, 16, 1, 32, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(DTKernelError, match="rows"):
+        attn_prefill(q, k, k.clone(), cos, sin)  # cos has 8 rows < S = 16
