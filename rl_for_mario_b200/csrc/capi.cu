@@ -34,6 +34,7 @@ __device__ int g_dev_status;
 constexpr int kMaxDevices = 64;
 int* g_status_ptr[kMaxDevices] = {};
 int g_cc_major[kMaxDevices] = {};
+int g_num_sms[kMaxDevices] = {};
 std::mutex g_dev_mu;
 
 // Resolves, once per device, the status word's device address and the
@@ -51,7 +52,11 @@ int device_setup(int* dev_out, int** status_out) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_dev_status);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
     g_cc_major[dev] = major;
+    g_num_sms[dev] = sms;
     g_status_ptr[dev] = static_cast<int*>(p);
   }
   *dev_out = dev;
@@ -161,10 +166,14 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
 
   const bool bf16 = dtype == DT_DTYPE_BF16;
   const int PT = 128 / R;
+  // Short sequences with head_dim 32 (the DT's 192-token context) use the
+  // persistent kernel that keeps a unit's whole K/V in shared memory.
+  const bool short_path = (D == 32 && S <= 192);
+  const uint32_t kv_box = short_path ? (uint32_t)((S + 15) & ~15) : 128u;
   CUtensorMap mq, mk, mv;
   if ((rc = encode_bshd(&mq, q, bf16, B, S, Hq, D, q_sb, q_ss, q_sh, (uint32_t)R, (uint32_t)PT, "q"))) return rc;
-  if ((rc = encode_bshd(&mk, k, bf16, B, S, Hkv, D, k_sb, k_ss, k_sh, 1, 128, "k"))) return rc;
-  if ((rc = encode_bshd(&mv, v, bf16, B, S, Hkv, D, v_sb, v_ss, v_sh, 1, 128, "v"))) return rc;
+  if ((rc = encode_bshd(&mk, k, bf16, B, S, Hkv, D, k_sb, k_ss, k_sh, 1, kv_box, "k"))) return rc;
+  if ((rc = encode_bshd(&mv, v, bf16, B, S, Hkv, D, v_sb, v_ss, v_sh, 1, kv_box, "v"))) return rc;
 
   dtk::PrefillParams prm;
   prm.o = o;
@@ -183,7 +192,16 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   prm.scale_log2 = sc * 1.4426950408889634f;
   prm.rope = apply_rope ? 1 : 0;
-  cudaError_t e = dtk::launch_prefill_sm100(mq, mk, mv, prm, D, bf16, B * Hkv, static_cast<cudaStream_t>(stream));
+  const int units = B * Hkv;
+  cudaError_t e;
+  if (short_path) {
+    int grid = units < g_num_sms[dev] ? units : g_num_sms[dev];
+    // The persistent kernel stages at most 2048 units' padding per CTA.
+    if ((units + grid - 1) / grid > 2048) grid = (units + 2047) / 2048;
+    e = dtk::launch_prefill_short_sm100(mq, mk, mv, prm, bf16, units, grid, static_cast<cudaStream_t>(stream));
+  } else {
+    e = dtk::launch_prefill_sm100(mq, mk, mv, prm, D, bf16, units, static_cast<cudaStream_t>(stream));
+  }
   if (e != cudaSuccess) return cuda_fail(e, "dt_attn_prefill launch");
   return DT_OK;
 }

@@ -1,0 +1,512 @@
+// Persistent fused causal GQA prefill for short sequences (S <= 192,
+// head_dim 32): the Decision Transformer's own context (64 timesteps x 3
+// tokens).  Same mathematics as prefill_sm100.cu (reference
+// model/model_decision_transformer.py:179-224); different schedule:
+//
+//  * one CTA per SM loops over (sample b, KV head g) units; the M tiles of a
+//    unit pack 128 rows (position, head) of the R query heads sharing KV head g;
+//  * K and V of a unit (S x 32 each) stay resident in shared memory for all
+//    of the unit's tiles; K is rotated once per unit; the cos/sin tables are
+//    staged in shared memory once per CTA;
+//  * S = Q K^T lands in one of two TMEM slots, so the tensor core computes
+//    the next tile while the current one is in softmax;
+//  * softmax: 8 warps, two threads per row, each owning half of the row's
+//    key chunks.  A thread reads its S columns from TMEM once, the two halves
+//    exchange the exact row maximum through shared memory, and P (bf16) is
+//    written back into TMEM over the S columns it came from; O = P V reads
+//    it from there (tcgen05 MMA with A in TMEM);
+//  * the epilogue (O / rowsum -> bf16 -> HBM) of a tile runs while the tensor
+//    core computes the next tile's P V, from a second TMEM O slot;
+//  * the TMA producer runs an 8-deep ring of Q tiles and a 3-deep ring of K/V.
+//
+// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-3 RoPE workers,
+// 4-11 softmax / epilogue.
+#include "dt_common.cuh"
+#include "dt_internal.h"
+#include "prefill_common.cuh"
+
+namespace dtk {
+
+namespace {
+
+struct SS {
+  static constexpr int D = 32;
+  static constexpr int ROWB = 64;
+  static constexpr int SMAX = 192;
+  static constexpr int Q_BYTES = 128 * ROWB;   // one 128-row Q tile
+  static constexpr int NQ = 8;
+  static constexpr int KV_BYTES = SMAX * ROWB; // K (or V) of one unit
+  static constexpr int NKV = 3;
+  static constexpr int CS_STRIDE = D + 4;      // floats per staged cos/sin row (bank spread)
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + NQ * Q_BYTES;
+  static constexpr int OFF_V = OFF_K + NKV * KV_BYTES;
+  static constexpr int OFF_COS = OFF_V + NKV * KV_BYTES;
+  static constexpr int OFF_SIN = OFF_COS + SMAX * CS_STRIDE * 4;
+  static constexpr int OFF_RED = OFF_SIN + SMAX * CS_STRIDE * 4;  // row max / row sum exchange
+  static constexpr int RED_FLOATS = 2 * 2 * 128 + 2 * 2 * 128;    // max[slot][half][row], sum[slot][half][row]
+  static constexpr int OFF_PAD = OFF_RED + RED_FLOATS * 4;
+  static constexpr int MAX_UNITS = 2048;       // units per CTA (per-unit pads staged in smem)
+  static constexpr int OFF_BAR = OFF_PAD + MAX_UNITS * 4;
+  // q_full, q_ready, q_empty [NQ]; kv_full, kv_ready, kv_empty [NKV]; s_full, p_full, o_full, xchg [2];
+  // fin; drain
+  static constexpr int NBAR = 3 * NQ + 3 * NKV + 8 + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t TMEM_S = 0;    // + 192 * slot (P aliases the first half of the slot)
+  static constexpr uint32_t TMEM_O = 384;  // + 32 * slot
+  static constexpr int NTHREADS = 384;
+  static constexpr int NROPE = 64;
+  static constexpr int NSOFT = 256;
+};
+static_assert(SS::SMEM_BYTES <= 232448, "shared memory budget");
+
+// Work cursor: local unit lu, tile t within the unit, local tile index i.
+struct Cursor {
+  int lu, t, i;
+  __device__ __forceinline__ void next(int ntiles) {
+    ++i;
+    if (++t == ntiles) {
+      t = 0;
+      ++lu;
+    }
+  }
+};
+
+// Key window of a tile: columns [kb0, kb0 + n) of S, chunked by 32 from kb0.
+// kb0 is placed so that the last 32-column chunk ends at the tile's causal
+// edge (the diagonal block is one chunk), rounded down to 16 keys and >= 0.
+struct TileInfo {
+  int pad, pos0, kb0, n, nc;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const Cursor& c, const int* pads_s, int PT, int S) {
+  TileInfo T;
+  T.pad = pads_s[c.lu];
+  const TilePlan p = plan_tile(c.t, PT, S, T.pad);
+  T.pos0 = p.pos0;
+  int kb0 = p.kend - 32 * ((p.kend - p.kstart + 31) >> 5);
+  kb0 = max(kb0, 0) & ~15;
+  T.kb0 = kb0;
+  T.n = (p.kend - kb0 + 15) & ~15;
+  T.nc = (T.n + 31) >> 5;
+  return T;
+}
+
+}  // namespace
+
+template <bool BF16>
+__global__ void __launch_bounds__(SS::NTHREADS, 1)
+    dt_prefill_short_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, const PrefillParams prm, int n_units) {
+  using E = Elem<BF16>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SS::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* q_ready = bars + SS::NQ;
+  uint64_t* q_empty = bars + 2 * SS::NQ;
+  uint64_t* kv_full = bars + 3 * SS::NQ;
+  uint64_t* kv_ready = kv_full + SS::NKV;
+  uint64_t* kv_empty = kv_full + 2 * SS::NKV;
+  uint64_t* s_full = kv_full + 3 * SS::NKV;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = s_full + 4;
+  uint64_t* xchg = s_full + 6;  // softmax halves: row-max exchange, one per slot
+  uint64_t* fin = s_full + 8;   // softmax halves: last row sums published
+  uint64_t* drain = s_full + 9;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + SS::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SS::OFF_MISC + 4);
+  float* cos_s = reinterpret_cast<float*>(smem + SS::OFF_COS);
+  float* sin_s = reinterpret_cast<float*>(smem + SS::OFF_SIN);
+  float* red = reinterpret_cast<float*>(smem + SS::OFF_RED);
+  int* pads_s = reinterpret_cast<int*>(smem + SS::OFF_PAD);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int S = prm.S;
+  const int R = prm.R;
+  const int PT = prm.PT;
+  const int ntiles = (S + PT - 1) / PT;
+  const int my_units = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int ntotal = my_units * ntiles;
+  const int SB = (S + 15) & ~15;  // K/V rows loaded per unit (TMA box height)
+
+  if (tid == 0) {
+    for (int i = 0; i < SS::NQ; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_ready[i], SS::NROPE);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < SS::NKV; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_ready[i], SS::NROPE);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], SS::NSOFT);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&xchg[i], SS::NSOFT);
+    }
+    mbar_init(fin, SS::NSOFT);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  // Stage this CTA's per-unit padding and (when rotating) the cos/sin rows.
+  for (int j = tid; j < my_units; j += SS::NTHREADS) {
+    const int unit = blockIdx.x + j * gridDim.x;
+    const int pad = prm.pad_len ? prm.pad_len[unit / prm.Hkv] : 0;
+    pads_s[j] = max(0, min(pad, S));
+  }
+  if (prm.rope) {
+    for (int j = tid; j < S * (SS::D / 4); j += SS::NTHREADS) {
+      const int row = j / (SS::D / 4), c4 = j % (SS::D / 4);
+      *reinterpret_cast<float4*>(cos_s + row * SS::CS_STRIDE + c4 * 4) =
+          __ldg(reinterpret_cast<const float4*>(prm.cos + (size_t)row * prm.cs_stride) + c4);
+      *reinterpret_cast<float4*>(sin_s + row * SS::CS_STRIDE + c4 * 4) =
+          __ldg(reinterpret_cast<const float4*>(prm.sin + (size_t)row * prm.cs_stride) + c4);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, SS::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  uint8_t* q_s = smem + SS::OFF_Q;
+  uint8_t* k_s = smem + SS::OFF_K;
+  uint8_t* v_s = smem + SS::OFF_V;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      int qi = 0, lu = 0;
+      bool ok = true;
+      for (; lu < my_units && ok; ++lu) {
+        const int unit = blockIdx.x + lu * gridDim.x;
+        const int b = unit / prm.Hkv;
+        const int g = unit - b * prm.Hkv;
+        const int kvb = lu % SS::NKV;
+        if (!(ok = mbar_wait(&kv_empty[kvb], ((lu / SS::NKV) & 1) ^ 1, abort_flag, prm.status))) break;
+        mbar_arrive_expect_tx(&kv_full[kvb], (uint32_t)(2 * SB * SS::ROWB));
+        tma_load_4d(k_s + kvb * SS::KV_BYTES, &tmK, &kv_full[kvb], 0, g, 0, b);
+        tma_load_4d(v_s + kvb * SS::KV_BYTES, &tmV, &kv_full[kvb], 0, g, 0, b);
+        for (int t = 0; t < ntiles; ++t) {
+          const int qs = qi % SS::NQ;
+          if (!(ok = mbar_wait(&q_empty[qs], ((qi / SS::NQ) & 1) ^ 1, abort_flag, prm.status))) break;
+          mbar_arrive_expect_tx(&q_full[qs], (uint32_t)(PT * R * SS::ROWB));
+          tma_load_4d(q_s + qs * SS::Q_BYTES, &tmQ, &q_full[qs], 0, g * R, t * PT, b);
+          ++qi;
+        }
+      }
+      if (*abort_flag) {
+        // Let every load already issued land before the CTA can exit.
+        for (int i = 0; i < SS::NQ; ++i) {
+          const int uses = qi / SS::NQ + (i < qi % SS::NQ ? 1 : 0);
+          if (uses > 0) mbar_wait(&q_full[i], (uses - 1) & 1, nullptr, nullptr);
+        }
+        for (int i = 0; i < SS::NKV; ++i) {
+          const int uses = lu / SS::NKV + (i < lu % SS::NKV ? 1 : 0);
+          if (uses > 0) mbar_wait(&kv_full[i], (uses - 1) & 1, nullptr, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_pv = umma_idesc_f16(BF16, 128, SS::D, 0, 1);
+      // S for tile c into TMEM slot (c.i & 1).
+      auto issue_s = [&](const Cursor& c) -> bool {
+        const TileInfo T = tile_info(c, pads_s, PT, S);
+        const int qs = c.i % SS::NQ;
+        const int kvb = c.lu % SS::NKV;
+        if (!mbar_wait(&q_ready[qs], (c.i / SS::NQ) & 1, abort_flag, prm.status)) return false;
+        if (c.t == 0 && !mbar_wait(&kv_ready[kvb], (c.lu / SS::NKV) & 1, abort_flag, prm.status)) return false;
+        tc_fence_after();
+        // K-major 64B-swizzled operands; the second K step starts 32 bytes in.
+        const uint64_t ad = umma_smem_desc(smem_u32(q_s + qs * SS::Q_BYTES), 16, 8 * SS::ROWB, kSw64);
+        const uint64_t bd = umma_smem_desc(smem_u32(k_s + kvb * SS::KV_BYTES) + (uint32_t)T.kb0 * SS::ROWB, 16,
+                                           8 * SS::ROWB, kSw64);
+        const uint32_t idesc_s = umma_idesc_f16(BF16, 128, (uint32_t)T.n, 0, 0);
+        const uint32_t td = tmem + SS::TMEM_S + 192u * (c.i & 1);
+        umma_f16_ss(td, ad, bd, idesc_s, 0u);
+        umma_f16_ss(td, ad + 2, bd + 2, idesc_s, 1u);
+        umma_commit(&s_full[c.i & 1]);
+        umma_commit(&q_empty[qs]);
+        return true;
+      };
+      // O = P V for tile c into TMEM O slot (c.i & 1), P read from the S slot.
+      auto issue_pv = [&](const Cursor& c) -> bool {
+        const TileInfo T = tile_info(c, pads_s, PT, S);
+        const int kvb = c.lu % SS::NKV;
+        const int slot = c.i & 1;
+        if (!mbar_wait(&p_full[slot], (c.i >> 1) & 1, abort_flag, prm.status)) return false;
+        tc_fence_after();
+        const uint32_t pa = tmem + SS::TMEM_S + 192u * slot;  // packed bf16 P, 2 keys per column
+        const uint32_t td = tmem + SS::TMEM_O + 32u * slot;
+        // MN-major V rows: 16 keys per K step = 1024 bytes = 64 descriptor units.
+        const uint64_t bd = umma_smem_desc(smem_u32(v_s + kvb * SS::KV_BYTES) + (uint32_t)T.kb0 * SS::ROWB,
+                                           SS::KV_BYTES, 8 * SS::ROWB, kSw64);
+        // Unrolled issue (no loop-carried scalar work between MMAs): K steps of
+        // 16 keys; ksteps = n / 16 <= 12.
+        const int ksteps = T.n / 16;
+        umma_f16_ts(td, pa, bd, idesc_pv, 0u);
+#pragma unroll
+        for (int kk = 1; kk < 12; ++kk)
+          if (kk < ksteps) umma_f16_ts(td, pa + kk * 8, bd + (uint64_t)(kk * 64), idesc_pv, 1u);
+        umma_commit(&o_full[slot]);
+        if (c.t == ntiles - 1) umma_commit(&kv_empty[kvb]);
+        return true;
+      };
+      // S of tiles i and i+1 run ahead; after P V of tile i (same TMEM slot,
+      // executed first by the in-order tensor pipe) comes S of tile i+2.
+      Cursor c0{0, 0, 0}, c2{0, 0, 0};
+      bool ok = true;
+      if (ntotal > 0) ok = issue_s(c0);
+      c2.next(ntiles);
+      if (ok && ntotal > 1) ok = issue_s(c2);
+      c2.next(ntiles);
+      for (Cursor c = c0; ok && c.i < ntotal; c.next(ntiles)) {
+        if (!(ok = issue_pv(c))) break;
+        if (c2.i < ntotal && !(ok = issue_s(c2))) break;
+        c2.next(ntiles);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, nullptr);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ RoPE workers
+    const int rt = tid - 64;  // 0..63
+    int qi = 0;
+    bool ok = true;
+    for (int lu = 0; lu < my_units && ok; ++lu) {
+      const int kvb = lu % SS::NKV;
+      if (!(ok = mbar_wait(&kv_full[kvb], (lu / SS::NKV) & 1, abort_flag, prm.status))) break;
+      if (prm.rope) {
+        uint8_t* kt = k_s + kvb * SS::KV_BYTES;
+        for (int row = rt; row < S; row += SS::NROPE)
+          rope_row_inplace_smem<32, BF16>(kt, row, cos_s + row * SS::CS_STRIDE, sin_s + row * SS::CS_STRIDE);
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(&kv_ready[kvb]);
+      for (int t = 0; t < ntiles; ++t) {
+        const int qs = qi % SS::NQ;
+        if (!(ok = mbar_wait(&q_full[qs], (qi / SS::NQ) & 1, abort_flag, prm.status))) break;
+        if (prm.rope) {
+          // Rows r = p * R + h: walk rows so consecutive ones share a position
+          // (the cos/sin row is re-read from shared memory, which hits the same
+          // address for the R heads of a position).
+          const int rows = PT * R;
+          const int per = (rows + SS::NROPE - 1) / SS::NROPE;
+          const int r0 = rt * per;
+          for (int k2 = 0; k2 < per; ++k2) {
+            const int row = r0 + k2;
+            const int pos = t * PT + row / R;
+            if (row < rows && pos < S)
+              rope_row_inplace_smem<32, BF16>(q_s + qs * SS::Q_BYTES, row, cos_s + pos * SS::CS_STRIDE,
+                                              sin_s + pos * SS::CS_STRIDE);
+          }
+          fence_proxy_async_smem();
+        }
+        mbar_arrive(&q_ready[qs]);
+        ++qi;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int half = (warp - 4) >> 2;  // which half of each row's key chunks
+    const int wq = warp & 3;           // TMEM lane quarter this warp may access
+    const int r = wq * 32 + lane;      // tile row = TMEM lane
+    const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
+    const float c2 = prm.scale_log2;
+    const int h = r % R;
+    const int rowpos = r / R;
+    float* red_max = red;                 // [slot][half][128]
+    float* red_sum = red + 2 * 2 * 128;   // [slot][half][128]
+    bool ok = true;
+
+    // Epilogue of tile c: O from its TMEM slot / row sum -> bf16 -> HBM.
+    // Each half stores 16 of the 32 output columns.
+    auto epilogue = [&](const Cursor& c) -> bool {
+      const int slot = c.i & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&o_full[slot], (c.i >> 1) & 1, abort_flag, prm.status)))
+        return false;
+      tc_fence_after();
+      float o[16];
+      tmem_ld16(t_lane + SS::TMEM_O + 32u * slot + 16u * half, o);
+      tc_fence_before();
+      const int pos = c.t * PT + rowpos;
+      if (r < PT * R && pos < S) {
+        const float l = red_sum[(slot * 2 + 0) * 128 + r] + red_sum[(slot * 2 + 1) * 128 + r];
+        const int unit = blockIdx.x + c.lu * gridDim.x;
+        const int b = unit / prm.Hkv;
+        const int g = unit - b * prm.Hkv;
+        const float inv = 1.f / l;
+        typename E::T* orow = reinterpret_cast<typename E::T*>(prm.o) + (size_t)b * prm.o_sb +
+                              (size_t)pos * prm.o_ss + (size_t)(g * R + h) * prm.o_sh + 16 * half;
+#pragma unroll
+        for (int cc = 0; cc < 16; cc += 8) {
+          uint4 v;
+          v.x = E::from_f2(o[cc + 0] * inv, o[cc + 1] * inv);
+          v.y = E::from_f2(o[cc + 2] * inv, o[cc + 3] * inv);
+          v.z = E::from_f2(o[cc + 4] * inv, o[cc + 5] * inv);
+          v.w = E::from_f2(o[cc + 6] * inv, o[cc + 7] * inv);
+          *reinterpret_cast<uint4*>(orow + cc) = v;
+        }
+      }
+      return true;
+    };
+
+    Cursor prev{0, 0, -1};
+    for (Cursor cur{0, 0, 0}; cur.i < ntotal && ok; cur.next(ntiles)) {
+      const TileInfo T = tile_info(cur, pads_s, PT, S);
+      const int slot = cur.i & 1;
+      const int pos = T.pos0 + rowpos;
+      const bool valid_row = (r < PT * R) && (pos < S);
+      const bool padded = pos < T.pad;
+      const int lo = padded ? 0 : T.pad;
+      const int hi = valid_row ? pos : -1;
+      // This half's chunks: [c_begin, c_begin + myc) of the tile's T.nc chunks.
+      const int c_split = (T.nc + 1) >> 1;
+      const int c_begin = half ? c_split : 0;
+      const int myc = (half ? T.nc : c_split) - c_begin;  // 0..3
+      const bool tile_clean = T.pos0 >= T.pad;
+      const uint32_t t_s = t_lane + SS::TMEM_S + 192u * slot + 32u * c_begin;
+
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[slot], (cur.i >> 1) & 1, abort_flag, prm.status))))
+        break;
+      tc_fence_after();
+      uint32_t sa[32], sb[32], sc[32];
+      if (myc > 0) tmem_ld32_async(t_s, sa);
+      if (myc > 1) tmem_ld32_async(t_s + 32, sb);
+      if (myc > 2) tmem_ld32_async(t_s + 64, sc);
+      tmem_wait_ld3(sa, sb, sc);
+
+      // Allowed keys of this row inside chunk ci, as a 32-bit mask (bit j =
+      // key kb0 + 32 ci + j): [lo, hi] clipped to the chunk.
+      auto chunk_mask = [&](int ci) -> uint32_t {
+        const int k0 = T.kb0 + 32 * ci;
+        const int jlo = lo - k0, jhi = hi - k0;
+        const uint32_t hm = jhi < 0 ? 0u : (jhi >= 31 ? 0xffffffffu : ((2u << jhi) - 1u));
+        const uint32_t lm = jlo <= 0 ? 0xffffffffu : (jlo >= 32 ? 0u : (0xffffffffu << jlo));
+        return hm & lm;
+      };
+      // A chunk is free of masking for every row of the tile when the tile has
+      // no padded rows and the chunk lies in [pad, pos0] (warp-uniform test).
+      auto chunk_clean = [&](int ci) -> bool {
+        const int k0 = T.kb0 + 32 * ci;
+        return tile_clean && k0 >= T.pad && k0 + 31 <= T.pos0;
+      };
+      // Partial row maximum over this half's allowed keys, in 4 independent
+      // accumulators (short dependency chains).
+      float mx[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) mx[j] = -INFINITY;
+      auto chunk_max = [&](const uint32_t (&u)[32], int ci) {
+        if (chunk_clean(ci)) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(u[j]));
+        } else {
+          const uint32_t mk = chunk_mask(ci);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            mx[j & 3] = fmaxf(mx[j & 3], ((mk >> j) & 1u) ? __uint_as_float(u[j]) : -INFINITY);
+        }
+      };
+      if (myc > 0) chunk_max(sa, c_begin);
+      if (myc > 1) chunk_max(sb, c_begin + 1);
+      if (myc > 2) chunk_max(sc, c_begin + 2);
+      const float pmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      // Exchange partial maxima between the halves (bounded mbarrier wait).  The
+      // tcgen05 fences order every S read of both halves before any P write.
+      red_max[(slot * 2 + half) * 128 + r] = pmax;
+      tc_fence_before();
+      mbar_arrive(&xchg[slot]);
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&xchg[slot], (cur.i >> 1) & 1, abort_flag, prm.status))))
+        break;
+      tc_fence_after();
+      const float rmax = fmaxf(pmax, red_max[(slot * 2 + (half ^ 1)) * 128 + r]);
+      // t = s * c2 - m.  Padded rows use c2 = m = 0, so every allowed key gets
+      // exp2(0) = 1 (the reference's tie over keys 0..q); masked keys get -inf.
+      const float m = (padded || rmax == -INFINITY) ? 0.f : rmax * c2;
+      const float cr = padded ? 0.f : c2;
+
+      // P = exp2(t), packed bf16 pairs stored over the S columns just read;
+      // partial row sum in fp32.
+      float ls[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ls[j] = 0.f;
+      auto chunk_p = [&](const uint32_t (&u)[32], int ci) {
+        uint32_t pk[16];
+        if (chunk_clean(ci)) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(u[j]), c2, -m));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(u[j + 1]), c2, -m));
+            ls[j & 3] += p0;
+            ls[(j + 1) & 3] += p1;
+            pk[j >> 1] = E::from_f2(p0, p1);
+          }
+        } else {
+          const uint32_t mk = chunk_mask(ci);
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float t0 = ((mk >> j) & 1u) ? fmaf(__uint_as_float(u[j]), cr, -m) : -INFINITY;
+            const float t1 = ((mk >> (j + 1)) & 1u) ? fmaf(__uint_as_float(u[j + 1]), cr, -m) : -INFINITY;
+            const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
+            ls[j & 3] += p0;
+            ls[(j + 1) & 3] += p1;
+            pk[j >> 1] = E::from_f2(p0, p1);
+          }
+        }
+        tmem_st16(t_lane + SS::TMEM_S + 192u * slot + 16u * ci, pk);
+      };
+      if (myc > 0) chunk_p(sa, c_begin);
+      if (myc > 1) chunk_p(sb, c_begin + 1);
+      if (myc > 2) chunk_p(sc, c_begin + 2);
+      const float l = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      red_sum[(slot * 2 + half) * 128 + r] = l;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[slot]);
+      // While the tensor core runs this tile's P V and the next S, finish the
+      // previous tile (its row sums were published before this tile's exchange).
+      if (prev.i >= 0 && !(ok = epilogue(prev))) break;
+      prev = cur;
+    }
+    if (ok && prev.i >= 0) {
+      // Publish the last tile's row sums to the other half, then finish it.
+      mbar_arrive(fin);
+      if (__all_sync(0xffffffffu, mbar_wait(fin, 0, abort_flag, prm.status))) epilogue(prev);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, SS::TMEM_COLS);
+  }
+}
+
+cudaError_t launch_prefill_short_sm100(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                                       const PrefillParams& prm, bool bf16, int n_units, int grid,
+                                       cudaStream_t stream) {
+  if ((n_units + grid - 1) / grid > SS::MAX_UNITS) return cudaErrorInvalidValue;
+  auto kfn = bf16 ? dt_prefill_short_kernel<true> : dt_prefill_short_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, SS::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  kfn<<<grid, SS::NTHREADS, SS::SMEM_BYTES, stream>>>(q, k, v, prm, n_units);
+  return cudaGetLastError();
+}
+
+}  // namespace dtk

@@ -28,6 +28,10 @@ CASES = [
     (2, 64, 16, 2, 32, [0, 10], torch.bfloat16),
     (1, 255, 8, 2, 32, None, torch.bfloat16),
     (2, 129, 4, 4, 64, [0, 128], torch.bfloat16),
+    (3, 100, 4, 4, 32, [0, 50, 99], torch.bfloat16),
+    (4, 190, 4, 2, 32, [0, 1, 100, 189], torch.float16),
+    (300, 96, 8, 2, 32, "random", torch.bfloat16),
+    (150, 192, 8, 2, 32, "random", torch.bfloat16),
 ]
 
 
@@ -47,6 +51,8 @@ def _run_case(B, S, Hq, Hkv, D, pads, dtype, seed=0, fused_layout=False, rope=Tr
         v32 = (torch.randn(B, S, Hkv, D, generator=g) * 0.5).to(dtype).float()
         q, k, v = (t.to(dtype).cuda() for t in (q32, k32, v32))
     cos, sin = precompute_freqs_cis(D, S, 1e4)
+    if isinstance(pads, str):
+        pads = torch.randint(0, S // 2 + 1, (B,), generator=g).tolist()
     pad_t = None if pads is None else torch.tensor(pads, dtype=torch.int32)
     mask = None if pads is None else mask_from_pad_len(pad_t, S)
     ref = attention_prefill_ref(q32, k32, v32, cos, sin, mask, rope=rope)
@@ -67,7 +73,7 @@ def _check(out, ref, dtype):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", CASES, ids=lambda c: f"B{c[0]}_S{c[1]}_{c[2]}x{c[3]}_D{c[4]}_{str(c[6])[6:]}")
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"B{c[0]}_S{c[1]}_{c[2]}x{c[3]}_D{c[4]}_{str(c[6])[6:]}{'_rp' if c[5] == 'random' else ''}")
 def test_prefill_matches_oracle(case):
     out, ref = _run_case(*case)
     _check(out, ref, case[6])
