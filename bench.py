@@ -1,0 +1,346 @@
+"""Benchmark of the Decision Transformer attention path on B200.
+
+One "step" is one fused prefill pass (dt_attn_prefill) over the attention-op
+workload of 4096 samples x 192 tokens (64 timesteps x 3), 8 query / 2 KV
+heads, head_dim 32, bf16, RoPE positions 0..191, causal + per-sample left
+padding U{0..96} tokens.  Inputs are seeded synthetic Q/K/V ~ N(0,1) * 0.5
+(no dataset exists for this op; the shapes and value ranges follow the
+workload definition).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 the script runs under torchrun (one rank per GPU); every rank
+processes its own full batch (weak scaling, no data-path collective) and the
+reported time is the maximum over ranks.  ``--impl reference`` times the
+CPU oracle (the reference algorithm restated in float32 PyTorch) on the
+host cores.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+WORKLOAD = dict(batch=4096, seq_len=192, timesteps=64, q_heads=8, kv_heads=2, head_dim=32, max_pad=96)
+METRIC = "DT attention prefill tokens/s (4096 x 192 tokens, 8/2 heads, head_dim 32, causal + left padding)"
+UNIT = "tokens/s"
+
+
+def _peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def _algorithmic_bytes(B, S, Hq, Hkv, D) -> int:
+    # Read Q, K, V and write O once, bf16 (masks and scores are never stored).
+    return 2 * B * S * D * (Hq + 2 * Hkv + Hq)
+
+
+def _profiled_traffic_per_launch(B: int):
+    """DRAM bytes per launch from the committed ncu summary, scaled to B samples."""
+    f = REPO / "profiles" / "prefill_short_b1024_s192.txt"
+    if not f.exists():
+        return None
+    meas_b, dram = None, None
+    for line in f.read_text().splitlines():
+        if line.startswith("batch:"):
+            meas_b = int(line.split(":", 1)[1])
+        if line.startswith("dram_bytes_per_launch:"):
+            dram = float(line.split(":", 1)[1])
+    if meas_b and dram:
+        return dram * B / meas_b
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML during the timed region."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        self.idx, self.period = device_index, period_s
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception:
+            self.ok = False
+        return self
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def _dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        pg = dist
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, world, local, pg
+
+
+def _make_inputs(B, S, Hq, Hkv, D, seed, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = (torch.randn(B, S, Hq, D, device=device, generator=g) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, S, Hkv, D, device=device, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, S, Hkv, D, device=device, generator=g) * 0.5).to(torch.bfloat16)
+    pad = torch.randint(0, WORKLOAD["max_pad"] + 1, (B,), device=device, generator=g, dtype=torch.int32)
+    return q, k, v, pad
+
+
+def cpu_oracle_rate(budget_s: float = 12.0, sample_b: int = 256, threads: int | None = None):
+    """Tokens/s of the CPU oracle (reference algorithm in float32 PyTorch) on a bounded sample."""
+    from oracle import attention_prefill_ref, mask_from_pad_len, precompute_freqs_cis
+
+    if threads:
+        torch.set_num_threads(threads)
+    W = WORKLOAD
+    B, S, Hq, Hkv, D = sample_b, W["seq_len"], W["q_heads"], W["kv_heads"], W["head_dim"]
+    g = torch.Generator().manual_seed(1)
+    q = (torch.randn(B, S, Hq, D, generator=g) * 0.5).bfloat16().float()
+    k = (torch.randn(B, S, Hkv, D, generator=g) * 0.5).bfloat16().float()
+    v = (torch.randn(B, S, Hkv, D, generator=g) * 0.5).bfloat16().float()
+    pad = torch.randint(0, W["max_pad"] + 1, (B,), generator=g)
+    mask = mask_from_pad_len(pad, S)
+    cos, sin = precompute_freqs_cis(D, S)
+    attention_prefill_ref(q[:8], k[:8], v[:8], cos, sin, mask[:8])  # warm-up
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        attention_prefill_ref(q, k, v, cos, sin, mask)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 64:
+            break
+    tokens = reps * B * S
+    return tokens / el, {"cores": torch.get_num_threads(),
+                         "sample": f"{reps} x B={B} of {W['batch']} samples, S={S}, fp32 oracle, {el:.1f} s"}
+
+
+def run_reference(args):
+    rank, world, local, pg = _dist_setup(args.gpus)
+    if rank != 0:
+        if pg:
+            pg.destroy_process_group()
+        return
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    for _ in range(args.warmup):
+        cpu_oracle_rate(budget_s=0.5, sample_b=64, threads=threads)
+    rates, samples = [], []
+    for _ in range(args.steps):
+        r, info = cpu_oracle_rate(budget_s=2.0, sample_b=128, threads=threads)
+        rates.append(r)
+        samples.append(info["sample"])
+    value = statistics.median(rates)
+    W = WORKLOAD
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": W["batch"] * W["seq_len"] / value * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "attention-op prefill, B=4096 S=192 Hq=8 Hkv=2 D=32, left pad U{0..96}",
+                   "note": "CPU oracle (reference algorithm in float32 PyTorch), bounded sample per step"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": samples[0] if samples else ""},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    if pg:
+        pg.destroy_process_group()
+
+
+def run_ours(args):
+    from rl_for_mario_b200 import _lib
+    from rl_for_mario_b200.kernels import attn_prefill, device_status
+    from oracle import precompute_freqs_cis
+
+    rank, world, local, pg = _dist_setup(args.gpus)
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (there is no CPU path)")
+    _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W = WORKLOAD
+    B, S, Hq, Hkv, D = W["batch"], W["seq_len"], W["q_heads"], W["kv_heads"], W["head_dim"]
+    q, k, v, pad = _make_inputs(B, S, Hq, Hkv, D, seed=1234 + rank, device=dev)
+    cos, sin = (t.to(dev) for t in precompute_freqs_cis(D, S))
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if pg:
+            pg.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        attn_prefill(q, k, v, cos, sin, pad, out=out)
+    torch.cuda.synchronize()
+    if device_status() != 0:
+        raise SystemExit("device status error during warm-up")
+
+    # ---- device-timed region: inputs resident in HBM (1.0 GB/step > 126 MB L2).
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    with ClockSampler(dev.index) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            attn_prefill(q, k, v, cos, sin, pad, out=out)
+            launches += 1
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_max = ms
+    if pg:
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms_max = float(t.item())
+    tokens_per_rank = B * S
+    value = tokens_per_rank * world / (ms_max * 1e-3)
+
+    # ---- end to end through the public API with pinned host buffers.
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hpad = pad.cpu().pin_memory()
+    ho = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    dq, dk, dv, dpad = (torch.empty_like(t) for t in (q, k, v, pad))
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dpad.copy_(hpad, non_blocking=True)
+        attn_prefill(dq, dk, dv, cos, sin, dpad, out=out)
+        ho.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if pg:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv, hpad))
+    d2h = ho.numel() * ho.element_size()
+    if device_status() != 0:
+        raise SystemExit("device status error in the timed region")
+
+    peaks = _peaks()
+    byts = _algorithmic_bytes(B, S, Hq, Hkv, D)
+    achieved = byts / (ms * 1e-3) / 1e9
+    traffic = _profiled_traffic_per_launch(B)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"attention-op prefill, B={B} S=192 Hq=8 Hkv=2 D=32 per GPU, left pad U{{0..96}}",
+                   "parallelism": f"dp{world} (independent batches, no data-path collective)",
+                   "l2": "inputs larger than L2 (1.0 GB per step vs 126 MB)",
+                   "kernel": "dt_prefill_short_kernel (tcgen05 + TMA, persistent)"},
+        "clocks": clk.summary(),
+        "e2e": {"value": tokens_per_rank * world / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                     "algorithmic_bytes_per_launch": byts, "peak_source": peaks["source"]},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
+        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
+                                "sample": info["sample"]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the batch (profiling of small cases only; the bench line is B=4096)")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.batch:
+        WORKLOAD["batch"] = args.batch
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
