@@ -68,6 +68,46 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
                     int64_t o_ss, int64_t o_sh, float scale, int apply_rope, int dtype, void* stream);
 
 /*
+ * KV-cached decode step with an in-place paged cache.
+ *
+ * Replaces the cached branch of DecisionTransformerAttention.forward
+ * (model_decision_transformer.py:179-191 and :225-245): rotates q and k_new
+ * (RoPE at the new tokens' positions), appends the rotated k_new and v_new to
+ * the cache at positions seq_lens[b] .. seq_lens[b] + Sn - 1 (the reference
+ * builds a new tensor with torch.cat, :188-190), then attends the Sn new
+ * queries over all seq_lens[b] + Sn keys: causal on the new columns
+ * (:230-237), optional left padding pad_len[b] of the [B, kv_len] mask
+ * (:238-242), softmax in fp32 (:243).  seq_lens is read, not advanced.
+ *
+ * Cache: k_pages / v_pages [num_pages, Hkv, page_size, D]; block_table
+ * [B, max_pages] int32 page ids.  cos/sin rows are indexed by absolute
+ * position when rope_abs != 0, else by the new-token index 0..Sn-1 (the
+ * reference passes tables already sliced at start_pos, :439-443).
+ * Out-of-range positions or page ids are rejected on the device: the kernel
+ * skips the sample and sets the status word (dt_device_status).
+ */
+int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o, void* k_pages, void* v_pages,
+                   int num_pages, int page_size, const int32_t* block_table, int max_pages,
+                   const int32_t* seq_lens, const int32_t* pad_len, const float* cos_tab, const float* sin_tab,
+                   int cos_rows, int64_t cos_stride, int rope_abs, int B, int Sn, int Hq, int Hkv, int D,
+                   int64_t q_sb, int64_t q_ss, int64_t q_sh, int64_t kn_sb, int64_t kn_ss, int64_t kn_sh,
+                   int64_t vn_sb, int64_t vn_ss, int64_t vn_sh, int64_t o_sb, int64_t o_ss, int64_t o_sh,
+                   float scale, int apply_rope, int dtype, void* stream);
+
+/*
+ * Writes S tokens of K (rotated when apply_rope) and V into the paged cache at
+ * positions start_pos[b] + s (start_pos may be null: 0).  This is the cache
+ * produced by the prefill branch with use_cache=True
+ * (model_decision_transformer.py:179-191: present = (RoPE(k), v)); a dense
+ * [B, Hkv, L, D] cache is the case page_size = L, block_table[b] = {b}.
+ */
+int dt_kv_write(const void* k, const void* v, void* k_pages, void* v_pages, int num_pages, int page_size,
+                const int32_t* block_table, int max_pages, const int32_t* start_pos, const float* cos_tab,
+                const float* sin_tab, int cos_rows, int64_t cos_stride, int rope_abs, int B, int S, int Hkv, int D,
+                int64_t k_sb, int64_t k_ss, int64_t k_sh, int64_t v_sb, int64_t v_ss, int64_t v_sh, int apply_rope,
+                int dtype, void* stream);
+
+/*
  * Synchronises `stream`, then returns and clears the device status word that
  * the kernels of this library write when a bounded wait runs out or a
  * device-side check fails (0 = no error).  Used by tests and debugging.

@@ -34,6 +34,11 @@ SIGNATURES = {
     "dt_device_status": (_I, [_P]),
     "dt_attn_prefill": (_I, [_P, _P, _P, _P, _P, _P, _I, _L, _P, _I, _I, _I, _I, _I,
                              _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _F, _I, _I, _P]),
+    "dt_attn_decode": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _P, _I, _P, _P, _P, _P, _I, _L, _I,
+                            _I, _I, _I, _I, _I, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L, _L,
+                            _F, _I, _I, _P]),
+    "dt_kv_write": (_I, [_P, _P, _P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _L, _I, _I, _I, _I, _I,
+                         _L, _L, _L, _L, _L, _L, _I, _I, _P]),
 }
 
 

@@ -207,3 +207,91 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
 }
 
 }  // extern "C"
+
+namespace {
+// Shared checks of the paged-cache arguments.
+int check_cache(const char* fn, const void* k_pages, const void* v_pages, int num_pages, int page_size,
+                const int32_t* block_table, int max_pages, int D, int dtype) {
+  if (!k_pages || !v_pages || !block_table) return fail(DT_ERR_INVALID, "%s: null cache pointer", fn);
+  if (num_pages < 1 || page_size < 1 || max_pages < 1)
+    return fail(DT_ERR_INVALID, "%s: num_pages, page_size, max_pages must be positive", fn);
+  if (D != 32 && D != 64) return fail(DT_ERR_UNSUPPORTED, "%s: head_dim %d not in {32, 64}", fn, D);
+  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
+    return fail(DT_ERR_UNSUPPORTED, "%s: dtype %d not supported", fn, dtype);
+  if (!aligned16(k_pages) || !aligned16(v_pages)) return fail(DT_ERR_INVALID, "%s: cache pages must be 16-byte aligned", fn);
+  return DT_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o, void* k_pages, void* v_pages,
+                   int num_pages, int page_size, const int32_t* block_table, int max_pages,
+                   const int32_t* seq_lens, const int32_t* pad_len, const float* cos_tab, const float* sin_tab,
+                   int cos_rows, int64_t cos_stride, int rope_abs, int B, int Sn, int Hq, int Hkv, int D,
+                   int64_t q_sb, int64_t q_ss, int64_t q_sh, int64_t kn_sb, int64_t kn_ss, int64_t kn_sh,
+                   int64_t vn_sb, int64_t vn_ss, int64_t vn_sh, int64_t o_sb, int64_t o_ss, int64_t o_sh,
+                   float scale, int apply_rope, int dtype, void* stream) {
+  const char* fn = "dt_attn_decode";
+  if (!q || !k_new || !v_new || !o || !seq_lens) return fail(DT_ERR_INVALID, "%s: null q/k_new/v_new/o/seq_lens", fn);
+  if (B < 1 || Sn < 1 || Hq < 1 || Hkv < 1) return fail(DT_ERR_INVALID, "%s: sizes must be positive", fn);
+  if (Hq % Hkv != 0)
+    return fail(DT_ERR_INVALID, "%s: num_attention_heads (%d) must be divisible by num_key_value_heads (%d)", fn,
+                Hq, Hkv);
+  int rc = check_cache(fn, k_pages, v_pages, num_pages, page_size, block_table, max_pages, D, dtype);
+  if (rc) return rc;
+  if ((long long)max_pages * page_size > 0x7fffffffLL) return fail(DT_ERR_INVALID, "%s: cache capacity too large", fn);
+  if (apply_rope) {
+    if (!cos_tab || !sin_tab) return fail(DT_ERR_INVALID, "%s: null cos/sin with apply_rope", fn);
+    if (!rope_abs && cos_rows < Sn) return fail(DT_ERR_INVALID, "%s: cos/sin have %d rows < Sn=%d", fn, cos_rows, Sn);
+    if (cos_stride < D) return fail(DT_ERR_INVALID, "%s: cos/sin row stride < D", fn);
+  }
+  int dev = 0;
+  int* status = nullptr;
+  if ((rc = device_setup(&dev, &status))) return rc;
+  if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
+  dtk::DecodeParams p;
+  p.q = q; p.k_new = k_new; p.v_new = v_new; p.o = o; p.k_pages = k_pages; p.v_pages = v_pages;
+  p.block_table = block_table; p.seq_lens = seq_lens; p.pad_len = pad_len; p.cos = cos_tab; p.sin = sin_tab;
+  p.status = status;
+  p.q_sb = q_sb; p.q_ss = q_ss; p.q_sh = q_sh; p.kn_sb = kn_sb; p.kn_ss = kn_ss; p.kn_sh = kn_sh;
+  p.vn_sb = vn_sb; p.vn_ss = vn_ss; p.vn_sh = vn_sh; p.o_sb = o_sb; p.o_ss = o_ss; p.o_sh = o_sh;
+  p.cs_stride = (int)cos_stride; p.rope = apply_rope ? 1 : 0; p.rope_abs = rope_abs ? 1 : 0; p.cos_rows = cos_rows;
+  p.Sn = Sn; p.Hkv = Hkv; p.R = Hq / Hkv; p.page_size = page_size; p.max_pages = max_pages; p.num_pages = num_pages;
+  const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
+  p.scale_log2 = sc * 1.4426950408889634f;
+  if ((long long)B * Hkv > 0x7fffffffLL) return fail(DT_ERR_UNSUPPORTED, "%s: B*Hkv too large", fn);
+  cudaError_t e = dtk::launch_decode_sm100(p, D, dtype == DT_DTYPE_BF16, B * Hkv, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dt_attn_decode launch");
+  return DT_OK;
+}
+
+int dt_kv_write(const void* k, const void* v, void* k_pages, void* v_pages, int num_pages, int page_size,
+                const int32_t* block_table, int max_pages, const int32_t* start_pos, const float* cos_tab,
+                const float* sin_tab, int cos_rows, int64_t cos_stride, int rope_abs, int B, int S, int Hkv, int D,
+                int64_t k_sb, int64_t k_ss, int64_t k_sh, int64_t v_sb, int64_t v_ss, int64_t v_sh, int apply_rope,
+                int dtype, void* stream) {
+  const char* fn = "dt_kv_write";
+  if (!k || !v) return fail(DT_ERR_INVALID, "%s: null k/v", fn);
+  if (B < 1 || S < 1 || Hkv < 1) return fail(DT_ERR_INVALID, "%s: sizes must be positive", fn);
+  int rc = check_cache(fn, k_pages, v_pages, num_pages, page_size, block_table, max_pages, D, dtype);
+  if (rc) return rc;
+  if (apply_rope) {
+    if (!cos_tab || !sin_tab) return fail(DT_ERR_INVALID, "%s: null cos/sin with apply_rope", fn);
+    if (!rope_abs && cos_rows < S) return fail(DT_ERR_INVALID, "%s: cos/sin have %d rows < S=%d", fn, cos_rows, S);
+  }
+  int dev = 0;
+  int* status = nullptr;
+  if ((rc = device_setup(&dev, &status))) return rc;
+  dtk::KvWriteParams p;
+  p.k = k; p.v = v; p.k_pages = k_pages; p.v_pages = v_pages; p.block_table = block_table; p.start_pos = start_pos;
+  p.cos = cos_tab; p.sin = sin_tab; p.status = status;
+  p.k_sb = k_sb; p.k_ss = k_ss; p.k_sh = k_sh; p.v_sb = v_sb; p.v_ss = v_ss; p.v_sh = v_sh;
+  p.cs_stride = (int)cos_stride; p.cos_rows = cos_rows; p.rope = apply_rope ? 1 : 0; p.rope_abs = rope_abs ? 1 : 0;
+  p.S = S; p.Hkv = Hkv; p.page_size = page_size; p.max_pages = max_pages; p.num_pages = num_pages;
+  cudaError_t e = dtk::launch_kv_write_sm100(p, D, dtype == DT_DTYPE_BF16, B, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dt_kv_write launch");
+  return DT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,387 @@
+// KV-cached decode attention for the Decision Transformer rollout, sm_100a.
+//
+// Replaces the cached ("slow") branch of DecisionTransformerAttention.forward
+// (model/model_decision_transformer.py:179-191 and :225-245): the new tokens'
+// K/V are rotated (RoPE, :180) and appended to the cache (the reference's
+// torch.cat, :188-190; here an in-place write into a paged cache), then the
+// new queries attend over all cached keys with the causal rule on the new
+// columns (:230-237), the optional padding mask (:238-242) and an fp32
+// softmax (:243).
+//
+// One CTA per (sample b, KV head g), 4 warps.  The cached K/V of the unit are
+// staged into shared memory (swizzled, 16-byte cp.async) in blocks of up to
+// KMAX keys; each warp takes a quarter of the keys of a block and runs the
+// R x Sn query rows (<= 16 per row group) against them with mma.sync
+// m16n8k16 (bf16/fp16 in, fp32 accumulate) and an online softmax; the four
+// partial (max, sum, O) are merged through shared memory (split-K).
+//
+// Cache layout: k_pages / v_pages [num_pages, Hkv, page_size, D], a page
+// holding page_size consecutive positions of one KV head contiguously;
+// block_table [B, max_pages] maps position p of sample b to page
+// block_table[b][p / page_size], slot p % page_size.  seq_lens[b] is the
+// number of cached positions before this call; the kernel writes the new
+// tokens at seq_lens[b] .. seq_lens[b] + Sn - 1 and leaves seq_lens alone.
+#include "dt_common.cuh"
+#include "dt_internal.h"
+
+namespace dtk {
+
+namespace {
+
+constexpr int kDecThreads = 128;
+constexpr int kDecWarps = 4;
+constexpr int kKMax = 256;  // keys staged per block
+
+template <int D>
+struct DecShape {
+  static constexpr int ROWB = D * 2;
+  static constexpr int CH = D / 8;  // 16-byte chunks per row
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + kKMax * ROWB;
+  static constexpr int OFF_Q = OFF_V + kKMax * ROWB;  // 16 rows
+  static constexpr int OFF_RED = OFF_Q + 16 * ROWB;   // [warps][16][D + 2] floats
+  static constexpr int RED_STRIDE = D + 2;
+  static constexpr int SMEM = OFF_RED + kDecWarps * 16 * RED_STRIDE * 4;
+};
+
+// Swizzled byte offset of 16-byte chunk c of row r (64-byte rows: XOR with
+// (r >> 1) & 3; 128-byte rows: XOR with r & 7) -- conflict-free ldmatrix.
+template <int D>
+__device__ __forceinline__ uint32_t dswz(int r, int c) {
+  if constexpr (D == 32) return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+  else return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// Rotate-half RoPE of element pair (d, d + D/2) given fp32 inputs.
+__device__ __forceinline__ void rope_pair(float x0, float x1, float c0, float s0, float c1, float s1, float& y0,
+                                          float& y1) {
+  y0 = x0 * c0 - x1 * s0;
+  y1 = x1 * c1 + x0 * s1;
+}
+
+}  // namespace
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodeParams p) {
+  using SH = DecShape<D>;
+  using E = Elem<BF16>;
+  using T = typename E::T;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int b = blockIdx.x / p.Hkv;
+  const int g = blockIdx.x - b * p.Hkv;
+  const int R = p.R, Sn = p.Sn;
+  const int L = p.seq_lens[b];
+  const int kv_len = L + Sn;
+  int pad = p.pad_len ? p.pad_len[b] : 0;
+  pad = max(0, min(pad, kv_len));
+  const int32_t* bt = p.block_table + (size_t)b * p.max_pages;
+
+  // Device-side bounds: capacity and page ids of every position touched.
+  bool bad = L < 0 || kv_len > p.max_pages * p.page_size || (p.rope && p.rope_abs && kv_len > p.cos_rows);
+  if (!bad) {
+    for (int pg = tid; pg * p.page_size < kv_len; pg += kDecThreads) {
+      const int id = bt[pg];
+      if (id < 0 || id >= p.num_pages) bad = true;
+    }
+  }
+  if (__syncthreads_or(bad)) {
+    if (tid == 0 && p.status) atomicExch(p.status, (int)kDevBadShape);
+    return;
+  }
+
+  uint8_t* ks = smem + SH::OFF_K;
+  uint8_t* vs = smem + SH::OFF_V;
+  uint8_t* qs = smem + SH::OFF_Q;
+  float* red = reinterpret_cast<float*>(smem + SH::OFF_RED);
+  const size_t page_stride = (size_t)p.Hkv * p.page_size * D;  // elements per page
+  auto cache_off = [&](int pos) -> size_t {
+    return (size_t)bt[pos / p.page_size] * page_stride + ((size_t)g * p.page_size + pos % p.page_size) * D;
+  };
+  auto cos_row = [&](int i) -> const float* {
+    return p.cos + (size_t)(p.rope_abs ? L + i : i) * p.cs_stride;
+  };
+  auto sin_row = [&](int i) -> const float* {
+    return p.sin + (size_t)(p.rope_abs ? L + i : i) * p.cs_stride;
+  };
+
+  // ---- append: rotate the new keys, write new K/V into the paged cache.
+  for (int e = tid; e < Sn * (D / 2); e += kDecThreads) {
+    const int i = e / (D / 2), d = e - i * (D / 2);
+    const T* kn = reinterpret_cast<const T*>(p.k_new) + (size_t)b * p.kn_sb + (size_t)i * p.kn_ss +
+                  (size_t)g * p.kn_sh;
+    const T* vn = reinterpret_cast<const T*>(p.v_new) + (size_t)b * p.vn_sb + (size_t)i * p.vn_ss +
+                  (size_t)g * p.vn_sh;
+    float k0 = (float)kn[d], k1 = (float)kn[d + D / 2];
+    if (p.rope) {
+      const float* cr = cos_row(i);
+      const float* sr = sin_row(i);
+      float y0, y1;
+      rope_pair(k0, k1, cr[d], sr[d], cr[d + D / 2], sr[d + D / 2], y0, y1);
+      k0 = y0;
+      k1 = y1;
+    }
+    const size_t off = cache_off(L + i);
+    T* kc = reinterpret_cast<T*>(p.k_pages) + off;
+    T* vc = reinterpret_cast<T*>(p.v_pages) + off;
+    kc[d] = (T)k0;
+    kc[d + D / 2] = (T)k1;
+    vc[d] = vn[d];
+    vc[d + D / 2] = vn[d + D / 2];
+  }
+  // ---- queries: rows r = i * R + h (i < Sn), rotated, into shared memory.
+  const int nrows = Sn * R;
+  const int ngroups = (nrows + 15) / 16;
+  const float c2 = p.scale_log2;
+  // Make this CTA's cache writes visible to its own loads below.
+  __threadfence_block();
+  __syncthreads();
+
+  for (int rg = 0; rg < ngroups; ++rg) {
+    for (int e = tid; e < 16 * (D / 2); e += kDecThreads) {
+      const int rr = e / (D / 2), d = e - rr * (D / 2);
+      const int row = rg * 16 + rr;
+      float y0 = 0.f, y1 = 0.f;
+      if (row < nrows) {
+        const int i = row / R, h = row - (row / R) * R;
+        const T* qr = reinterpret_cast<const T*>(p.q) + (size_t)b * p.q_sb + (size_t)i * p.q_ss +
+                      (size_t)(g * R + h) * p.q_sh;
+        float x0 = (float)qr[d], x1 = (float)qr[d + D / 2];
+        if (p.rope) {
+          const float* cr = cos_row(i);
+          const float* sr = sin_row(i);
+          rope_pair(x0, x1, cr[d], sr[d], cr[d + D / 2], sr[d + D / 2], y0, y1);
+        } else {
+          y0 = x0;
+          y1 = x1;
+        }
+      }
+      // element d lives in chunk d / 8 (swizzled) at offset d % 8
+      reinterpret_cast<T*>(qs + dswz<D>(rr, d / 8))[d % 8] = (T)y0;
+      reinterpret_cast<T*>(qs + dswz<D>(rr, (d + D / 2) / 8))[(d + D / 2) % 8] = (T)y1;
+    }
+    __syncthreads();
+
+    // A fragments of Q (16 rows x D) for every k16 step.
+    uint32_t qa[D / 16][4];
+    {
+      const int r = lane & 15, cb = lane >> 4;  // row, 8-column block within the k16 step
+#pragma unroll
+      for (int s = 0; s < D / 16; ++s)
+        ldsm_x4(smem_u32(qs + dswz<D>(r, 2 * s + cb)), qa[s][0], qa[s][1], qa[s][2], qa[s][3]);
+    }
+    // This thread's two rows: g8 and g8 + 8 (C-fragment layout).
+    const int g8 = lane >> 2, t4 = lane & 3;
+    int rpos[2], rlo[2], rhi[2];
+    bool rpad[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int row = rg * 16 + g8 + 8 * k;
+      const bool valid = row < nrows;
+      const int i = valid ? row / R : 0;
+      rpos[k] = L + i;  // absolute position of this query
+      rpad[k] = rpos[k] < pad;
+      rlo[k] = rpad[k] ? 0 : pad;
+      rhi[k] = valid ? rpos[k] : -1;
+    }
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    float oacc[D / 8][4];
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
+
+    for (int kb = 0; kb < kv_len; kb += kKMax) {
+      const int nk = min(kKMax, kv_len - kb);
+      // ---- stage keys [kb, kb + nk) of K and V (16-byte cp.async, swizzled rows).
+      if (rg > 0 || kb > 0) __syncthreads();  // previous block fully consumed
+      for (int e = tid; e < nk * SH::CH; e += kDecThreads) {
+        const int key = e / SH::CH, c = e - key * SH::CH;
+        const size_t off = cache_off(kb + key) + (size_t)c * 8;
+        cp_async16(smem_u32(ks + dswz<D>(key, c)), reinterpret_cast<const T*>(p.k_pages) + off);
+        cp_async16(smem_u32(vs + dswz<D>(key, c)), reinterpret_cast<const T*>(p.v_pages) + off);
+      }
+      // zero-fill the tail of the last 16-key chunk so masked keys hold finite data
+      const int nk16 = (nk + 15) & ~15;
+      for (int e = tid; e < (nk16 - nk) * SH::CH; e += kDecThreads) {
+        const int key = nk + e / SH::CH, c = e % SH::CH;
+        *reinterpret_cast<uint4*>(ks + dswz<D>(key, c)) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(vs + dswz<D>(key, c)) = make_uint4(0, 0, 0, 0);
+      }
+      cp_async_wait_all();
+      __syncthreads();
+
+      // ---- this warp's 16-key chunks of the block (split-K across warps).
+      const int nchunks = nk16 / 16;
+      for (int ch = warp; ch < nchunks; ch += kDecWarps) {
+        const int key0 = ch * 16;  // within block
+        float sc[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+        // S = Q K^T: key blocks j (8 keys), k16 steps s.
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int krow = key0 + 8 * j + (lane & 7);
+#pragma unroll
+          for (int s2 = 0; s2 < D / 32; ++s2) {
+            // four 8x8 matrices: dims [32 s2 + 8 m, +8) for m = lane / 8
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(smem_u32(ks + dswz<D>(krow, 4 * s2 + (lane >> 3))), b0, b1, b2, b3);
+            mma16816<BF16>(sc[j], qa[2 * s2], b0, b1);
+            mma16816<BF16>(sc[j], qa[2 * s2 + 1], b2, b3);
+          }
+        }
+        // Online softmax over these 16 keys (rows g8 / g8 + 8; cols 2 t4 + {0,1} per key block).
+        float pv[2][4];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          float cmax = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e2 = 0; e2 < 2; ++e2) {
+              const int key = kb + key0 + 8 * j + 2 * t4 + e2;
+              const bool ok = key >= rlo[k] && key <= rhi[k];
+              const float v = sc[j][2 * k + e2];
+              if (ok) cmax = fmaxf(cmax, v);
+            }
+          cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
+          cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
+          float m_new, cr;
+          if (rpad[k]) {
+            m_new = 0.f;  // padded row: unit weights (exp2(0)) on keys 0..q
+            cr = 0.f;
+          } else {
+            m_new = fmaxf(m_run[k], cmax * c2);
+            cr = c2;
+          }
+          const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+          const float alpha = rpad[k] ? 1.f : ex2_approx(m_run[k] - m_use);
+          float lsum = 0.f;
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e2 = 0; e2 < 2; ++e2) {
+              const int key = kb + key0 + 8 * j + 2 * t4 + e2;
+              const bool ok = key >= rlo[k] && key <= rhi[k];
+              const float pe = ok ? ex2_approx(fmaf(sc[j][2 * k + e2], cr, -m_use)) : 0.f;
+              pv[j][2 * k + e2] = pe;
+              lsum += pe;
+            }
+          lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+          lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+          l_run[k] = l_run[k] * alpha + lsum;
+          m_run[k] = rpad[k] ? m_run[k] : m_new;
+#pragma unroll
+          for (int jd = 0; jd < D / 8; ++jd) {
+            oacc[jd][2 * k] *= alpha;
+            oacc[jd][2 * k + 1] *= alpha;
+          }
+        }
+        // O += P V: P (16 rows x 16 keys) as the A fragment, V via ldmatrix.trans.
+        uint32_t pa[4];
+        pa[0] = E::from_f2(pv[0][0], pv[0][1]);
+        pa[1] = E::from_f2(pv[0][2], pv[0][3]);
+        pa[2] = E::from_f2(pv[1][0], pv[1][1]);
+        pa[3] = E::from_f2(pv[1][2], pv[1][3]);
+#pragma unroll
+        for (int jd2 = 0; jd2 < D / 16; ++jd2) {
+          // matrices: (keys 0-7 | 8-15) x (dims 16 jd2 + 0-7 | 8-15)
+          const int vrow = key0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int vch = 2 * jd2 + (lane >> 4);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(smem_u32(vs + dswz<D>(vrow, vch)), b0, b1, b2, b3);
+          mma16816<BF16>(oacc[2 * jd2], pa, b0, b1);
+          mma16816<BF16>(oacc[2 * jd2 + 1], pa, b2, b3);
+        }
+      }
+    }
+    // ---- merge the four warps' partials (m, l, O) per row and store.
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int rr = g8 + 8 * k;
+      float* rw = red + (warp * 16 + rr) * SH::RED_STRIDE;
+      if (t4 == 0) {
+        rw[D] = m_run[k];
+        rw[D + 1] = l_run[k];
+      }
+#pragma unroll
+      for (int jd = 0; jd < D / 8; ++jd) {
+        rw[8 * jd + 2 * t4] = oacc[jd][2 * k];
+        rw[8 * jd + 2 * t4 + 1] = oacc[jd][2 * k + 1];
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < 16 * D; e += kDecThreads) {
+      const int rr = e / D, d = e - rr * D;
+      const int row = rg * 16 + rr;
+      if (row >= nrows) continue;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, red[(w * 16 + rr) * SH::RED_STRIDE + D]);
+      const float Mu = (M == -INFINITY) ? 0.f : M;
+      float lt = 0.f, ot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) {
+        const float* rw = red + (w * 16 + rr) * SH::RED_STRIDE;
+        const float sc = ex2_approx(rw[D] - Mu);  // padded rows: m = -inf for all warps -> M = -inf -> factor 1
+        const float f = (rw[D] == -INFINITY) ? (M == -INFINITY ? 1.f : 0.f) : sc;
+        lt += f * rw[D + 1];
+        ot += f * rw[d];
+      }
+      const int i = row / R, h = row - (row / R) * R;
+      T* orow = reinterpret_cast<T*>(p.o) + (size_t)b * p.o_sb + (size_t)i * p.o_ss + (size_t)(g * R + h) * p.o_sh;
+      orow[d] = (T)(ot / lt);
+    }
+    __syncthreads();
+  }
+}
+
+cudaError_t launch_decode_sm100(const DecodeParams& prm, int D, bool bf16, int grid, cudaStream_t stream) {
+  auto go = [&](auto kfn, int smem) -> cudaError_t {
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    kfn<<<grid, kDecThreads, smem, stream>>>(prm);
+    return cudaGetLastError();
+  };
+  if (D == 32) return bf16 ? go(dt_decode_kernel<32, true>, DecShape<32>::SMEM)
+                           : go(dt_decode_kernel<32, false>, DecShape<32>::SMEM);
+  if (D == 64) return bf16 ? go(dt_decode_kernel<64, true>, DecShape<64>::SMEM)
+                           : go(dt_decode_kernel<64, false>, DecShape<64>::SMEM);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace dtk

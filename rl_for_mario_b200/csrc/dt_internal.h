@@ -29,4 +29,45 @@ cudaError_t launch_prefill_short_sm100(const CUtensorMap& q, const CUtensorMap& 
                                        const PrefillParams& prm, bool bf16, int n_units, int grid,
                                        cudaStream_t stream);
 
+// Kernel parameters of the paged-cache decode (dt_attn_decode).
+struct DecodeParams {
+  const void* q;             // [B, Sn, Hq, D] new queries (pre-RoPE)
+  const void* k_new;         // [B, Sn, Hkv, D] new keys (pre-RoPE)
+  const void* v_new;         // [B, Sn, Hkv, D] new values
+  void* o;                   // [B, Sn, Hq, D]
+  void* k_pages;             // [num_pages, Hkv, page_size, D]
+  void* v_pages;
+  const int32_t* block_table;  // [B, max_pages]
+  const int32_t* seq_lens;     // [B] cached positions before this call
+  const int32_t* pad_len;      // [B] or null
+  const float* cos;
+  const float* sin;
+  int* status;
+  long long q_sb, q_ss, q_sh, kn_sb, kn_ss, kn_sh, vn_sb, vn_ss, vn_sh, o_sb, o_ss, o_sh;
+  int cs_stride, rope, rope_abs;
+  int cos_rows;
+  int Sn, Hkv, R, page_size, max_pages, num_pages;
+  float scale_log2;
+};
+
+// Kernel parameters of dt_kv_write.
+struct KvWriteParams {
+  const void* k;               // [B, S, Hkv, D] keys (pre-RoPE)
+  const void* v;               // [B, S, Hkv, D]
+  void* k_pages;
+  void* v_pages;
+  const int32_t* block_table;  // [B, max_pages]
+  const int32_t* start_pos;    // [B] or null (0)
+  const float* cos;
+  const float* sin;
+  int* status;
+  long long k_sb, k_ss, k_sh, v_sb, v_ss, v_sh;
+  int cs_stride, cos_rows, rope, rope_abs;
+  int S, Hkv, page_size, max_pages, num_pages;
+};
+
+cudaError_t launch_kv_write_sm100(const KvWriteParams& prm, int D, bool bf16, int B, cudaStream_t stream);
+
+cudaError_t launch_decode_sm100(const DecodeParams& prm, int D, bool bf16, int grid, cudaStream_t stream);
+
 }  // namespace dtk

@@ -101,3 +101,83 @@ def device_status(device: Optional[torch.device] = None) -> int:
 
 def default_scale(D: int) -> float:
     return 1.0 / math.sqrt(D)
+
+
+def _prep_tables(cos: Optional[Tensor], sin: Optional[Tensor]):
+    if cos is None or sin is None:
+        raise ValueError("apply_rope needs cos and sin")
+    if cos.dtype != torch.float32 or cos.stride(-1) != 1:
+        cos = cos.float().contiguous()
+    if sin.dtype != torch.float32 or sin.stride(-1) != 1:
+        sin = sin.float().contiguous()
+    if cos.stride(0) != sin.stride(0):
+        cos, sin = cos.contiguous(), sin.contiguous()
+    return cos, sin
+
+
+def attn_decode(q: Tensor, k_new: Tensor, v_new: Tensor, layer, cos: Optional[Tensor], sin: Optional[Tensor],
+                pad_len: Optional[Tensor] = None, rope_abs: bool = False, out: Optional[Tensor] = None,
+                apply_rope: bool = True, scale: Optional[float] = None) -> Tensor:
+    """Cached decode step: q [B,Sn,Hq,D], k_new/v_new [B,Sn,Hkv,D] -> out [B,Sn,Hq,D].
+
+    Appends the rotated k_new / v_new to ``layer`` (a cache.LayerKV) at
+    positions layer.seq_lens .. +Sn and attends over all cached keys.  Does not
+    advance the layer's length (the caller does, once per step).
+    """
+    _require_cuda(q, k_new, v_new, cos, sin, pad_len, out)
+    B, Sn, Hq, D = q.shape
+    Hkv = k_new.shape[2]
+    if k_new.shape != (B, Sn, Hkv, D) or v_new.shape != (B, Sn, Hkv, D):
+        raise ValueError("k_new/v_new shapes do not match q")
+    if not (q.dtype == k_new.dtype == v_new.dtype == layer.k_pages.dtype):
+        raise TypeError("q, k_new, v_new and the cache must share a dtype")
+    if layer.batch != B or layer.num_kv_heads != Hkv or layer.head_dim != D:
+        raise ValueError("cache geometry does not match the inputs")
+    if layer.length + Sn > layer.capacity:
+        raise ValueError(f"cache full: {layer.length} + {Sn} > capacity {layer.capacity}")
+    for name, t in (("q", q), ("k_new", k_new), ("v_new", v_new)):
+        if t.stride(3) != 1:
+            raise ValueError(f"{name} must be contiguous in head_dim")
+    if out is None:
+        out = torch.empty((B, Sn, Hq, D), dtype=q.dtype, device=q.device)
+    if apply_rope:
+        cos, sin = _prep_tables(cos, sin)
+    if pad_len is not None:
+        pad_len = pad_len.to(torch.int32).contiguous()
+    lib = _lib.load()
+    rc = lib.dt_attn_decode(
+        _ptr(q), _ptr(k_new), _ptr(v_new), _ptr(out), _ptr(layer.k_pages), _ptr(layer.v_pages),
+        layer.k_pages.shape[0], layer.page_size, _ptr(layer.block_table), layer.block_table.shape[1],
+        _ptr(layer.seq_lens), _ptr(pad_len), _ptr(cos) if apply_rope else None, _ptr(sin) if apply_rope else None,
+        cos.shape[0] if apply_rope else 0, cos.stride(0) if apply_rope else 0, 1 if rope_abs else 0,
+        B, Sn, Hq, Hkv, D, q.stride(0), q.stride(1), q.stride(2), k_new.stride(0), k_new.stride(1),
+        k_new.stride(2), v_new.stride(0), v_new.stride(1), v_new.stride(2), out.stride(0), out.stride(1),
+        out.stride(2), float(scale) if scale is not None else 0.0, 1 if apply_rope else 0, _dtype_code(q),
+        _stream_ptr(q.device))
+    _lib.check("dt_attn_decode", rc)
+    return out
+
+
+def kv_write(k: Tensor, v: Tensor, layer, cos: Optional[Tensor], sin: Optional[Tensor],
+             start_pos: Optional[Tensor] = None, rope_abs: bool = False, apply_rope: bool = True) -> None:
+    """Writes k (rotated) and v [B,S,Hkv,D] into ``layer`` at positions start_pos[b] + s."""
+    _require_cuda(k, v, cos, sin, start_pos)
+    B, S, Hkv, D = k.shape
+    if v.shape != k.shape:
+        raise ValueError("k and v shapes differ")
+    if k.dtype != layer.k_pages.dtype or v.dtype != k.dtype:
+        raise TypeError("k, v and the cache must share a dtype")
+    if k.stride(3) != 1 or v.stride(3) != 1:
+        raise ValueError("k/v must be contiguous in head_dim")
+    if apply_rope:
+        cos, sin = _prep_tables(cos, sin)
+    if start_pos is not None:
+        start_pos = start_pos.to(torch.int32).contiguous()
+    lib = _lib.load()
+    rc = lib.dt_kv_write(
+        _ptr(k), _ptr(v), _ptr(layer.k_pages), _ptr(layer.v_pages), layer.k_pages.shape[0], layer.page_size,
+        _ptr(layer.block_table), layer.block_table.shape[1], _ptr(start_pos), _ptr(cos) if apply_rope else None,
+        _ptr(sin) if apply_rope else None, cos.shape[0] if apply_rope else 0, cos.stride(0) if apply_rope else 0,
+        1 if rope_abs else 0, B, S, Hkv, D, k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
+        v.stride(2), 1 if apply_rope else 0, _dtype_code(k), _stream_ptr(k.device))
+    _lib.check("dt_kv_write", rc)
