@@ -1,0 +1,141 @@
+"""Drop-in replacement of DecisionTransformerAttention backed by the sm_100a kernels.
+
+``FastDTAttention`` keeps the reference module's constructor contract
+(model/model_decision_transformer.py:137-163: same parameter names
+q_proj/k_proj/v_proj/o_proj, ValueError when heads do not divide) and its
+forward contract (:165-172, 249):
+
+    forward(x, position_embeddings, past_key_value=None, use_cache=False,
+            attention_mask=None) -> (out, past_kv)
+
+Dispatch follows the reference (:198): the prefill kernel when
+``flash and seq_len > 1 and past_key_value is None``, the cached decode
+kernel otherwise.  ``past_key_value`` may be the reference's tuple of dense
+tensors (functional: a new, longer tuple is returned, like torch.cat) or a
+``cache.LayerKV`` (paged, appended in place and returned).
+
+Masks: ``attention_mask`` [B, S] (prefill) or [B, kv_len] (decode), 1 =
+valid, is taken as left padding (the layout scripts/mario/dt_offline_dataset.py
+:228-235 produces); set ``check_masks=True`` to verify that on the host.
+Numerics: the kernels compute in bf16 (or fp16) with fp32 softmax and
+accumulation; an fp32 module casts Q/K/V to ``compute_dtype`` for the kernels
+and casts the result back.  There is no CPU path: CPU inputs raise.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+from torch import nn
+
+from . import kernels
+from .cache import LayerKV, dense_layer
+
+Tensor = torch.Tensor
+
+
+class FastDTAttention(nn.Module):
+    def __init__(self, config, compute_dtype: torch.dtype = torch.bfloat16, check_masks: bool = False):
+        super().__init__()
+        self.num_key_value_heads = (config.num_attention_heads if config.num_key_value_heads is None
+                                    else config.num_key_value_heads)
+        if config.num_attention_heads % self.num_key_value_heads != 0:
+            raise ValueError("num_attention_heads must be divisible by num_key_value_heads")
+        self.n_local_heads = config.num_attention_heads
+        self.n_local_kv_heads = self.num_key_value_heads
+        self.n_rep = self.n_local_heads // self.n_local_kv_heads
+        self.head_dim = config.hidden_size // config.num_attention_heads
+        self.dropout = getattr(config, "dropout", 0.0)
+        self.flash = bool(getattr(config, "flash_attn", True))
+        self.q_proj = nn.Linear(config.hidden_size, self.n_local_heads * self.head_dim, bias=False)
+        self.k_proj = nn.Linear(config.hidden_size, self.n_local_kv_heads * self.head_dim, bias=False)
+        self.v_proj = nn.Linear(config.hidden_size, self.n_local_kv_heads * self.head_dim, bias=False)
+        self.o_proj = nn.Linear(self.n_local_heads * self.head_dim, config.hidden_size, bias=False)
+        self.attn_dropout = nn.Dropout(self.dropout)
+        self.resid_dropout = nn.Dropout(self.dropout)
+        self.compute_dtype = compute_dtype
+        self.check_masks = check_masks
+
+    @classmethod
+    def from_reference(cls, ref_attn: nn.Module, config, **kw) -> "FastDTAttention":
+        """Builds the fast module with the weights of a reference DecisionTransformerAttention."""
+        m = cls(config, **kw)
+        m.load_state_dict(ref_attn.state_dict())
+        p = next(ref_attn.parameters())
+        return m.to(device=p.device, dtype=p.dtype)
+
+    # ------------------------------------------------------------------ helpers
+    def _kernel_dtype(self, x: Tensor) -> torch.dtype:
+        return x.dtype if x.dtype in (torch.bfloat16, torch.float16) else self.compute_dtype
+
+    def _pad_len(self, mask: Optional[Tensor], length: int) -> Optional[Tensor]:
+        if mask is None:
+            return None
+        if mask.dim() != 2 or mask.shape[1] != length:
+            raise ValueError(f"attention_mask must be [B, {length}], got {tuple(mask.shape)}")
+        pad = kernels.pad_len_from_mask(mask, length)
+        if self.check_masks:
+            want = torch.arange(length, device=mask.device)[None] >= pad[:, None]
+            if not torch.equal(want, mask != 0):
+                raise ValueError("attention_mask is not a left-padding mask (zeros then ones per row)")
+        return pad
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, x: Tensor, position_embeddings: Tuple[Tensor, Tensor],
+                past_key_value=None, use_cache: bool = False, attention_mask: Optional[Tensor] = None):
+        if not x.is_cuda:
+            raise ValueError("FastDTAttention runs on CUDA only (no CPU path)")
+        bsz, seq_len, _ = x.shape
+        kd = self._kernel_dtype(x)
+        xq = self.q_proj(x).view(bsz, seq_len, self.n_local_heads, self.head_dim).to(kd)
+        xk = self.k_proj(x).view(bsz, seq_len, self.n_local_kv_heads, self.head_dim).to(kd)
+        xv = self.v_proj(x).view(bsz, seq_len, self.n_local_kv_heads, self.head_dim).to(kd)
+        cos, sin = position_embeddings
+
+        if self.flash and seq_len > 1 and past_key_value is None:
+            out = kernels.attn_prefill(xq, xk, xv, cos, sin, self._pad_len(attention_mask, seq_len))
+            past_kv = None
+            if use_cache:
+                kc = torch.empty(bsz, self.n_local_kv_heads, seq_len, self.head_dim, dtype=kd, device=x.device)
+                vc = torch.empty_like(kc)
+                layer = dense_layer(kc, vc, 0)
+                kernels.kv_write(xk, xv, layer, cos, sin)
+                past_kv = (kc, vc)
+        else:
+            if isinstance(past_key_value, LayerKV):
+                layer = past_key_value
+                if layer.k_pages.dtype != kd:
+                    raise TypeError(f"cache dtype {layer.k_pages.dtype} differs from compute dtype {kd}")
+                kv_len = layer.length + seq_len
+                out = kernels.attn_decode(xq, xk, xv, layer, cos, sin, self._pad_len(attention_mask, kv_len))
+                layer.advance(seq_len)
+                past_kv = layer if use_cache else None
+            else:
+                # Reference tuple (or no cache): functional append into new dense tensors.
+                L = 0 if past_key_value is None else past_key_value[0].shape[2]
+                kc = torch.empty(bsz, self.n_local_kv_heads, L + seq_len, self.head_dim, dtype=kd,
+                                 device=x.device)
+                vc = torch.empty_like(kc)
+                if L:
+                    kc[:, :, :L].copy_(past_key_value[0])
+                    vc[:, :, :L].copy_(past_key_value[1])
+                layer = dense_layer(kc, vc, L)
+                out = kernels.attn_decode(xq, xk, xv, layer, cos, sin,
+                                          self._pad_len(attention_mask, L + seq_len))
+                past_kv = (kc, vc) if use_cache else None
+
+        out = out.reshape(bsz, seq_len, -1).to(x.dtype)
+        return self.resid_dropout(self.o_proj(out)), past_kv
+
+
+def swap_attention(model: nn.Module, config, **kw) -> int:
+    """Replaces every ``self_attn`` DecisionTransformerAttention of a reference DT
+    (or of dt_model.MarioDT) by FastDTAttention with the same weights; returns
+    the number of modules swapped."""
+    n = 0
+    for name, mod in list(model.named_modules()):
+        attn = getattr(mod, "self_attn", None)
+        if attn is not None and not isinstance(attn, FastDTAttention) and hasattr(attn, "q_proj"):
+            mod.self_attn = FastDTAttention.from_reference(attn, config, **kw)
+            n += 1
+    return n

@@ -1,0 +1,254 @@
+"""Host model around the attention kernels: the Mario Decision Transformer.
+
+A restatement of the reference model (model/model_decision_transformer.py:
+config :17-55, RMSNorm :76-86, RoPE tables :93-99, FeedForward :256-271,
+block :278-304, state encoder :315-341, backbone :348-461, wrapper :468-548)
+whose attention is ``FastDTAttention``.  Parameter names match the reference,
+so a reference state_dict loads unchanged (checkpoint compatibility).  The
+glue around the attention (CNN encoder, embeddings, norms, SwiGLU FFN, heads)
+runs as ordinary PyTorch on the GPU.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .attention import FastDTAttention
+from .cache import LayerKV, PagedKVCache
+
+Tensor = torch.Tensor
+
+
+@dataclass
+class DTConfig:
+    """Fields and defaults of DecisionTransformerConfig (:20-55)."""
+
+    state_shape: Tuple[int, int, int] = (4, 84, 84)
+    act_dim: int = 7
+    max_ep_len: int = 4096
+    context_len: int = 64
+    hidden_size: int = 512
+    intermediate_size: Optional[int] = None
+    num_hidden_layers: int = 6
+    num_attention_heads: int = 8
+    num_key_value_heads: int = 2
+    hidden_act: str = "silu"
+    dropout: float = 0.1
+    rms_norm_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    flash_attn: bool = True
+    label_smoothing: float = 0.1
+    max_position_embeddings: int = field(init=False)
+
+    def __post_init__(self):
+        self.state_shape = tuple(self.state_shape)
+        self.max_position_embeddings = self.context_len * 3
+
+    @classmethod
+    def from_reference(cls, ref_cfg) -> "DTConfig":
+        names = [f for f in cls.__dataclass_fields__ if f != "max_position_embeddings"]
+        return cls(**{n: getattr(ref_cfg, n) for n in names})
+
+
+class RMSNorm(nn.Module):
+    """weight * (x * rsqrt(mean(x^2) + eps)) in fp32, cast back (:76-86)."""
+
+    def __init__(self, dim: int, eps: float = 1e-5):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: Tensor) -> Tensor:
+        xf = x.float()
+        return self.weight * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).type_as(x)
+
+
+def rope_tables(dim: int, end: int, base: float) -> Tuple[Tensor, Tensor]:
+    """cos/sin [end, dim] with duplicated halves (:93-99)."""
+    inv = 1.0 / (base ** (torch.arange(0, dim, 2).float() / dim))
+    ang = torch.outer(torch.arange(end).float(), inv)
+    return torch.cat([ang.cos(), ang.cos()], -1), torch.cat([ang.sin(), ang.sin()], -1)
+
+
+class FeedForward(nn.Module):
+    """SwiGLU, width 64 * ceil(8H/3 / 64) by default (:256-271)."""
+
+    def __init__(self, cfg: DTConfig):
+        super().__init__()
+        inter = cfg.intermediate_size
+        if inter is None:
+            inter = int(cfg.hidden_size * 8 / 3)
+            inter = 64 * ((inter + 63) // 64)
+        self.gate_proj = nn.Linear(cfg.hidden_size, inter, bias=False)
+        self.up_proj = nn.Linear(cfg.hidden_size, inter, bias=False)
+        self.down_proj = nn.Linear(inter, cfg.hidden_size, bias=False)
+        self.dropout = nn.Dropout(cfg.dropout)
+
+    def forward(self, x: Tensor) -> Tensor:
+        return self.dropout(self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x)))
+
+
+class DTBlock(nn.Module):
+    """Pre-norm block (:278-304)."""
+
+    def __init__(self, cfg: DTConfig):
+        super().__init__()
+        self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        self.self_attn = FastDTAttention(cfg)
+        self.mlp = FeedForward(cfg)
+
+    def forward(self, hidden_states, position_embeddings, past_key_value=None, use_cache=False,
+                attention_mask=None):
+        h, present = self.self_attn(self.input_layernorm(hidden_states), position_embeddings,
+                                    past_key_value=past_key_value, use_cache=use_cache,
+                                    attention_mask=attention_mask)
+        h = h + hidden_states
+        h = h + self.mlp(self.post_attention_layernorm(h))
+        return h, present
+
+
+class MarioStateEncoder(nn.Module):
+    """Nature-DQN CNN (:315-341)."""
+
+    def __init__(self, state_shape, hidden_size: int):
+        super().__init__()
+        c = state_shape[0]
+        self.cnn = nn.Sequential(
+            nn.Conv2d(c, 32, 8, 4), nn.ReLU(inplace=True), nn.Conv2d(32, 64, 4, 2), nn.ReLU(inplace=True),
+            nn.Conv2d(64, 64, 3, 1), nn.ReLU(inplace=True), nn.Flatten(), nn.Linear(64 * 7 * 7, hidden_size))
+
+    def forward(self, states: Tensor) -> Tensor:
+        if states.ndim != 5:
+            raise ValueError(f"states must be [B,T,C,H,W], got {tuple(states.shape)}")
+        B, T, C, H, W = states.shape
+        x = states.to(self.cnn[0].weight.dtype)
+        if x.max() > 1.0:
+            x = x / 255.0
+        return self.cnn(x.reshape(B * T, C, H, W)).reshape(B, T, -1)
+
+
+class DTBackbone(nn.Module):
+    """DecisionTransformerModel (:348-461)."""
+
+    def __init__(self, cfg: DTConfig):
+        super().__init__()
+        self.config = cfg
+        self.state_encoder = MarioStateEncoder(cfg.state_shape, cfg.hidden_size)
+        self.embed_return = nn.Linear(1, cfg.hidden_size)
+        self.embed_action = nn.Embedding(cfg.act_dim, cfg.hidden_size)
+        self.embed_timestep = nn.Embedding(cfg.max_ep_len, cfg.hidden_size)
+        self.embed_norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        self.dropout = nn.Dropout(cfg.dropout)
+        self.layers = nn.ModuleList([DTBlock(cfg) for _ in range(cfg.num_hidden_layers)])
+        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        cos, sin = rope_tables(cfg.hidden_size // cfg.num_attention_heads, cfg.max_position_embeddings,
+                               cfg.rope_theta)
+        self.register_buffer("freqs_cos", cos, persistent=False)
+        self.register_buffer("freqs_sin", sin, persistent=False)
+
+    def embed(self, states, actions, returns_to_go, timesteps) -> Tensor:
+        """Token embeddings interleaved (R, s, a) -> [B, 3T, H] after embed_norm (:401-420)."""
+        cfg = self.config
+        B, T = states.shape[0], states.shape[1]
+        ts = timesteps.clamp(0, cfg.max_ep_len - 1).long()
+        te = self.embed_timestep(ts)
+        se = self.state_encoder(states) + te
+        re = self.embed_return(returns_to_go.unsqueeze(-1).to(self.embed_return.weight.dtype)) + te
+        ae = self.embed_action(actions.long().clamp(0, cfg.act_dim - 1)) + te
+        h = torch.stack((re, se, ae), dim=2).reshape(B, 3 * T, cfg.hidden_size)
+        return self.dropout(self.embed_norm(h))
+
+    def forward(self, states, actions, returns_to_go, timesteps, attention_mask=None, past_key_values=None,
+                use_cache=False):
+        cfg = self.config
+        B, T = states.shape[0], states.shape[1]
+        if states.ndim != 5:
+            raise ValueError(f"states must be [B,T,C,H,W], got {tuple(states.shape)}")
+        if states.shape[2:] != tuple(cfg.state_shape):
+            raise ValueError(f"states spatial shape {tuple(states.shape[2:])} != config {cfg.state_shape}")
+        if actions is None or actions.shape[:2] != (B, T):
+            raise ValueError("actions must be [B,T]")
+        if returns_to_go.shape[:2] != (B, T):
+            raise ValueError("returns_to_go must be [B,T]")
+        if timesteps.shape[:2] != (B, T):
+            raise ValueError("timesteps must be [B,T]")
+        if T > cfg.context_len:
+            raise ValueError(f"seq_len={T} exceeds context_len={cfg.context_len}")
+        h = self.embed(states, actions, returns_to_go, timesteps)
+        mask3 = None
+        if attention_mask is not None:
+            if attention_mask.shape != (B, T):
+                raise ValueError(f"attention_mask must be [B,T], got {tuple(attention_mask.shape)}")
+            mask3 = torch.stack((attention_mask,) * 3, dim=2).reshape(B, 3 * T).to(h.dtype)
+        return self.run_layers(h, mask3, past_key_values, use_cache)
+
+    def run_layers(self, h, mask3=None, past_key_values=None, use_cache=False):
+        """Layers + final norm on [B, 3T, H] token states (:435-461)."""
+        cfg = self.config
+        B, S = h.shape[0], h.shape[1]
+        if hasattr(past_key_values, "layers") and not isinstance(past_key_values, PagedKVCache):
+            past_key_values = None  # the reference drops HF Cache objects (:436-437)
+        if isinstance(past_key_values, PagedKVCache):
+            past_key_values = past_key_values.as_past()
+        past = past_key_values or [None] * len(self.layers)
+        start = past[0][0].shape[2] if past[0] is not None else 0
+        if start + S > self.freqs_cos.shape[0]:
+            raise ValueError(f"positions {start}..{start + S - 1} exceed max_position_embeddings "
+                             f"{self.freqs_cos.shape[0]}")
+        pe = (self.freqs_cos[start:start + S], self.freqs_sin[start:start + S])
+        presents = []
+        for layer, pkv in zip(self.layers, past):
+            h, pr = layer(h, pe, past_key_value=pkv, use_cache=use_cache, attention_mask=mask3)
+            presents.append(pr)
+        h = self.norm(h)
+        if S % 3 == 0:
+            h = h.view(B, S // 3, 3, cfg.hidden_size)
+        return h, presents
+
+
+@dataclass
+class DTOutput:
+    loss: Optional[Tensor] = None
+    action_logits: Optional[Tensor] = None
+    value_preds: Optional[Tensor] = None
+    last_hidden_state: Optional[Tensor] = None
+    past_key_values: Optional[List] = None
+
+
+class MarioDT(nn.Module):
+    """MarioDecisionTransformer (:468-548) with FastDTAttention."""
+
+    def __init__(self, cfg: DTConfig):
+        super().__init__()
+        self.config = cfg
+        self.model = DTBackbone(cfg)
+        self.action_head = nn.Linear(cfg.hidden_size, cfg.act_dim, bias=False)
+        self.value_head = nn.Linear(cfg.hidden_size, 1)
+
+    def heads(self, hidden: Tensor) -> Tuple[Tensor, Tensor]:
+        st = hidden[:, :, 1, :]  # state tokens predict the action (:505-507)
+        return self.action_head(st), self.value_head(st).squeeze(-1)
+
+    def forward(self, states, actions, returns_to_go, timesteps, attention_mask=None, action_targets=None,
+                past_key_values=None, use_cache=False, **kw) -> DTOutput:
+        hidden, presents = self.model(states, actions, returns_to_go, timesteps, attention_mask,
+                                      past_key_values, use_cache)
+        logits, values = self.heads(hidden)
+        targets = action_targets if action_targets is not None else actions
+        loss = F.cross_entropy(logits.reshape(-1, self.config.act_dim).float(), targets.reshape(-1).long(),
+                               ignore_index=-100, label_smoothing=self.config.label_smoothing)
+        return DTOutput(loss, logits, values, hidden, presents)
+
+    @torch.no_grad()
+    def act(self, states, actions, returns_to_go, timesteps, attention_mask=None, deterministic=False):
+        """Next action from the last state token; re-prefills the context (:526-548)."""
+        out = self.forward(states, actions, returns_to_go, timesteps, attention_mask, use_cache=False)
+        logits = out.action_logits[:, -1, :]
+        if deterministic:
+            return torch.argmax(logits, dim=-1)
+        return torch.distributions.Categorical(logits=logits.float()).sample()

@@ -1,0 +1,151 @@
+"""Drop-in parity on the GPU against outputs of the reference itself.
+
+The golden fixtures were produced by the unmodified reference modules
+(tests/golden/make_golden.py).  Here the same seeded weights are loaded into
+FastDTAttention / MarioDT and run through the CUDA kernels.
+
+Tolerances (stated per test): attention-module outputs in bf16 are compared
+with 1.5e-2 abs + 1e-2 rel (bf16 rounding of Q/K/V, P and O).  DT action
+logits of an fp32 model whose attention runs on the bf16 tensor-core kernels
+carry the bf16 rounding of two attention layers: 1e-2 max-abs with identical
+argmax.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.dt_ref import dt_param_shapes
+from oracle.seeded import seeded_normal, seeded_state_dict, seeded_uniform, seeded_uniform_int
+
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+def load(name):
+    return dict(np.load(GOLD / f"{name}.npz"))
+
+
+class _Cfg:
+    def __init__(self, hidden, nh, nkv):
+        self.hidden_size, self.num_attention_heads, self.num_key_value_heads = hidden, nh, nkv
+        self.dropout, self.flash_attn = 0.0, True
+
+
+def _attn(g, dtype):
+    from rl_for_mario_b200.attention import FastDTAttention
+
+    H, nh, nkv = int(g["hidden"]), int(g["nh"]), int(g["nkv"])
+    D = H // nh
+    m = FastDTAttention(_Cfg(H, nh, nkv))
+    shapes = [(n, tuple(p.shape)) for n, p in m.named_parameters()]
+    m.load_state_dict(seeded_state_dict(shapes, int(g["seed"])))
+    return m.cuda().to(dtype).eval(), D
+
+
+def _close(out, ref, atol, rtol):
+    err = (out - ref).abs()
+    worst = (err - (atol + rtol * ref.abs())).max().item()
+    assert worst <= 0, f"max err {err.max().item():.3e}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["attn_d32_mask", "attn_d32_nomask", "attn_d32_decmask", "attn_d64_mask",
+                                  "attn_d32_long"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_attention_module_matches_reference_outputs(name, dtype):
+    from oracle import precompute_freqs_cis
+
+    g = load(name)
+    m, D = _attn(g, dtype)
+    H, B, S, seed = int(g["hidden"]), int(g["B"]), int(g["S"]), int(g["seed"])
+    x = seeded_normal((B, S, H), seed, name + ":x").cuda().to(dtype)
+    cos, sin = (t.cuda() for t in precompute_freqs_cis(D, S + 16))
+    mask = None
+    if "pad_len" in g:
+        mask = (torch.arange(S)[None] >= torch.from_numpy(g["pad_len"]).long()[:, None]).float().cuda()
+    with torch.no_grad():
+        y, past = m(x, (cos[:S], sin[:S]), use_cache=True, attention_mask=mask)
+    _close(y.float().cpu(), torch.from_numpy(g["out"]), 1.5e-2, 1e-2)
+    _close(past[0].float().cpu(), torch.from_numpy(g["past_k"]), 1.5e-2, 1e-2)
+    _close(past[1].float().cpu(), torch.from_numpy(g["past_v"]), 1.5e-2, 1e-2)
+    if "dec_out" in g:
+        n_new = g["dec_out"].shape[1]
+        xn = seeded_normal((B, n_new, H), seed, name + ":xn").cuda().to(dtype)
+        dmask = None
+        if int(g["decode_mask"]):
+            dmask = (torch.arange(S + n_new)[None] >= torch.from_numpy(g["pad_len"]).long()[:, None]).float().cuda()
+        with torch.no_grad():
+            yd, pd = m(xn, (cos[S:S + n_new], sin[S:S + n_new]), past_key_value=past, use_cache=True,
+                       attention_mask=dmask)
+        _close(yd.float().cpu(), torch.from_numpy(g["dec_out"]), 1.5e-2, 1e-2)
+        _close(pd[0].float().cpu(), torch.from_numpy(g["dec_k"]), 1.5e-2, 1e-2)
+        _close(pd[1].float().cpu(), torch.from_numpy(g["dec_v"]), 1.5e-2, 1e-2)
+
+
+def _dt(dtype):
+    from rl_for_mario_b200.dt_model import DTConfig, MarioDT
+
+    g = load("dt_small")
+    cfgd = {k[4:]: (tuple(v.tolist()) if v.ndim else v.item()) for k, v in g.items() if k.startswith("cfg_")}
+    cfg = DTConfig(**cfgd, dropout=0.0)
+    model = MarioDT(cfg)
+    model.load_state_dict(seeded_state_dict(dt_param_shapes(cfgd), int(g["seed"])), strict=True)
+    model = model.cuda().to(dtype).eval()
+    seed, B = int(g["seed"]), int(g["B"])
+    T = int(g["T"]) + int(g["decode_steps"])
+    states = seeded_uniform_int((B, T, *cfg.state_shape), 0, 256, seed, "dt_small:states").to(torch.uint8).cuda()
+    actions = torch.from_numpy(g["actions"]).cuda()
+    rtg = torch.from_numpy(g["rtg"]).cuda()
+    ts = torch.from_numpy(g["timesteps"]).cuda()
+    return g, model, states, actions, rtg, ts
+
+
+@pytest.mark.gpu
+def test_dt_logits_match_reference_fp32_model_bf16_kernels():
+    """fp32 weights/activations, attention on the bf16 tensor-core kernels: logits within 1e-2."""
+    g, model, states, actions, rtg, ts = _dt(torch.float32)
+    T = int(g["T"])
+    mask = (torch.arange(T)[None] >= torch.from_numpy(g["pad_steps"]).long()[:, None]).long().cuda()
+    with torch.no_grad():
+        out = model(states[:, :T], actions[:, :T], rtg[:, :T], ts[:, :T], attention_mask=mask)
+    ref = torch.from_numpy(g["logits"])
+    err = (out.action_logits.float().cpu() - ref).abs().max().item()
+    assert err < 1e-2, f"logits max abs err {err:.3e}"
+    assert torch.equal(out.action_logits.argmax(-1).cpu(), ref.argmax(-1))
+    np.testing.assert_allclose(out.value_preds.float().cpu().numpy(), g["values"], atol=1e-2)
+
+
+@pytest.mark.gpu
+def test_dt_cached_step_matches_reference():
+    """Prefill 7 timesteps with use_cache into a paged cache, then one cached 3-token step."""
+    from rl_for_mario_b200.cache import PagedKVCache
+
+    g, model, states, actions, rtg, ts = _dt(torch.float32)
+    T = int(g["T"])
+    cfg = model.config
+    cache = PagedKVCache(cfg.num_hidden_layers, states.shape[0], cfg.num_key_value_heads,
+                         cfg.hidden_size // cfg.num_attention_heads, max_len=3 * cfg.context_len, page_size=16,
+                         dtype=torch.bfloat16)
+    with torch.no_grad():
+        # Prefill through the decode path into the paged cache (L = 0 -> 3T tokens).
+        o0 = model(states[:, :T], actions[:, :T], rtg[:, :T], ts[:, :T], past_key_values=cache, use_cache=True)
+        o1 = model(states[:, T:], actions[:, T:], rtg[:, T:], ts[:, T:], past_key_values=cache, use_cache=True)
+    e0 = (o0.action_logits.float().cpu() - torch.from_numpy(g["nomask_logits"])).abs().max().item()
+    e1 = (o1.action_logits.float().cpu() - torch.from_numpy(g["dec_logits"])).abs().max().item()
+    assert e0 < 1e-2 and e1 < 1e-2, (e0, e1)
+    assert torch.equal(o1.action_logits.argmax(-1).cpu(), torch.from_numpy(g["dec_logits"]).argmax(-1))
+    assert cache.length == 3 * (T + 1)
+
+
+@pytest.mark.gpu
+def test_dt_bf16_model_argmax_agreement():
+    """Whole model in bf16: logits within 5e-2 of the fp32 reference and identical argmax."""
+    g, model, states, actions, rtg, ts = _dt(torch.bfloat16)
+    T = int(g["T"])
+    mask = (torch.arange(T)[None] >= torch.from_numpy(g["pad_steps"]).long()[:, None]).long().cuda()
+    with torch.no_grad():
+        out = model(states[:, :T], actions[:, :T], rtg[:, :T], ts[:, :T], attention_mask=mask)
+    ref = torch.from_numpy(g["logits"])
+    err = (out.action_logits.float().cpu() - ref).abs().max().item()
+    assert err < 5e-2, f"bf16 model logits max abs err {err:.3e}"
