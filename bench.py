@@ -312,6 +312,10 @@ def run_ours(args):
                      "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                      "algorithmic_bytes_per_launch": byts, "peak_source": peaks["source"]},
     }
+    if not args.no_decode:
+        if world == 1:
+            line["decode"] = bench_decode_cfg3(dev, peaks)
+        line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
@@ -322,6 +326,152 @@ def run_ours(args):
         pg.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- decode workloads
+DECODE_CFG = dict(envs=16384, prefix=189, steps=21, hidden=256, layers=4, q_heads=8, kv_heads=2, head_dim=32)
+ROLLOUT_CFG = dict(envs_per_gpu=8192, steps=64, hidden=256, layers=4, q_heads=8, kv_heads=2, context_len=64)
+
+
+def _decode_kernel_bytes(B, L, Sn, Hq, Hkv, D):
+    """Algorithmic bytes of one dt_attn_decode launch: read the L cached K/V rows,
+    read q / k_new / v_new, write o and the appended K/V rows (bf16)."""
+    return 2 * (2 * B * Hkv * L * D + B * Sn * (2 * Hq + 4 * Hkv) * D)
+
+
+def bench_decode_cfg3(dev, peaks):
+    """16,384 environments, cache prefilled with 189 tokens, 21 cached steps of 3 tokens."""
+    from rl_for_mario_b200 import kernels
+    from rl_for_mario_b200.cache import PagedKVCache
+    from rl_for_mario_b200.dt_model import DTConfig, MarioDT
+
+    C = DECODE_CFG
+    torch.manual_seed(2)
+    cfg = DTConfig(hidden_size=C["hidden"], num_hidden_layers=C["layers"], num_attention_heads=C["q_heads"],
+                   num_key_value_heads=C["kv_heads"], context_len=(C["prefix"] + 3 * C["steps"]) // 3, dropout=0.0)
+    model = MarioDT(cfg).to(dev, torch.bfloat16).eval()
+    B, H = C["envs"], C["hidden"]
+    max_len = C["prefix"] + 3 * C["steps"]
+    cache = PagedKVCache(C["layers"], B, C["kv_heads"], C["head_dim"], max_len, page_size=64, dtype=torch.bfloat16,
+                         device=dev)
+    g = torch.Generator(device=dev).manual_seed(3)
+    steps_h = torch.randn(C["steps"], B, 3, H, device=dev, generator=g).to(torch.bfloat16)
+    bb = model.model
+
+    def prefill():
+        cache.reset()
+        with torch.no_grad():
+            hp = torch.randn(B, C["prefix"], H, device=dev, generator=g).to(torch.bfloat16)
+            bb.run_layers(hp, None, cache, use_cache=True, flat=True)
+            del hp
+
+    def run_steps():
+        acts = None
+        with torch.no_grad():
+            for t in range(C["steps"]):
+                h, _ = bb.run_layers(steps_h[t], None, cache, use_cache=True, flat=True)
+                acts = model.action_head(h[:, 1]).argmax(-1)  # state token of (R, s, a)
+        return acts
+
+    prefill()
+    run_steps()  # warm-up
+    times = []
+    for _ in range(2):
+        prefill()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run_steps()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    ms = min(times)
+    # The decode kernel alone at the mid-point length (no advance: same slots rewritten).
+    lay = cache[0]
+    L_mid = C["prefix"] + 3 * (C["steps"] // 2)
+    saved = lay.length
+    lay.seq_lens.fill_(L_mid)
+    lay.length = L_mid
+    q = torch.randn(B, 3, C["q_heads"], C["head_dim"], device=dev, generator=g).to(torch.bfloat16)
+    kn = torch.randn(B, 3, C["kv_heads"], C["head_dim"], device=dev, generator=g).to(torch.bfloat16)
+    cos, sin = bb.freqs_cos[L_mid:L_mid + 3], bb.freqs_sin[L_mid:L_mid + 3]
+    out = torch.empty_like(q)
+    for _ in range(3):
+        kernels.attn_decode(q, kn, kn, lay, cos, sin, out=out)
+    torch.cuda.synchronize()
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 20
+    k0.record()
+    for _ in range(n):
+        kernels.attn_decode(q, kn, kn, lay, cos, sin, out=out)
+    k1.record()
+    torch.cuda.synchronize()
+    kms = k0.elapsed_time(k1) / n
+    lay.seq_lens.fill_(saved)
+    lay.length = saved
+    kb = _decode_kernel_bytes(B, L_mid, 3, C["q_heads"], C["kv_heads"], C["head_dim"])
+    ach = kb / (kms * 1e-3) / 1e9
+    res = {
+        "metric": "rollout decode env-steps/s (cached, 3 tokens per step)", "unit": "env-steps/s",
+        "value": B * C["steps"] / (ms * 1e-3), "ms_total": ms,
+        "config": {"workload": "16384 envs, 189-token prefix, 21 steps x 3 tokens -> 252, 4 layers, hidden 256, "
+                               "8/2 heads, head_dim 32, bf16, hidden inputs N(0,1), argmax of the 7-way head"},
+        "kernel_roofline": {"kernel": "dt_decode_kernel", "bound": "hbm", "kv_len": L_mid + 3, "ms": kms,
+                            "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
+                            "algorithmic_bytes_per_launch": kb},
+    }
+    del cache, model, steps_h
+    torch.cuda.empty_cache()
+    return res
+
+
+def bench_rollout_cfg5(dev, world, rank, pg):
+    """8,192 environments per GPU, 64 cached steps, CNN on synthetic frames, all-gather of logits."""
+    from rl_for_mario_b200.dt_model import DTConfig, MarioDT
+    from rl_for_mario_b200.rollout import DTRollout
+
+    C = ROLLOUT_CFG
+    torch.manual_seed(4)  # identical replicated weights on every rank
+    cfg = DTConfig(hidden_size=C["hidden"], num_hidden_layers=C["layers"], num_attention_heads=C["q_heads"],
+                   num_key_value_heads=C["kv_heads"], context_len=C["context_len"], dropout=0.0)
+    model = MarioDT(cfg).to(dev, torch.bfloat16).eval()
+    b = C["envs_per_gpu"]
+    B = b * world
+    ro = DTRollout(model, num_envs=B, max_steps=C["steps"], page_size=64, device=dev)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    frames = torch.randint(0, 256, (4, b, 4, 84, 84), device=dev, generator=g, dtype=torch.uint8)
+    rtg = torch.rand(C["steps"], b, device=dev, generator=g) * 3000
+    ts0 = torch.randint(0, 4000 - C["steps"], (b,), device=dev, generator=g)
+
+    def run():
+        ro.reset()
+        a = None
+        for t in range(C["steps"]):
+            a, _ = ro.step(frames[t % 4], rtg[t], ts0 + t)
+        return a
+
+    run()  # warm-up
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if pg:
+        t = torch.tensor([ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    res = {"metric": "sharded rollout env-steps/s (CNN + 4 layers + cached attention + all-gather)",
+           "unit": "env-steps/s", "value": B * C["steps"] / (ms * 1e-3), "ms_total": ms, "n_gpus": world,
+           "scaling": "weak",
+           "config": {"workload": f"{b} envs per GPU ({B} total), 64 steps, window 192, repo-default DT bf16, "
+                                  "synthetic uint8 frames, all_gather of [B/N, 7] logits per step"}}
+    del ro, model, frames
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -329,6 +479,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode / rollout sub-benchmarks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
     args = ap.parse_args()

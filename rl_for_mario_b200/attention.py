@@ -92,7 +92,21 @@ class FastDTAttention(nn.Module):
         xv = self.v_proj(x).view(bsz, seq_len, self.n_local_kv_heads, self.head_dim).to(kd)
         cos, sin = position_embeddings
 
-        if self.flash and seq_len > 1 and past_key_value is None:
+        if (isinstance(past_key_value, LayerKV) and past_key_value.length == 0 and seq_len > 1 and self.flash
+                and attention_mask is None):
+            # First fill of a paged cache: prefill kernel, then write the rotated
+            # keys and values into the pages (same result as the cached branch
+            # with an empty cache, :225-245).
+            layer = past_key_value
+            if layer.k_pages.dtype != kd:
+                raise TypeError(f"cache dtype {layer.k_pages.dtype} differs from compute dtype {kd}")
+            if seq_len > layer.capacity:
+                raise ValueError(f"cache full: {seq_len} > capacity {layer.capacity}")
+            out = kernels.attn_prefill(xq, xk, xv, cos, sin, None)
+            kernels.kv_write(xk, xv, layer, cos, sin)
+            layer.advance(seq_len)
+            past_kv = layer if use_cache else None
+        elif self.flash and seq_len > 1 and past_key_value is None:
             out = kernels.attn_prefill(xq, xk, xv, cos, sin, self._pad_len(attention_mask, seq_len))
             past_kv = None
             if use_cache:

@@ -127,8 +127,9 @@ class MarioStateEncoder(nn.Module):
             raise ValueError(f"states must be [B,T,C,H,W], got {tuple(states.shape)}")
         B, T, C, H, W = states.shape
         x = states.to(self.cnn[0].weight.dtype)
-        if x.max() > 1.0:
-            x = x / 255.0
+        # The reference rescales when max > 1 (:338); the same test is done on
+        # the device here, so no host synchronisation per call.
+        x = torch.where(x.max() > 1.0, x / 255.0, x)
         return self.cnn(x.reshape(B * T, C, H, W)).reshape(B, T, -1)
 
 
@@ -187,8 +188,9 @@ class DTBackbone(nn.Module):
             mask3 = torch.stack((attention_mask,) * 3, dim=2).reshape(B, 3 * T).to(h.dtype)
         return self.run_layers(h, mask3, past_key_values, use_cache)
 
-    def run_layers(self, h, mask3=None, past_key_values=None, use_cache=False):
-        """Layers + final norm on [B, 3T, H] token states (:435-461)."""
+    def run_layers(self, h, mask3=None, past_key_values=None, use_cache=False, flat: bool = False):
+        """Layers + final norm on [B, S, H] token states (:435-461); returns [B, S/3, 3, H]
+        (the reference's view) unless ``flat``."""
         cfg = self.config
         B, S = h.shape[0], h.shape[1]
         if hasattr(past_key_values, "layers") and not isinstance(past_key_values, PagedKVCache):
@@ -206,7 +208,7 @@ class DTBackbone(nn.Module):
             h, pr = layer(h, pe, past_key_value=pkv, use_cache=use_cache, attention_mask=mask3)
             presents.append(pr)
         h = self.norm(h)
-        if S % 3 == 0:
+        if not flat:
             h = h.view(B, S // 3, 3, cfg.hidden_size)
         return h, presents
 
