@@ -204,7 +204,7 @@ def run_reference(args):
                          "sample": samples[0] if samples else ""},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     if pg:
         pg.destroy_process_group()
 
@@ -321,7 +321,7 @@ def run_ours(args):
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
                                 "sample": info["sample"]}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     if pg:
         pg.destroy_process_group()
 
@@ -472,7 +472,22 @@ def bench_rollout_cfg5(dev, world, rank, pg):
     return res
 
 
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Writes the result line to the process's real stdout (library banners go to stderr)."""
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _JSON_OUT
+    # Keep stdout for the one JSON line: anything a library prints on fd 1
+    # (e.g. a collective library's version banner) is sent to stderr instead.
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
