@@ -17,9 +17,11 @@ tensors (functional: a new, longer tuple is returned, like torch.cat) or a
 Masks: ``attention_mask`` [B, S] (prefill) or [B, kv_len] (decode), 1 =
 valid, is taken as left padding (the layout scripts/mario/dt_offline_dataset.py
 :228-235 produces); set ``check_masks=True`` to verify that on the host.
-Numerics: the kernels compute in bf16 (or fp16) with fp32 softmax and
-accumulation; an fp32 module casts Q/K/V to ``compute_dtype`` for the kernels
-and casts the result back.  There is no CPU path: CPU inputs raise.
+Numerics: bf16 / fp16 inputs run on the tensor-core kernels (fp32 softmax and
+accumulation); fp32 inputs run on the fp32 kernels (CUDA cores, fp32
+throughout) unless ``compute_dtype`` selects bf16/fp16 tensor-core compute, in
+which case Q/K/V are cast for the kernels and the result is cast back.  There
+is no CPU path: CPU inputs raise.
 """
 from __future__ import annotations
 
@@ -35,7 +37,7 @@ Tensor = torch.Tensor
 
 
 class FastDTAttention(nn.Module):
-    def __init__(self, config, compute_dtype: torch.dtype = torch.bfloat16, check_masks: bool = False):
+    def __init__(self, config, compute_dtype: Optional[torch.dtype] = None, check_masks: bool = False):
         super().__init__()
         self.num_key_value_heads = (config.num_attention_heads if config.num_key_value_heads is None
                                     else config.num_key_value_heads)
@@ -66,7 +68,10 @@ class FastDTAttention(nn.Module):
 
     # ------------------------------------------------------------------ helpers
     def _kernel_dtype(self, x: Tensor) -> torch.dtype:
-        return x.dtype if x.dtype in (torch.bfloat16, torch.float16) else self.compute_dtype
+        kd = self.compute_dtype or x.dtype
+        if kd not in (torch.bfloat16, torch.float16, torch.float32):
+            raise TypeError(f"unsupported compute dtype {kd}")
+        return kd
 
     def _pad_len(self, mask: Optional[Tensor], length: int) -> Optional[Tensor]:
         if mask is None:

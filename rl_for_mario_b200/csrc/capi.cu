@@ -138,22 +138,25 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
     return fail(DT_ERR_INVALID, "dt_attn_prefill: num_attention_heads (%d) must be divisible by "
                                 "num_key_value_heads (%d)", Hq, Hkv);
   if (D != 32 && D != 64) return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: head_dim %d not in {32, 64}", D);
-  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
-    return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: dtype %d not supported by the tensor-core path", dtype);
+  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16 && dtype != DT_DTYPE_FP32)
+    return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: dtype %d not supported", dtype);
   const int R = Hq / Hkv;
   if (R > 128) return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: group size %d > 128", R);
   if ((long long)B * Hkv > 0x7fffffffLL) return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: B*Hkv too large");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+  const bool f32 = dtype == DT_DTYPE_FP32;
+  if (!f32 && (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)))
     return fail(DT_ERR_INVALID, "dt_attn_prefill: q/k/v/o must be 16-byte aligned");
   const int64_t strides[12] = {q_sb, q_ss, q_sh, k_sb, k_ss, k_sh, v_sb, v_ss, v_sh, o_sb, o_ss, o_sh};
   for (int i = 0; i < 12; ++i)
-    if (strides[i] <= 0 || strides[i] % 8 != 0)
+    if (strides[i] <= 0 || (!f32 && strides[i] % 8 != 0))
       return fail(DT_ERR_INVALID, "dt_attn_prefill: stride #%d (%lld) must be a positive multiple of 8", i,
                   (long long)strides[i]);
   if (apply_rope) {
     if (!cos_tab || !sin_tab) return fail(DT_ERR_INVALID, "dt_attn_prefill: null cos/sin with apply_rope");
     if (cos_rows < S) return fail(DT_ERR_INVALID, "dt_attn_prefill: cos/sin have %d rows < S=%d", cos_rows, S);
-    if (!aligned16(cos_tab) || !aligned16(sin_tab) || cos_stride < D || cos_stride % 4 != 0)
+    if (!f32 && (!aligned16(cos_tab) || !aligned16(sin_tab) || cos_stride % 4 != 0))
+      return fail(DT_ERR_INVALID, "dt_attn_prefill: cos/sin must be 16-byte aligned with row stride %% 4 == 0");
+    if (cos_stride < D)
       return fail(DT_ERR_INVALID, "dt_attn_prefill: cos/sin must be 16-byte aligned with row stride >= D, %% 4");
   }
   int dev = 0;
@@ -164,6 +167,19 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
     return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: needs an sm_100 GPU (device %d is cc %d.x)", dev,
                 g_cc_major[dev]);
 
+  const float sc0 = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
+  if (f32) {
+    dtk::PrefillF32Params fp;
+    fp.q = static_cast<const float*>(q); fp.k = static_cast<const float*>(k); fp.v = static_cast<const float*>(v);
+    fp.o = static_cast<float*>(o); fp.cos = cos_tab; fp.sin = sin_tab; fp.pad_len = pad_len;
+    fp.q_sb = q_sb; fp.q_ss = q_ss; fp.q_sh = q_sh; fp.k_sb = k_sb; fp.k_ss = k_ss; fp.k_sh = k_sh;
+    fp.v_sb = v_sb; fp.v_ss = v_ss; fp.v_sh = v_sh; fp.o_sb = o_sb; fp.o_ss = o_ss; fp.o_sh = o_sh;
+    fp.cs_stride = (int)cos_stride; fp.rope = apply_rope ? 1 : 0; fp.S = S; fp.Hkv = Hkv; fp.R = R;
+    fp.scale_log2 = sc0 * 1.4426950408889634f;
+    cudaError_t e = dtk::launch_prefill_f32(fp, D, B, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "dt_attn_prefill (fp32) launch");
+    return DT_OK;
+  }
   const bool bf16 = dtype == DT_DTYPE_BF16;
   const int PT = 128 / R;
   // Short sequences with head_dim 32 (the DT's 192-token context) use the
@@ -216,7 +232,7 @@ int check_cache(const char* fn, const void* k_pages, const void* v_pages, int nu
   if (num_pages < 1 || page_size < 1 || max_pages < 1)
     return fail(DT_ERR_INVALID, "%s: num_pages, page_size, max_pages must be positive", fn);
   if (D != 32 && D != 64) return fail(DT_ERR_UNSUPPORTED, "%s: head_dim %d not in {32, 64}", fn, D);
-  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
+  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16 && dtype != DT_DTYPE_FP32)
     return fail(DT_ERR_UNSUPPORTED, "%s: dtype %d not supported", fn, dtype);
   if (!aligned16(k_pages) || !aligned16(v_pages)) return fail(DT_ERR_INVALID, "%s: cache pages must be 16-byte aligned", fn);
   return DT_OK;
@@ -261,7 +277,9 @@ int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o,
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   p.scale_log2 = sc * 1.4426950408889634f;
   if ((long long)B * Hkv > 0x7fffffffLL) return fail(DT_ERR_UNSUPPORTED, "%s: B*Hkv too large", fn);
-  cudaError_t e = dtk::launch_decode_sm100(p, D, dtype == DT_DTYPE_BF16, B * Hkv, static_cast<cudaStream_t>(stream));
+  cudaError_t e = dtype == DT_DTYPE_FP32
+                      ? dtk::launch_decode_f32(p, D, B, static_cast<cudaStream_t>(stream))
+                      : dtk::launch_decode_sm100(p, D, dtype == DT_DTYPE_BF16, B * Hkv, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dt_attn_decode launch");
   return DT_OK;
 }
@@ -289,7 +307,7 @@ int dt_kv_write(const void* k, const void* v, void* k_pages, void* v_pages, int 
   p.k_sb = k_sb; p.k_ss = k_ss; p.k_sh = k_sh; p.v_sb = v_sb; p.v_ss = v_ss; p.v_sh = v_sh;
   p.cs_stride = (int)cos_stride; p.cos_rows = cos_rows; p.rope = apply_rope ? 1 : 0; p.rope_abs = rope_abs ? 1 : 0;
   p.S = S; p.Hkv = Hkv; p.page_size = page_size; p.max_pages = max_pages; p.num_pages = num_pages;
-  cudaError_t e = dtk::launch_kv_write_sm100(p, D, dtype == DT_DTYPE_BF16, B, static_cast<cudaStream_t>(stream));
+  cudaError_t e = dtk::launch_kv_write_sm100(p, D, dtype, B, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dt_kv_write launch");
   return DT_OK;
 }

@@ -66,7 +66,26 @@ struct KvWriteParams {
   int S, Hkv, page_size, max_pages, num_pages;
 };
 
-cudaError_t launch_kv_write_sm100(const KvWriteParams& prm, int D, bool bf16, int B, cudaStream_t stream);
+// float32 prefill (CUDA cores).
+struct PrefillF32Params {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* o;
+  const float* cos;
+  const float* sin;
+  const int32_t* pad_len;
+  long long q_sb, q_ss, q_sh, k_sb, k_ss, k_sh, v_sb, v_ss, v_sh, o_sb, o_ss, o_sh;
+  int cs_stride, rope;
+  int S, Hkv, R;
+  float scale_log2;
+};
+
+cudaError_t launch_prefill_f32(const PrefillF32Params& prm, int D, int B, cudaStream_t stream);
+cudaError_t launch_decode_f32(const DecodeParams& prm, int D, int B, cudaStream_t stream);
+
+// dtype: 0 bf16, 1 fp16, 2 fp32
+cudaError_t launch_kv_write_sm100(const KvWriteParams& prm, int D, int dtype, int B, cudaStream_t stream);
 
 cudaError_t launch_decode_sm100(const DecodeParams& prm, int D, bool bf16, int grid, cudaStream_t stream);
 

@@ -10,9 +10,8 @@
 
 namespace dtk {
 
-template <int D, bool BF16>
+template <int D, typename T>
 __global__ void __launch_bounds__(256) dt_kv_write_kernel(const KvWriteParams p) {
-  using T = typename Elem<BF16>::T;
   const int b = blockIdx.x / p.Hkv;
   const int g = blockIdx.x - b * p.Hkv;
   const int start = p.start_pos ? p.start_pos[b] : 0;
@@ -56,19 +55,20 @@ __global__ void __launch_bounds__(256) dt_kv_write_kernel(const KvWriteParams p)
   }
 }
 
-cudaError_t launch_kv_write_sm100(const KvWriteParams& prm, int D, bool bf16, int B, cudaStream_t stream) {
+template <typename T>
+static void kv_write_d(const KvWriteParams& prm, int D, dim3 grid, cudaStream_t stream) {
+  if (D == 32) dt_kv_write_kernel<32, T><<<grid, 256, 0, stream>>>(prm);
+  else dt_kv_write_kernel<64, T><<<grid, 256, 0, stream>>>(prm);
+}
+
+cudaError_t launch_kv_write_sm100(const KvWriteParams& prm, int D, int dtype, int B, cudaStream_t stream) {
+  if (D != 32 && D != 64) return cudaErrorInvalidValue;
   const int per = prm.S * (D / 2);
   const int gy = (per + 255) / 256 < 64 ? (per + 255) / 256 : 64;
   dim3 grid(B * prm.Hkv, gy);
-  if (D == 32) {
-    if (bf16) dt_kv_write_kernel<32, true><<<grid, 256, 0, stream>>>(prm);
-    else dt_kv_write_kernel<32, false><<<grid, 256, 0, stream>>>(prm);
-  } else if (D == 64) {
-    if (bf16) dt_kv_write_kernel<64, true><<<grid, 256, 0, stream>>>(prm);
-    else dt_kv_write_kernel<64, false><<<grid, 256, 0, stream>>>(prm);
-  } else {
-    return cudaErrorInvalidValue;
-  }
+  if (dtype == 0) kv_write_d<__nv_bfloat16>(prm, D, grid, stream);
+  else if (dtype == 1) kv_write_d<__half>(prm, D, grid, stream);
+  else kv_write_d<float>(prm, D, grid, stream);
   return cudaGetLastError();
 }
 

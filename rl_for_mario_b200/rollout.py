@@ -69,8 +69,8 @@ class DTRollout:
         self.lo, self.hi = shard_range(num_envs, self.rank, self.world)
         self.local_envs = self.hi - self.lo
         self.device = device or next(model.parameters()).device
-        dtype = next(model.parameters()).dtype
-        kv_dtype = dtype if dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
+        attn0 = model.model.layers[0].self_attn
+        kv_dtype = attn0.compute_dtype or next(model.parameters()).dtype
         max_len = 3 * max_steps
         if max_len > cfg.max_position_embeddings:
             raise ValueError(f"{max_steps} steps need {max_len} positions > {cfg.max_position_embeddings}")

@@ -6,7 +6,8 @@ import torch
 from oracle import apply_rotary_pos_emb, attention_decode_ref, mask_from_pad_len, precompute_freqs_cis
 
 TOL = {torch.bfloat16: dict(atol=1.5e-2, rtol=1e-2, mean=2.5e-3),
-       torch.float16: dict(atol=4e-3, rtol=4e-3, mean=5e-4)}
+       torch.float16: dict(atol=4e-3, rtol=4e-3, mean=5e-4),
+       torch.float32: dict(atol=1e-5, rtol=1e-5, mean=1e-6)}
 
 CASES = [
     # B, L, Sn, Hq, Hkv, D, page, pads, dtype, permute
@@ -19,6 +20,9 @@ CASES = [
     (2, 50, 8, 8, 2, 32, 64, [0, 20], torch.bfloat16, False),
     (5, 253, 3, 8, 2, 32, 64, "random", torch.bfloat16, True),
     (2, 100, 3, 4, 4, 64, 64, None, torch.bfloat16, True),
+    (3, 24, 3, 8, 2, 32, 16, [0, 6, 15], torch.float32, True),
+    (2, 300, 3, 12, 4, 64, 64, [0, 120], torch.float32, False),
+    (2, 40, 130, 8, 2, 32, 64, [0, 50], torch.float32, False),
 ]
 
 
@@ -82,7 +86,8 @@ def test_decode_matches_oracle(case, rope_abs):
     layer.advance(Sn)
     dk, dv = layer.dense()
     torch.testing.assert_close(dv.float().cpu(), v_all, atol=0, rtol=0)
-    torch.testing.assert_close(dk.float().cpu(), k_all, atol=2e-2, rtol=1e-2)
+    ktol = 1e-5 if dtype == torch.float32 else 2e-2
+    torch.testing.assert_close(dk.float().cpu(), k_all, atol=ktol, rtol=ktol)
 
 
 @pytest.mark.gpu

@@ -12,7 +12,8 @@ import torch
 from oracle import attention_prefill_ref, mask_from_pad_len, precompute_freqs_cis
 
 TOL = {torch.bfloat16: dict(atol=1.5e-2, rtol=1e-2, mean=2.5e-3),
-       torch.float16: dict(atol=4e-3, rtol=4e-3, mean=5e-4)}
+       torch.float16: dict(atol=4e-3, rtol=4e-3, mean=5e-4),
+       torch.float32: dict(atol=1e-5, rtol=1e-5, mean=1e-6)}
 
 CASES = [
     # B, S, Hq, Hkv, D, pads, dtype
@@ -32,6 +33,10 @@ CASES = [
     (4, 190, 4, 2, 32, [0, 1, 100, 189], torch.float16),
     (300, 96, 8, 2, 32, "random", torch.bfloat16),
     (150, 192, 8, 2, 32, "random", torch.bfloat16),
+    (3, 24, 8, 2, 32, [0, 6, 15], torch.float32),
+    (4, 192, 8, 2, 32, [0, 96, 47, 191], torch.float32),
+    (2, 300, 12, 4, 64, [0, 100], torch.float32),
+    (2, 1, 8, 2, 32, None, torch.float32),
 ]
 
 
