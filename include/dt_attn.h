@@ -108,6 +108,19 @@ int dt_kv_write(const void* k, const void* v, void* k_pages, void* v_pages, int 
                 int dtype, void* stream);
 
 /*
+ * Fused RMSNorm + Q/K/V projection: y[m, :] = rsqrt(mean(x[m, :]^2) + eps) *
+ * (x[m, :] @ w_fused^T), with w_fused = [Wq; Wk; Wv] * diag(w_norm) ([N, K],
+ * K contiguous).  Replaces the block's input_layernorm (RMSNorm,
+ * model_decision_transformer.py:76-86, called at :296) followed by the
+ * attention's q_proj / k_proj / v_proj (:175-177); a row of y is the fused
+ * [q | k | v] the prefill / decode entry points take as strided views.
+ * x [M, K] (row stride x_row_stride), y [M, N] (row stride y_row_stride);
+ * bf16 or fp16; K, N and strides multiples of 8, 16-byte aligned pointers.
+ */
+int dt_rmsnorm_qkv(const void* x, int64_t x_row_stride, const void* w_fused, void* y, int64_t y_row_stride, int M,
+                   int K, int N, float eps, int dtype, void* stream);
+
+/*
  * Synchronises `stream`, then returns and clears the device status word that
  * the kernels of this library write when a bounded wait runs out or a
  * device-side check fails (0 = no error).  Used by tests and debugging.

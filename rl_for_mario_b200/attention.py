@@ -57,6 +57,11 @@ class FastDTAttention(nn.Module):
         self.resid_dropout = nn.Dropout(self.dropout)
         self.compute_dtype = compute_dtype
         self.check_masks = check_masks
+        # RMSNorm of the owning block, fused into the projections when set
+        # (held outside the module tree so the state_dict is unchanged).
+        object.__setattr__(self, "_fused_norm", None)
+        object.__setattr__(self, "_fused_w", None)
+        object.__setattr__(self, "_fused_key", None)
 
     @classmethod
     def from_reference(cls, ref_attn: nn.Module, config, **kw) -> "FastDTAttention":
@@ -85,16 +90,46 @@ class FastDTAttention(nn.Module):
                 raise ValueError("attention_mask is not a left-padding mask (zeros then ones per row)")
         return pad
 
+    def set_fused_norm(self, norm: Optional[nn.Module]) -> None:
+        """Fuses ``norm`` (an RMSNorm with ``weight`` and ``eps``) into the Q/K/V
+        projections: forward(..., raw_input=True) then takes the un-normalised x."""
+        object.__setattr__(self, "_fused_norm", norm)
+        object.__setattr__(self, "_fused_w", None)
+
+    def _fused_weight(self, dtype: torch.dtype) -> Tensor:
+        ps = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self._fused_norm.weight)
+        key = tuple((p.data_ptr(), p._version) for p in ps) + (dtype,)
+        if self._fused_w is None or self._fused_key != key:
+            w = kernels.fold_norm_weight(*ps, dtype=dtype)
+            object.__setattr__(self, "_fused_w", w)
+            object.__setattr__(self, "_fused_key", key)
+        return self._fused_w
+
+    def _project(self, x: Tensor, kd: torch.dtype, raw_input: bool):
+        bsz, seq_len, _ = x.shape
+        Hq, Hkv, D = self.n_local_heads, self.n_local_kv_heads, self.head_dim
+        if raw_input:
+            if self._fused_norm is None:
+                raise ValueError("raw_input=True needs set_fused_norm()")
+            if x.dtype in (torch.bfloat16, torch.float16) and kd == x.dtype:
+                qkv = kernels.rmsnorm_qkv(x, self._fused_weight(x.dtype), self._fused_norm.eps)
+                qkv = qkv.view(bsz, seq_len, Hq + 2 * Hkv, D)
+                return qkv[:, :, :Hq], qkv[:, :, Hq:Hq + Hkv], qkv[:, :, Hq + Hkv:]
+            x = self._fused_norm(x)  # fp32 models: exact RMSNorm, then the projections
+        xq = self.q_proj(x).view(bsz, seq_len, Hq, D).to(kd)
+        xk = self.k_proj(x).view(bsz, seq_len, Hkv, D).to(kd)
+        xv = self.v_proj(x).view(bsz, seq_len, Hkv, D).to(kd)
+        return xq, xk, xv
+
     # ------------------------------------------------------------------ forward
     def forward(self, x: Tensor, position_embeddings: Tuple[Tensor, Tensor],
-                past_key_value=None, use_cache: bool = False, attention_mask: Optional[Tensor] = None):
+                past_key_value=None, use_cache: bool = False, attention_mask: Optional[Tensor] = None,
+                raw_input: bool = False):
         if not x.is_cuda:
             raise ValueError("FastDTAttention runs on CUDA only (no CPU path)")
         bsz, seq_len, _ = x.shape
         kd = self._kernel_dtype(x)
-        xq = self.q_proj(x).view(bsz, seq_len, self.n_local_heads, self.head_dim).to(kd)
-        xk = self.k_proj(x).view(bsz, seq_len, self.n_local_kv_heads, self.head_dim).to(kd)
-        xv = self.v_proj(x).view(bsz, seq_len, self.n_local_kv_heads, self.head_dim).to(kd)
+        xq, xk, xv = self._project(x, kd, raw_input)
         cos, sin = position_embeddings
 
         if (isinstance(past_key_value, LayerKV) and past_key_value.length == 0 and seq_len > 1 and self.flash

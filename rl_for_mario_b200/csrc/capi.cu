@@ -313,3 +313,49 @@ int dt_kv_write(const void* k, const void* v, void* k_pages, void* v_pages, int 
 }
 
 }  // extern "C"
+
+namespace {
+int encode_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t rows, uint64_t row_stride_el,
+              uint32_t box_inner, uint32_t box_rows, const char* name) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride_el * 2};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DT_ERR_INVALID, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name, (int)r);
+  return DT_OK;
+}
+}  // namespace
+
+extern "C" int dt_rmsnorm_qkv(const void* x, int64_t x_row_stride, const void* w_fused, void* y,
+                              int64_t y_row_stride, int M, int K, int N, float eps, int dtype, void* stream) {
+  const char* fn = "dt_rmsnorm_qkv";
+  if (!x || !w_fused || !y) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
+  if (M < 1 || K < 1 || N < 1) return fail(DT_ERR_INVALID, "%s: sizes must be positive", fn);
+  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
+    return fail(DT_ERR_UNSUPPORTED, "%s: dtype %d not supported (bf16 / fp16)", fn, dtype);
+  if (K % 8 || N % 8 || x_row_stride % 8 || y_row_stride % 8 || x_row_stride < K || y_row_stride < N)
+    return fail(DT_ERR_INVALID, "%s: K, N and row strides must be multiples of 8 (strides >= K / N)", fn);
+  if (!aligned16(x) || !aligned16(w_fused) || !aligned16(y)) return fail(DT_ERR_INVALID, "%s: 16-byte alignment", fn);
+  if (!(eps > 0.f)) return fail(DT_ERR_INVALID, "%s: eps must be positive", fn);
+  int dev = 0;
+  int* status = nullptr;
+  int rc = device_setup(&dev, &status);
+  if (rc) return rc;
+  if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
+  const bool bf16 = dtype == DT_DTYPE_BF16;
+  const int ncta = dtk::rmsnorm_qkv_ncta(N);
+  const int nsub = ncta <= 256 ? ncta : ncta / 2;
+  CUtensorMap mx, mw;
+  if ((rc = encode_2d(&mx, x, bf16, (uint64_t)K, (uint64_t)M, (uint64_t)x_row_stride, 64, 128, "x"))) return rc;
+  if ((rc = encode_2d(&mw, w_fused, bf16, (uint64_t)K, (uint64_t)N, (uint64_t)K, 64, (uint32_t)nsub, "w"))) return rc;
+  dtk::RmsQkvParams p;
+  p.y = y; p.status = status; p.y_stride = y_row_stride; p.M = M; p.K = K; p.N = N; p.bf16 = bf16 ? 1 : 0; p.eps = eps;
+  cudaError_t e = dtk::launch_rmsnorm_qkv_sm100(mx, mw, p, ncta, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dt_rmsnorm_qkv launch");
+  return DT_OK;
+}

@@ -84,6 +84,19 @@ struct PrefillF32Params {
 cudaError_t launch_prefill_f32(const PrefillF32Params& prm, int D, int B, cudaStream_t stream);
 cudaError_t launch_decode_f32(const DecodeParams& prm, int D, int B, cudaStream_t stream);
 
+// Fused RMSNorm + QKV projection.
+struct RmsQkvParams {
+  void* y;            // [M, N] output rows, row stride y_stride elements
+  int* status;
+  long long y_stride;
+  int M, K, N, bf16;
+  float eps;
+};
+
+int rmsnorm_qkv_ncta(int N);
+cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w, const RmsQkvParams& p, int ncta,
+                                     cudaStream_t st);
+
 // dtype: 0 bf16, 1 fp16, 2 fp32
 cudaError_t launch_kv_write_sm100(const KvWriteParams& prm, int D, int dtype, int B, cudaStream_t stream);
 

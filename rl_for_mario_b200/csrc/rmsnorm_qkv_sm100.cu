@@ -1,0 +1,221 @@
+// Fused RMSNorm + Q/K/V projection, sm_100a.
+//
+// Replaces the block's input_layernorm feeding the attention's projections
+// (model/model_decision_transformer.py:76-86 RMSNorm, :296 call site,
+// :175-177 q_proj / k_proj / v_proj):
+//
+//   y = RMSNorm(x) = w_norm * x * rsqrt(mean(x^2) + eps)
+//   [q | k | v] = y @ [Wq; Wk; Wv]^T
+//               = rsqrt(mean(x^2) + eps) * (x @ W'^T),  W' = [Wq; Wk; Wv] * diag(w_norm)
+//
+// so the GEMM runs on the raw residual stream x and the per-row scale is
+// applied in the epilogue.  One CTA computes a 128-row x NCTA-column output
+// tile: warp 0 streams 64-wide K chunks of x and W' with TMA (128B swizzle),
+// warp 1 issues tcgen05.mma into TMEM (fp32), warps 2-5 accumulate each row's
+// sum of squares from the same shared-memory x tiles during the main loop
+// and run the epilogue (TMEM -> scale -> bf16 -> HBM).  Output row layout is
+// the fused [q | k | v] of the projections: a [tokens, (Hq + 2 Hkv) * D] row
+// is the [B, S, Hq + 2 Hkv, D] view the attention kernels take directly.
+#include "dt_common.cuh"
+#include "dt_internal.h"
+
+namespace dtk {
+
+namespace {
+
+constexpr int kGemmThreads = 192;
+constexpr int kKC = 64;  // K elements per pipeline stage (one 128-byte swizzle atom)
+
+template <int NCTA>
+struct GemmShape {
+  static constexpr int NSUB = NCTA <= 256 ? NCTA : NCTA / 2;  // columns per MMA instruction
+  static constexpr int NMMA = NCTA / NSUB;
+  static constexpr int A_BYTES = 128 * kKC * 2;
+  static constexpr int B_BYTES = NCTA * kKC * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int NSTAGE = (200 * 1024) / STAGE < 6 ? (200 * 1024) / STAGE : 6;
+  static constexpr int OFF_BAR = NSTAGE * STAGE;
+  static constexpr int SMEM = OFF_BAR + (2 * NSTAGE + 2) * 8 + 16 + 1024;
+  static constexpr uint32_t TMEM_COLS = NCTA <= 256 ? 256 : 512;
+  static_assert(NSUB % 16 == 0 && NSUB <= 256, "MMA N");
+};
+
+}  // namespace
+
+template <int NCTA>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    dt_rmsnorm_qkv_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                          const RmsQkvParams p) {
+  using SH = GemmShape<NCTA>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SH::OFF_BAR);
+  uint64_t* empty = full + SH::NSTAGE;
+  uint64_t* acc_full = empty + SH::NSTAGE;
+  uint64_t* drain = acc_full + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m0 = blockIdx.x * 128;
+  const int n0 = blockIdx.y * NCTA;
+  const int nk = (p.K + kKC - 1) / kKC;
+
+  if (tid == 0) {
+    for (int s = 0; s < SH::NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + 128);  // the MMA commit + the 128 sum-of-squares threads
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, SH::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmX);
+      prefetch_tmap(&tmW);
+      int issued = 0;
+      for (int kc = 0; kc < nk; ++kc) {
+        const int s = kc % SH::NSTAGE;
+        if (!mbar_wait(&empty[s], ((kc / SH::NSTAGE) & 1) ^ 1, abort_flag, p.status)) break;
+        uint8_t* st = smem + s * SH::STAGE;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)SH::STAGE);
+        tma_load_2d(st, &tmX, &full[s], kc * kKC, m0);
+#pragma unroll
+        for (int j = 0; j < SH::NMMA; ++j)
+          tma_load_2d(st + SH::A_BYTES + j * SH::NSUB * 128, &tmW, &full[s], kc * kKC, n0 + j * SH::NSUB);
+        ++issued;
+      }
+      if (*abort_flag) {
+        for (int s = 0; s < SH::NSTAGE; ++s) {
+          const int uses = issued / SH::NSTAGE + (s < issued % SH::NSTAGE ? 1 : 0);
+          if (uses > 0) mbar_wait(&full[s], (uses - 1) & 1, nullptr, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(p.bf16 != 0, 128, SH::NSUB, 0, 0);
+      for (int kc = 0; kc < nk; ++kc) {
+        const int s = kc % SH::NSTAGE;
+        if (!mbar_wait(&full[s], (kc / SH::NSTAGE) & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + s * SH::STAGE);
+        const uint64_t ad = umma_smem_desc(a, 16, 1024, kSw128);
+#pragma unroll
+        for (int j = 0; j < SH::NMMA; ++j) {
+          const uint64_t bd = umma_smem_desc(a + SH::A_BYTES + j * SH::NSUB * 128, 16, 1024, kSw128);
+#pragma unroll
+          for (int kk = 0; kk < kKC / 16; ++kk)  // 32 bytes per K step inside the 128-byte atom
+            umma_f16_ss(tmem + j * SH::NSUB, ad + 2 * kk, bd + 2 * kk, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(acc_full);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, nullptr);
+    }
+  } else {
+    // Warps 2-5: row sums of squares during the main loop, then the epilogue.
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;  // tile row = TMEM lane
+    float ss[4] = {0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    for (int kc = 0; kc < nk && ok; ++kc) {
+      const int s = kc % SH::NSTAGE;
+      if (!(ok = mbar_wait(&full[s], (kc / SH::NSTAGE) & 1, abort_flag, p.status))) break;
+      // The 128-byte row r of the swizzled x tile holds 64 elements in permuted
+      // 16-byte chunks; a sum of squares does not care about the order.
+      const uint4* row = reinterpret_cast<const uint4*>(smem + s * SH::STAGE + r * 128);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 u = row[c];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = p.bf16 ? Elem<true>::to_f2(w[i]) : Elem<false>::to_f2(w[i]);
+          ss[i] = fmaf(f.x, f.x, fmaf(f.y, f.y, ss[i]));
+        }
+      }
+      mbar_arrive(&empty[s]);
+    }
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(acc_full, 0, abort_flag, p.status));
+    if (ok) {
+      tc_fence_after();
+      const float rs = rsqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / (float)p.K + p.eps);
+      const int row_g = m0 + r;
+      for (int c = 0; c < NCTA; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + c, v);
+        if (row_g < p.M) {
+          uint8_t* yrow = reinterpret_cast<uint8_t*>(p.y) + ((size_t)row_g * p.y_stride + n0 + c) * 2;
+#pragma unroll
+          for (int c8 = 0; c8 < 32; c8 += 8) {
+            if (n0 + c + c8 + 8 > p.N) break;
+            uint4 o;
+            if (p.bf16) {
+              o.x = Elem<true>::from_f2(v[c8] * rs, v[c8 + 1] * rs);
+              o.y = Elem<true>::from_f2(v[c8 + 2] * rs, v[c8 + 3] * rs);
+              o.z = Elem<true>::from_f2(v[c8 + 4] * rs, v[c8 + 5] * rs);
+              o.w = Elem<true>::from_f2(v[c8 + 6] * rs, v[c8 + 7] * rs);
+            } else {
+              o.x = Elem<false>::from_f2(v[c8] * rs, v[c8 + 1] * rs);
+              o.y = Elem<false>::from_f2(v[c8 + 2] * rs, v[c8 + 3] * rs);
+              o.z = Elem<false>::from_f2(v[c8 + 4] * rs, v[c8 + 5] * rs);
+              o.w = Elem<false>::from_f2(v[c8 + 6] * rs, v[c8 + 7] * rs);
+            }
+            *reinterpret_cast<uint4*>(yrow + c8 * 2) = o;
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, SH::TMEM_COLS);
+  }
+}
+
+template <int NCTA>
+static cudaError_t launch_rq(const CUtensorMap& x, const CUtensorMap& w, const RmsQkvParams& p, cudaStream_t st) {
+  using SH = GemmShape<NCTA>;
+  auto k = dt_rmsnorm_qkv_kernel<NCTA>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SH::SMEM);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.M + 127) / 128, (p.N + NCTA - 1) / NCTA);
+  k<<<grid, kGemmThreads, SH::SMEM, st>>>(x, w, p);
+  return cudaGetLastError();
+}
+
+int rmsnorm_qkv_ncta(int N) {
+  // Widest accumulator that covers N in one pass when possible (x read once).
+  if (N <= 128) return 128;
+  if (N <= 256) return 256;
+  if (N <= 384) return 384;
+  return 512;
+}
+
+cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w, const RmsQkvParams& p, int ncta,
+                                     cudaStream_t st) {
+  switch (ncta) {
+    case 128: return launch_rq<128>(x, w, p, st);
+    case 256: return launch_rq<256>(x, w, p, st);
+    case 384: return launch_rq<384>(x, w, p, st);
+    case 512: return launch_rq<512>(x, w, p, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace dtk

@@ -102,11 +102,19 @@ class DTBlock(nn.Module):
         self.self_attn = FastDTAttention(cfg)
         self.mlp = FeedForward(cfg)
 
+    def fuse_norm(self, on: bool = True) -> None:
+        """Runs input_layernorm inside the attention's fused RMSNorm + QKV kernel."""
+        self.self_attn.set_fused_norm(self.input_layernorm if on else None)
+
     def forward(self, hidden_states, position_embeddings, past_key_value=None, use_cache=False,
                 attention_mask=None):
-        h, present = self.self_attn(self.input_layernorm(hidden_states), position_embeddings,
-                                    past_key_value=past_key_value, use_cache=use_cache,
-                                    attention_mask=attention_mask)
+        if self.self_attn._fused_norm is not None:
+            h, present = self.self_attn(hidden_states, position_embeddings, past_key_value=past_key_value,
+                                        use_cache=use_cache, attention_mask=attention_mask, raw_input=True)
+        else:
+            h, present = self.self_attn(self.input_layernorm(hidden_states), position_embeddings,
+                                        past_key_value=past_key_value, use_cache=use_cache,
+                                        attention_mask=attention_mask)
         h = h + hidden_states
         h = h + self.mlp(self.post_attention_layernorm(h))
         return h, present
@@ -231,6 +239,12 @@ class MarioDT(nn.Module):
         self.model = DTBackbone(cfg)
         self.action_head = nn.Linear(cfg.hidden_size, cfg.act_dim, bias=False)
         self.value_head = nn.Linear(cfg.hidden_size, 1)
+
+    def fuse_norms(self, on: bool = True) -> "MarioDT":
+        """Fuses every block's input RMSNorm into its Q/K/V projection kernel."""
+        for layer in self.model.layers:
+            layer.fuse_norm(on)
+        return self
 
     def heads(self, hidden: Tensor) -> Tuple[Tensor, Tensor]:
         st = hidden[:, :, 1, :]  # state tokens predict the action (:505-507)

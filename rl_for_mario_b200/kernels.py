@@ -181,3 +181,32 @@ def kv_write(k: Tensor, v: Tensor, layer, cos: Optional[Tensor], sin: Optional[T
         1 if rope_abs else 0, B, S, Hkv, D, k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
         v.stride(2), 1 if apply_rope else 0, _dtype_code(k), _stream_ptr(k.device))
     _lib.check("dt_kv_write", rc)
+
+
+def fold_norm_weight(w_q: Tensor, w_k: Tensor, w_v: Tensor, w_norm: Tensor, dtype: torch.dtype) -> Tensor:
+    """[Wq; Wk; Wv] * diag(w_norm) in ``dtype``: the weight of rmsnorm_qkv."""
+    w = torch.cat([w_q, w_k, w_v], dim=0).float() * w_norm.float()[None, :]
+    return w.to(dtype).contiguous()
+
+
+def rmsnorm_qkv(x: Tensor, w_fused: Tensor, eps: float, out: Optional[Tensor] = None) -> Tensor:
+    """y = RMSNorm(x) @ [Wq; Wk; Wv]^T with the norm weight folded into ``w_fused`` [N, K].
+
+    x [..., K] bf16/fp16 (last dim contiguous) -> y [..., N] (the fused q|k|v rows).
+    """
+    _require_cuda(x, w_fused, out)
+    K = x.shape[-1]
+    N = w_fused.shape[0]
+    if w_fused.shape[1] != K or w_fused.dtype != x.dtype or not w_fused.is_contiguous():
+        raise ValueError("w_fused must be a contiguous [N, K] tensor of x's dtype")
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+    o2 = out.view(-1, N)
+    rc = _lib.load().dt_rmsnorm_qkv(_ptr(x2), x2.stride(0), _ptr(w_fused), _ptr(o2), o2.stride(0), M, K, N,
+                                    float(eps), _dtype_code(x), _stream_ptr(x.device))
+    _lib.check("dt_rmsnorm_qkv", rc)
+    return out

@@ -1,0 +1,46 @@
+"""GPU parity of the fused RMSNorm + QKV projection kernel (dt_rmsnorm_qkv)."""
+import pytest
+import torch
+
+from oracle import rmsnorm_ref
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,N", [(1, 256, 384), (300, 256, 384), (4096, 256, 384), (777, 768, 1280),
+                                   (130, 128, 192), (64, 64, 128), (257, 512, 512), (1000, 256, 96)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rmsnorm_qkv_matches_reference(M, K, N, dtype):
+    from rl_for_mario_b200.kernels import device_status, fold_norm_weight, rmsnorm_qkv
+
+    g = torch.Generator().manual_seed(M + K + N)
+    x = (torch.randn(M, K, generator=g) * 2).to(dtype)
+    wn = (1 + 0.1 * torch.randn(K, generator=g))
+    w = torch.randn(N, K, generator=g) / K ** 0.5
+    nq = N // 2
+    nk = (N - nq) // 2
+    wq, wk, wv = w[:nq], w[nq:nq + nk], w[nq + nk:]
+    wf = fold_norm_weight(wq, wk, wv, wn, dtype).cuda()
+    y = rmsnorm_qkv(x.cuda(), wf, 1e-5)
+    assert device_status() == 0
+    ref = rmsnorm_ref(x.float(), wn) @ w.t()
+    err = (y.float().cpu() - ref).abs()
+    tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
+    assert (err <= tol + tol * ref.abs()).all(), f"max err {err.max().item():.3e}"
+
+
+@pytest.mark.gpu
+def test_fused_block_matches_unfused_block():
+    from rl_for_mario_b200.dt_model import DTConfig, DTBlock, rope_tables
+
+    cfg = DTConfig(hidden_size=256, num_attention_heads=8, num_key_value_heads=2, context_len=64, dropout=0.0)
+    torch.manual_seed(0)
+    blk = DTBlock(cfg).cuda().to(torch.bfloat16).eval()
+    x = torch.randn(4, 96, 256, device="cuda").to(torch.bfloat16)
+    cos, sin = (t.cuda() for t in rope_tables(32, 96, 1e4))
+    mask = (torch.arange(96, device="cuda")[None] >= torch.tensor([0, 3, 30, 95], device="cuda")[:, None]).float()
+    with torch.no_grad():
+        ref, _ = blk(x, (cos, sin), attention_mask=mask)
+        blk.fuse_norm(True)
+        out, _ = blk(x, (cos, sin), attention_mask=mask)
+    err = (out.float() - ref.float()).abs().max().item()
+    assert err < 6e-2, err
