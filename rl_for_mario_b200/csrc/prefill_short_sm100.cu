@@ -8,19 +8,23 @@
 //  * K and V of a unit (S x 32 each) stay resident in shared memory for all
 //    of the unit's tiles; K is rotated once per unit; the cos/sin tables are
 //    staged in shared memory once per CTA;
-//  * S = Q K^T lands in one of two TMEM slots, so the tensor core computes
-//    the next tile while the current one is in softmax;
-//  * softmax: 8 warps, two threads per row, each owning half of the row's
-//    key chunks.  A thread reads its S columns from TMEM once, the two halves
-//    exchange the exact row maximum through shared memory, and P (bf16) is
-//    written back into TMEM over the S columns it came from; O = P V reads
-//    it from there (tcgen05 MMA with A in TMEM);
-//  * the epilogue (O / rowsum -> bf16 -> HBM) of a tile runs while the tensor
-//    core computes the next tile's P V, from a second TMEM O slot;
+//  * two softmax warpgroups take alternate M tiles (one thread per row), each
+//    with its own S columns and two O slots in TMEM, so one warpgroup's
+//    exponentials overlap the other's row-max pass and epilogue while the
+//    tensor core prepares the next tiles;
+//  * a warpgroup reads S from TMEM twice (row max, then P = exp2), each
+//    time with the next 32-column load in flight; P (bf16) is written back
+//    into TMEM over the S columns it came from and O = P V reads it from there
+//    (tcgen05 MMA with A in TMEM);
+//  * the epilogue (O / rowsum -> bf16 -> HBM) of a tile runs after the
+//    warpgroup's next tile is in softmax, from the other O slot;
 //  * the TMA producer runs an 8-deep ring of Q tiles and a 3-deep ring of K/V.
 //
-// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-3 RoPE workers,
-// 4-11 softmax / epilogue.
+// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer of warpgroup 0's tiles,
+// 2 MMA issuer of warpgroup 1's tiles, 3-5 RoPE workers, 6-9 softmax
+// warpgroup 0, 10-13 softmax warpgroup 1.  A tcgen05.mma costs the issuing
+// thread tens of cycles and shares its SMSP with busy softmax warps, so each
+// warpgroup has its own issuer on its own SMSP.
 #include "dt_common.cuh"
 #include "dt_internal.h"
 #include "prefill_common.cuh"
@@ -43,22 +47,19 @@ struct SS {
   static constexpr int OFF_V = OFF_K + NKV * KV_BYTES;
   static constexpr int OFF_COS = OFF_V + NKV * KV_BYTES;
   static constexpr int OFF_SIN = OFF_COS + SMAX * CS_STRIDE * 4;
-  static constexpr int OFF_RED = OFF_SIN + SMAX * CS_STRIDE * 4;  // row max / row sum exchange
-  static constexpr int RED_FLOATS = 2 * 2 * 128 + 2 * 2 * 128;    // max[slot][half][row], sum[slot][half][row]
-  static constexpr int OFF_PAD = OFF_RED + RED_FLOATS * 4;
+  static constexpr int OFF_PAD = OFF_SIN + SMAX * CS_STRIDE * 4;
   static constexpr int MAX_UNITS = 2048;       // units per CTA (per-unit pads staged in smem)
   static constexpr int OFF_BAR = OFF_PAD + MAX_UNITS * 4;
-  // q_full, q_ready, q_empty [NQ]; kv_full, kv_ready, kv_empty [NKV]; s_full, p_full, o_full, xchg [2];
-  // fin; drain
-  static constexpr int NBAR = 3 * NQ + 3 * NKV + 8 + 2;
+  // q_full, q_ready, q_empty [NQ]; kv_full, kv_ready, kv_empty [NKV]; s_full, p_full [2 warpgroups];
+  // o_full [2 warpgroups x 2 slots]; drain [2 issuers]
+  static constexpr int NBAR = 3 * NQ + 3 * NKV + 4 + 4 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t TMEM_S = 0;    // + 192 * slot (P aliases the first half of the slot)
-  static constexpr uint32_t TMEM_O = 384;  // + 32 * slot
-  static constexpr int NTHREADS = 384;
-  static constexpr int NROPE = 64;
-  static constexpr int NSOFT = 256;
+  static constexpr uint32_t TMEM_S = 0;    // + 192 * warpgroup (P aliases the first half)
+  static constexpr uint32_t TMEM_O = 384;  // + 64 * warpgroup + 32 * slot
+  static constexpr int NTHREADS = 448;
+  static constexpr int NROPE = 96;
 };
 static_assert(SS::SMEM_BYTES <= 232448, "shared memory budget");
 
@@ -74,9 +75,13 @@ struct Cursor {
   }
 };
 
-// Key window of a tile: columns [kb0, kb0 + n) of S, chunked by 32 from kb0.
-// kb0 is placed so that the last 32-column chunk ends at the tile's causal
-// edge (the diagonal block is one chunk), rounded down to 16 keys and >= 0.
+// Alternate warpgroups; (t + lu) flips the parity per unit when the tile
+// count is even, so both warpgroups see the same mix of causal tile lengths.
+__device__ __forceinline__ int tile_wg(const Cursor& c) { return (c.t + c.lu) & 1; }
+
+// Key window of a tile: S columns [kb0, kb0 + n), processed in 32-column
+// chunks from kb0.  kb0 is placed so that the last chunk ends at the tile's
+// causal edge (the diagonal block is one chunk), rounded down to 16, >= 0.
 struct TileInfo {
   int pad, pos0, kb0, n, nc;
 };
@@ -110,17 +115,14 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
   uint64_t* kv_full = bars + 3 * SS::NQ;
   uint64_t* kv_ready = kv_full + SS::NKV;
   uint64_t* kv_empty = kv_full + 2 * SS::NKV;
-  uint64_t* s_full = kv_full + 3 * SS::NKV;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_full = s_full + 4;
-  uint64_t* xchg = s_full + 6;  // softmax halves: row-max exchange, one per slot
-  uint64_t* fin = s_full + 8;   // softmax halves: last row sums published
-  uint64_t* drain = s_full + 9;
+  uint64_t* s_full = kv_full + 3 * SS::NKV;  // [warpgroup]
+  uint64_t* p_full = s_full + 2;             // [warpgroup]
+  uint64_t* o_full = s_full + 4;             // [warpgroup * 2 + slot]
+  uint64_t* drain = s_full + 8;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + SS::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SS::OFF_MISC + 4);
   float* cos_s = reinterpret_cast<float*>(smem + SS::OFF_COS);
   float* sin_s = reinterpret_cast<float*>(smem + SS::OFF_SIN);
-  float* red = reinterpret_cast<float*>(smem + SS::OFF_RED);
   int* pads_s = reinterpret_cast<int*>(smem + SS::OFF_PAD);
 
   const int tid = threadIdx.x;
@@ -143,16 +145,15 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
     for (int i = 0; i < SS::NKV; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_ready[i], SS::NROPE);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], 2);  // both MMA issuers release a unit's K/V
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], SS::NSOFT);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&xchg[i], SS::NSOFT);
+      mbar_init(&p_full[i], 128);
     }
-    mbar_init(fin, SS::NSOFT);
-    mbar_init(drain, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&o_full[i], 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -221,72 +222,85 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuers (one per warpgroup)
     if (lane == 0) {
+      const int w = warp - 1;  // this thread issues the tiles of warpgroup w
       const uint32_t idesc_pv = umma_idesc_f16(BF16, 128, SS::D, 0, 1);
-      // S for tile c into TMEM slot (c.i & 1).
+      uint32_t p_ph = 0u;   // phase of p_full[w]
+      uint32_t slot = 0u;   // O slot of the next P V
+      // S for tile c into warpgroup w's S columns.
       auto issue_s = [&](const Cursor& c) -> bool {
         const TileInfo T = tile_info(c, pads_s, PT, S);
         const int qs = c.i % SS::NQ;
         const int kvb = c.lu % SS::NKV;
         if (!mbar_wait(&q_ready[qs], (c.i / SS::NQ) & 1, abort_flag, prm.status)) return false;
-        if (c.t == 0 && !mbar_wait(&kv_ready[kvb], (c.lu / SS::NKV) & 1, abort_flag, prm.status)) return false;
+        if (!mbar_wait(&kv_ready[kvb], (c.lu / SS::NKV) & 1, abort_flag, prm.status)) return false;
         tc_fence_after();
         // K-major 64B-swizzled operands; the second K step starts 32 bytes in.
         const uint64_t ad = umma_smem_desc(smem_u32(q_s + qs * SS::Q_BYTES), 16, 8 * SS::ROWB, kSw64);
         const uint64_t bd = umma_smem_desc(smem_u32(k_s + kvb * SS::KV_BYTES) + (uint32_t)T.kb0 * SS::ROWB, 16,
                                            8 * SS::ROWB, kSw64);
         const uint32_t idesc_s = umma_idesc_f16(BF16, 128, (uint32_t)T.n, 0, 0);
-        const uint32_t td = tmem + SS::TMEM_S + 192u * (c.i & 1);
+        const uint32_t td = tmem + SS::TMEM_S + 192u * w;
         umma_f16_ss(td, ad, bd, idesc_s, 0u);
         umma_f16_ss(td, ad + 2, bd + 2, idesc_s, 1u);
-        umma_commit(&s_full[c.i & 1]);
+        umma_commit(&s_full[w]);
         umma_commit(&q_empty[qs]);
         return true;
       };
-      // O = P V for tile c into TMEM O slot (c.i & 1), P read from the S slot.
+      // O = P V for tile c into the next O slot, P read from warpgroup w's S columns.
       auto issue_pv = [&](const Cursor& c) -> bool {
         const TileInfo T = tile_info(c, pads_s, PT, S);
         const int kvb = c.lu % SS::NKV;
-        const int slot = c.i & 1;
-        if (!mbar_wait(&p_full[slot], (c.i >> 1) & 1, abort_flag, prm.status)) return false;
+        if (!mbar_wait(&p_full[w], p_ph, abort_flag, prm.status)) return false;
+        p_ph ^= 1u;
         tc_fence_after();
-        const uint32_t pa = tmem + SS::TMEM_S + 192u * slot;  // packed bf16 P, 2 keys per column
-        const uint32_t td = tmem + SS::TMEM_O + 32u * slot;
+        const uint32_t pa = tmem + SS::TMEM_S + 192u * w;  // packed bf16 P, 2 keys per column
+        const uint32_t td = tmem + SS::TMEM_O + 64u * w + 32u * slot;
         // MN-major V rows: 16 keys per K step = 1024 bytes = 64 descriptor units.
         const uint64_t bd = umma_smem_desc(smem_u32(v_s + kvb * SS::KV_BYTES) + (uint32_t)T.kb0 * SS::ROWB,
                                            SS::KV_BYTES, 8 * SS::ROWB, kSw64);
-        // Unrolled issue (no loop-carried scalar work between MMAs): K steps of
-        // 16 keys; ksteps = n / 16 <= 12.
         const int ksteps = T.n / 16;
         umma_f16_ts(td, pa, bd, idesc_pv, 0u);
 #pragma unroll
         for (int kk = 1; kk < 12; ++kk)
           if (kk < ksteps) umma_f16_ts(td, pa + kk * 8, bd + (uint64_t)(kk * 64), idesc_pv, 1u);
-        umma_commit(&o_full[slot]);
-        if (c.t == ntiles - 1) umma_commit(&kv_empty[kvb]);
+        umma_commit(&o_full[w * 2 + slot]);
+        slot ^= 1u;
         return true;
       };
-      // S of tiles i and i+1 run ahead; after P V of tile i (same TMEM slot,
-      // executed first by the in-order tensor pipe) comes S of tile i+2.
-      Cursor c0{0, 0, 0}, c2{0, 0, 0};
+      // This warpgroup's tiles in order; S of the next one goes after the
+      // current P V (same S columns; the in-order tensor pipe runs P V first).
+      // After the last tile of a unit that this issuer touches, it releases
+      // the unit's K/V buffer (the other issuer does the same).
+      Cursor cur{0, 0, 0};
+      while (cur.i < ntotal && tile_wg(cur) != w) cur.next(ntiles);
       bool ok = true;
-      if (ntotal > 0) ok = issue_s(c0);
-      c2.next(ntiles);
-      if (ok && ntotal > 1) ok = issue_s(c2);
-      c2.next(ntiles);
-      for (Cursor c = c0; ok && c.i < ntotal; c.next(ntiles)) {
-        if (!(ok = issue_pv(c))) break;
-        if (c2.i < ntotal && !(ok = issue_s(c2))) break;
-        c2.next(ntiles);
+      int lu_done = 0;  // units whose K/V this issuer has released
+      if (cur.i < ntotal) ok = issue_s(cur);
+      while (ok && cur.i < ntotal) {
+        Cursor nxt = cur;
+        nxt.next(ntiles);
+        while (nxt.i < ntotal && tile_wg(nxt) != w) nxt.next(ntiles);
+        if (!(ok = issue_pv(cur))) break;
+        // Release K/V of every unit that no later tile of this issuer uses
+        // (including units none of its tiles touch).
+        const int lu_next = nxt.i < ntotal ? nxt.lu : my_units;
+        for (; lu_done < lu_next; ++lu_done) umma_commit(&kv_empty[lu_done % SS::NKV]);
+        if (nxt.i < ntotal && !(ok = issue_s(nxt))) break;
+        cur = nxt;
       }
-      umma_commit(drain);
-      mbar_wait(drain, 0, nullptr, nullptr);
+      if (ok) {
+        // Units this issuer never touched (no tile of its warpgroup) still need its release.
+        for (; lu_done < my_units; ++lu_done) umma_commit(&kv_empty[lu_done % SS::NKV]);
+      }
+      umma_commit(&drain[w]);
+      mbar_wait(&drain[w], 0, nullptr, nullptr);
     }
-  } else if (warp < 4) {
+  } else if (warp < 6) {
     // ------------------------------------------------------------ RoPE workers
-    const int rt = tid - 64;  // 0..63
+    const int rt = tid - 96;  // 0..95
     int qi = 0;
     bool ok = true;
     for (int lu = 0; lu < my_units && ok; ++lu) {
@@ -303,16 +317,9 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
         const int qs = qi % SS::NQ;
         if (!(ok = mbar_wait(&q_full[qs], (qi / SS::NQ) & 1, abort_flag, prm.status))) break;
         if (prm.rope) {
-          // Rows r = p * R + h: walk rows so consecutive ones share a position
-          // (the cos/sin row is re-read from shared memory, which hits the same
-          // address for the R heads of a position).
-          const int rows = PT * R;
-          const int per = (rows + SS::NROPE - 1) / SS::NROPE;
-          const int r0 = rt * per;
-          for (int k2 = 0; k2 < per; ++k2) {
-            const int row = r0 + k2;
+          for (int row = rt; row < PT * R; row += SS::NROPE) {
             const int pos = t * PT + row / R;
-            if (row < rows && pos < S)
+            if (pos < S)
               rope_row_inplace_smem<32, BF16>(q_s + qs * SS::Q_BYTES, row, cos_s + pos * SS::CS_STRIDE,
                                               sin_s + pos * SS::CS_STRIDE);
           }
@@ -323,39 +330,39 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax + epilogue
-    const int half = (warp - 4) >> 2;  // which half of each row's key chunks
-    const int wq = warp & 3;           // TMEM lane quarter this warp may access
-    const int r = wq * 32 + lane;      // tile row = TMEM lane
+    // ------------------------------------------------------------ softmax warpgroups
+    const int w = (warp - 6) >> 2;  // warpgroup 0: warps 6-9, 1: warps 10-13
+    const int wq = warp & 3;        // TMEM lane quarter this warp may access
+    const int r = wq * 32 + lane;   // tile row = TMEM lane
     const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
+    const uint32_t t_s = t_lane + SS::TMEM_S + 192u * w;
+    const uint32_t t_o = t_lane + SS::TMEM_O + 64u * w;
     const float c2 = prm.scale_log2;
     const int h = r % R;
     const int rowpos = r / R;
-    float* red_max = red;                 // [slot][half][128]
-    float* red_sum = red + 2 * 2 * 128;   // [slot][half][128]
+    uint32_t sph = 0;
+    uint32_t done = 0;  // tiles of this warpgroup finished (selects O slot and phase)
     bool ok = true;
 
-    // Epilogue of tile c: O from its TMEM slot / row sum -> bf16 -> HBM.
-    // Each half stores 16 of the 32 output columns.
-    auto epilogue = [&](const Cursor& c) -> bool {
-      const int slot = c.i & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&o_full[slot], (c.i >> 1) & 1, abort_flag, prm.status)))
+    // Epilogue of this warpgroup's k-th tile: O from its slot / row sum -> bf16 -> HBM.
+    auto epilogue = [&](const Cursor& c, uint32_t k, float l) -> bool {
+      const uint32_t slot = k & 1u;
+      if (!__all_sync(0xffffffffu, mbar_wait(&o_full[w * 2 + slot], (k >> 1) & 1u, abort_flag, prm.status)))
         return false;
       tc_fence_after();
-      float o[16];
-      tmem_ld16(t_lane + SS::TMEM_O + 32u * slot + 16u * half, o);
+      float o[32];
+      tmem_ld32(t_o + 32u * slot, o);
       tc_fence_before();
       const int pos = c.t * PT + rowpos;
       if (r < PT * R && pos < S) {
-        const float l = red_sum[(slot * 2 + 0) * 128 + r] + red_sum[(slot * 2 + 1) * 128 + r];
         const int unit = blockIdx.x + c.lu * gridDim.x;
         const int b = unit / prm.Hkv;
         const int g = unit - b * prm.Hkv;
         const float inv = 1.f / l;
         typename E::T* orow = reinterpret_cast<typename E::T*>(prm.o) + (size_t)b * prm.o_sb +
-                              (size_t)pos * prm.o_ss + (size_t)(g * R + h) * prm.o_sh + 16 * half;
+                              (size_t)pos * prm.o_ss + (size_t)(g * R + h) * prm.o_sh;
 #pragma unroll
-        for (int cc = 0; cc < 16; cc += 8) {
+        for (int cc = 0; cc < 32; cc += 8) {
           uint4 v;
           v.x = E::from_f2(o[cc + 0] * inv, o[cc + 1] * inv);
           v.y = E::from_f2(o[cc + 2] * inv, o[cc + 3] * inv);
@@ -368,32 +375,19 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
     };
 
     Cursor prev{0, 0, -1};
+    float l_prev = 0.f;
     for (Cursor cur{0, 0, 0}; cur.i < ntotal && ok; cur.next(ntiles)) {
+      if (tile_wg(cur) != w) continue;
       const TileInfo T = tile_info(cur, pads_s, PT, S);
-      const int slot = cur.i & 1;
       const int pos = T.pos0 + rowpos;
       const bool valid_row = (r < PT * R) && (pos < S);
       const bool padded = pos < T.pad;
       const int lo = padded ? 0 : T.pad;
       const int hi = valid_row ? pos : -1;
-      // This half's chunks: [c_begin, c_begin + myc) of the tile's T.nc chunks.
-      const int c_split = (T.nc + 1) >> 1;
-      const int c_begin = half ? c_split : 0;
-      const int myc = (half ? T.nc : c_split) - c_begin;  // 0..3
       const bool tile_clean = T.pos0 >= T.pad;
-      const uint32_t t_s = t_lane + SS::TMEM_S + 192u * slot + 32u * c_begin;
-
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[slot], (cur.i >> 1) & 1, abort_flag, prm.status))))
-        break;
-      tc_fence_after();
-      uint32_t sa[32], sb[32], sc[32];
-      if (myc > 0) tmem_ld32_async(t_s, sa);
-      if (myc > 1) tmem_ld32_async(t_s + 32, sb);
-      if (myc > 2) tmem_ld32_async(t_s + 64, sc);
-      tmem_wait_ld3(sa, sb, sc);
-
-      // Allowed keys of this row inside chunk ci, as a 32-bit mask (bit j =
-      // key kb0 + 32 ci + j): [lo, hi] clipped to the chunk.
+      const int nc = T.nc;
+      // Allowed keys of this row inside chunk ci as a 32-bit mask (bit j = key
+      // kb0 + 32 ci + j): [lo, hi] clipped to the chunk.
       auto chunk_mask = [&](int ci) -> uint32_t {
         const int k0 = T.kb0 + 32 * ci;
         const int jlo = lo - k0, jhi = hi - k0;
@@ -401,61 +395,77 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
         const uint32_t lm = jlo <= 0 ? 0xffffffffu : (jlo >= 32 ? 0u : (0xffffffffu << jlo));
         return hm & lm;
       };
-      // A chunk is free of masking for every row of the tile when the tile has
-      // no padded rows and the chunk lies in [pad, pos0] (warp-uniform test).
+      // Chunks inside [pad, pos0] of a tile without padded rows need no mask
+      // for any row (warp-uniform test).
       auto chunk_clean = [&](int ci) -> bool {
         const int k0 = T.kb0 + 32 * ci;
         return tile_clean && k0 >= T.pad && k0 + 31 <= T.pos0;
       };
-      // Partial row maximum over this half's allowed keys, in 4 independent
-      // accumulators (short dependency chains).
-      float mx[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) mx[j] = -INFINITY;
+
+      // Warp-uniform wait outcome keeps the .sync.aligned TMEM accesses convergent.
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[w], sph, abort_flag, prm.status)))) break;
+      sph ^= 1u;
+      tc_fence_after();
+
+      uint32_t ra[32], rb[32];
+      // Pass 1: row maximum over the allowed keys; the next chunk's load is in
+      // flight while a chunk is reduced.
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
       auto chunk_max = [&](const uint32_t (&u)[32], int ci) {
         if (chunk_clean(ci)) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], __uint_as_float(u[j]));
+          for (int j = 0; j < 32; j += 4) {
+            mx0 = fmaxf(mx0, __uint_as_float(u[j]));
+            mx1 = fmaxf(mx1, __uint_as_float(u[j + 1]));
+            mx2 = fmaxf(mx2, __uint_as_float(u[j + 2]));
+            mx3 = fmaxf(mx3, __uint_as_float(u[j + 3]));
+          }
         } else {
           const uint32_t mk = chunk_mask(ci);
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            mx[j & 3] = fmaxf(mx[j & 3], ((mk >> j) & 1u) ? __uint_as_float(u[j]) : -INFINITY);
+          for (int j = 0; j < 32; j += 4) {
+            mx0 = fmaxf(mx0, ((mk >> j) & 1u) ? __uint_as_float(u[j]) : -INFINITY);
+            mx1 = fmaxf(mx1, ((mk >> (j + 1)) & 1u) ? __uint_as_float(u[j + 1]) : -INFINITY);
+            mx2 = fmaxf(mx2, ((mk >> (j + 2)) & 1u) ? __uint_as_float(u[j + 2]) : -INFINITY);
+            mx3 = fmaxf(mx3, ((mk >> (j + 3)) & 1u) ? __uint_as_float(u[j + 3]) : -INFINITY);
+          }
         }
       };
-      if (myc > 0) chunk_max(sa, c_begin);
-      if (myc > 1) chunk_max(sb, c_begin + 1);
-      if (myc > 2) chunk_max(sc, c_begin + 2);
-      const float pmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      // Exchange partial maxima between the halves (bounded mbarrier wait).  The
-      // tcgen05 fences order every S read of both halves before any P write.
-      red_max[(slot * 2 + half) * 128 + r] = pmax;
-      tc_fence_before();
-      mbar_arrive(&xchg[slot]);
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&xchg[slot], (cur.i >> 1) & 1, abort_flag, prm.status))))
-        break;
-      tc_fence_after();
-      const float rmax = fmaxf(pmax, red_max[(slot * 2 + (half ^ 1)) * 128 + r]);
+      tmem_ld32_async(t_s, ra);
+      for (int ci = 0; ci < nc; ci += 2) {
+        tmem_wait_ld(ra);
+        if (ci + 1 < nc) tmem_ld32_async(t_s + 32 * (ci + 1), rb);
+        chunk_max(ra, ci);
+        if (ci + 1 < nc) {
+          tmem_wait_ld(rb);
+          if (ci + 2 < nc) tmem_ld32_async(t_s + 32 * (ci + 2), ra);
+          chunk_max(rb, ci + 1);
+        }
+      }
+      const float bmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
       // t = s * c2 - m.  Padded rows use c2 = m = 0, so every allowed key gets
       // exp2(0) = 1 (the reference's tie over keys 0..q); masked keys get -inf.
-      const float m = (padded || rmax == -INFINITY) ? 0.f : rmax * c2;
+      const float m = (padded || bmax == -INFINITY) ? 0.f : bmax * c2;
       const float cr = padded ? 0.f : c2;
 
-      // P = exp2(t), packed bf16 pairs stored over the S columns just read;
-      // partial row sum in fp32.
-      float ls[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ls[j] = 0.f;
+      // Pass 2: P = exp2(t), packed bf16 pairs stored over the S columns just
+      // read; row sum in fp32.
+      float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
       auto chunk_p = [&](const uint32_t (&u)[32], int ci) {
         uint32_t pk[16];
         if (chunk_clean(ci)) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
+          for (int j = 0; j < 32; j += 4) {
             const float p0 = ex2_approx(fmaf(__uint_as_float(u[j]), c2, -m));
             const float p1 = ex2_approx(fmaf(__uint_as_float(u[j + 1]), c2, -m));
-            ls[j & 3] += p0;
-            ls[(j + 1) & 3] += p1;
+            const float p2 = ex2_approx(fmaf(__uint_as_float(u[j + 2]), c2, -m));
+            const float p3 = ex2_approx(fmaf(__uint_as_float(u[j + 3]), c2, -m));
+            l0 += p0;
+            l1 += p1;
+            l2 += p2;
+            l3 += p3;
             pk[j >> 1] = E::from_f2(p0, p1);
+            pk[(j >> 1) + 1] = E::from_f2(p2, p3);
           }
         } else {
           const uint32_t mk = chunk_mask(ci);
@@ -464,31 +474,40 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
             const float t0 = ((mk >> j) & 1u) ? fmaf(__uint_as_float(u[j]), cr, -m) : -INFINITY;
             const float t1 = ((mk >> (j + 1)) & 1u) ? fmaf(__uint_as_float(u[j + 1]), cr, -m) : -INFINITY;
             const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
-            ls[j & 3] += p0;
-            ls[(j + 1) & 3] += p1;
+            if (j & 2) {
+              l2 += p0;
+              l3 += p1;
+            } else {
+              l0 += p0;
+              l1 += p1;
+            }
             pk[j >> 1] = E::from_f2(p0, p1);
           }
         }
-        tmem_st16(t_lane + SS::TMEM_S + 192u * slot + 16u * ci, pk);
+        tmem_st16(t_s + 16 * ci, pk);
       };
-      if (myc > 0) chunk_p(sa, c_begin);
-      if (myc > 1) chunk_p(sb, c_begin + 1);
-      if (myc > 2) chunk_p(sc, c_begin + 2);
-      const float l = (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      red_sum[(slot * 2 + half) * 128 + r] = l;
+      tmem_ld32_async(t_s, ra);
+      for (int ci = 0; ci < nc; ci += 2) {
+        tmem_wait_ld(ra);
+        if (ci + 1 < nc) tmem_ld32_async(t_s + 32 * (ci + 1), rb);
+        chunk_p(ra, ci);
+        if (ci + 1 < nc) {
+          tmem_wait_ld(rb);
+          if (ci + 2 < nc) tmem_ld32_async(t_s + 32 * (ci + 2), ra);
+          chunk_p(rb, ci + 1);
+        }
+      }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_full[slot]);
+      mbar_arrive(&p_full[w]);
       // While the tensor core runs this tile's P V and the next S, finish the
-      // previous tile (its row sums were published before this tile's exchange).
-      if (prev.i >= 0 && !(ok = epilogue(prev))) break;
+      // previous tile of this warpgroup (other O slot).
+      if (prev.i >= 0 && !(ok = epilogue(prev, done - 1, l_prev))) break;
       prev = cur;
+      l_prev = (l0 + l1) + (l2 + l3);
+      ++done;
     }
-    if (ok && prev.i >= 0) {
-      // Publish the last tile's row sums to the other half, then finish it.
-      mbar_arrive(fin);
-      if (__all_sync(0xffffffffu, mbar_wait(fin, 0, abort_flag, prm.status))) epilogue(prev);
-    }
+    if (ok && prev.i >= 0) epilogue(prev, done - 1, l_prev);
   }
 
   __syncthreads();
