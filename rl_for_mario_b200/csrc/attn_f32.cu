@@ -22,18 +22,12 @@ constexpr int kF32KB = 64;
 // Online-softmax accumulation of one key for one row (log2 domain).
 template <int D>
 __device__ __forceinline__ void f32_accumulate(const float* __restrict__ kr, const float* __restrict__ vr,
-                                               const float (&q)[D], float c2, bool padded, float& m, float& l,
-                                               float (&acc)[D]) {
-  if (padded) {  // tie at -1e9 over keys 0..q: unit weights
-    l += 1.f;
-#pragma unroll
-    for (int d = 0; d < D; ++d) acc[d] += vr[d];
-    return;
-  }
+                                               const float (&q)[D], float c2, float sd64, bool padded, float& m,
+                                               float& l, float (&acc)[D]) {
   float s = 0.f;
 #pragma unroll
   for (int d = 0; d < D; ++d) s = fmaf(q[d], kr[d], s);
-  s *= c2;
+  s = RowScore(padded, c2, sd64)(s);
   if (s > m) {
     const float sc = exp2f(m - s);  // m = -inf -> 0
     l *= sc;
@@ -109,7 +103,7 @@ __global__ void __launch_bounds__(kF32Threads) dt_prefill_f32_kernel(const Prefi
     }
     __syncthreads();
     const int j0 = max(lo - kb, 0), j1 = min(hi - kb, nk - 1);
-    for (int j = j0; j <= j1; ++j) f32_accumulate<D>(ks[j], vs[j], q, c2, padded, m, l, acc);
+    for (int j = j0; j <= j1; ++j) f32_accumulate<D>(ks[j], vs[j], q, c2, p.scale_div64, padded, m, l, acc);
   }
   if (valid) {
     float* orow = p.o + (size_t)b * p.o_sb + (size_t)pos * p.o_ss + (size_t)(g * R + h) * p.o_sh;
@@ -210,7 +204,7 @@ __global__ void __launch_bounds__(kF32Threads) dt_decode_f32_kernel(const Decode
     }
     __syncthreads();
     const int j0 = max(lo - kb, 0), j1 = min(hi - kb, nk - 1);
-    for (int j = j0; j <= j1; ++j) f32_accumulate<D>(ks[j], vs[j], q, p.scale_log2, padded, m, l, acc);
+    for (int j = j0; j <= j1; ++j) f32_accumulate<D>(ks[j], vs[j], q, p.scale_log2, p.scale_div64, padded, m, l, acc);
   }
   if (valid) {
     float* orow = static_cast<float*>(p.o) + (size_t)b * p.o_sb + (size_t)i * p.o_ss + (size_t)(g * R + h) * p.o_sh;

@@ -176,6 +176,7 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
     fp.v_sb = v_sb; fp.v_ss = v_ss; fp.v_sh = v_sh; fp.o_sb = o_sb; fp.o_ss = o_ss; fp.o_sh = o_sh;
     fp.cs_stride = (int)cos_stride; fp.rope = apply_rope ? 1 : 0; fp.S = S; fp.Hkv = Hkv; fp.R = R;
     fp.scale_log2 = sc0 * 1.4426950408889634f;
+    fp.scale_div64 = sc0 / 64.f;
     cudaError_t e = dtk::launch_prefill_f32(fp, D, B, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "dt_attn_prefill (fp32) launch");
     return DT_OK;
@@ -207,6 +208,7 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
   prm.PT = PT;
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   prm.scale_log2 = sc * 1.4426950408889634f;
+  prm.scale_div64 = sc / 64.f;
   prm.rope = apply_rope ? 1 : 0;
   const int units = B * Hkv;
   cudaError_t e;
@@ -276,6 +278,7 @@ int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o,
   p.Sn = Sn; p.Hkv = Hkv; p.R = Hq / Hkv; p.page_size = page_size; p.max_pages = max_pages; p.num_pages = num_pages;
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   p.scale_log2 = sc * 1.4426950408889634f;
+  p.scale_div64 = sc / 64.f;
   if ((long long)B * Hkv > 0x7fffffffLL) return fail(DT_ERR_UNSUPPORTED, "%s: B*Hkv too large", fn);
   cudaError_t e = dtype == DT_DTYPE_FP32
                       ? dtk::launch_decode_f32(p, D, B, static_cast<cudaStream_t>(stream))

@@ -168,6 +168,7 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
   const int nrows = Sn * R;
   const int ngroups = (nrows + 15) / 16;
   const float c2 = p.scale_log2;
+  const float sd64 = p.scale_div64;
   // Make this CTA's cache writes visible to its own loads below.
   __threadfence_block();
   __syncthreads();
@@ -280,16 +281,11 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
             }
           cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
           cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
-          float m_new, cr;
-          if (rpad[k]) {
-            m_new = 0.f;  // padded row: unit weights (exp2(0)) on keys 0..q
-            cr = 0.f;
-          } else {
-            m_new = fmaxf(m_run[k], cmax * c2);
-            cr = c2;
-          }
+          // Fully padded rows score their keys in the reference's 64-wide bands.
+          const RowScore rs(rpad[k], c2, sd64);
+          const float m_new = fmaxf(m_run[k], rs(cmax));
           const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-          const float alpha = rpad[k] ? 1.f : ex2_approx(m_run[k] - m_use);
+          const float alpha = ex2_approx(m_run[k] - m_use);  // m_run = -inf -> 0
           float lsum = 0.f;
 #pragma unroll
           for (int j = 0; j < 2; ++j)
@@ -297,14 +293,15 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
             for (int e2 = 0; e2 < 2; ++e2) {
               const int key = kb + key0 + 8 * j + 2 * t4 + e2;
               const bool ok = key >= rlo[k] && key <= rhi[k];
-              const float pe = ok ? ex2_approx(fmaf(sc[j][2 * k + e2], cr, -m_use)) : 0.f;
+              const float sv = sc[j][2 * k + e2];
+              const float pe = ok ? ex2_approx(rs(sv) - m_use) : 0.f;
               pv[j][2 * k + e2] = pe;
               lsum += pe;
             }
           lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
           lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
           l_run[k] = l_run[k] * alpha + lsum;
-          m_run[k] = rpad[k] ? m_run[k] : m_new;
+          m_run[k] = m_new;
 #pragma unroll
           for (int jd = 0; jd < D / 8; ++jd) {
             oacc[jd][2 * k] *= alpha;
@@ -357,7 +354,7 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
 #pragma unroll
       for (int w = 0; w < kDecWarps; ++w) {
         const float* rw = red + (w * 16 + rr) * SH::RED_STRIDE;
-        const float sc = ex2_approx(rw[D] - Mu);  // padded rows: m = -inf for all warps -> M = -inf -> factor 1
+        const float sc = ex2_approx(rw[D] - Mu);
         const float f = (rw[D] == -INFINITY) ? (M == -INFINITY ? 1.f : 0.f) : sc;
         lt += f * rw[D + 1];
         ot += f * rw[d];

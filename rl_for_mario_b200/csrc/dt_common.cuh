@@ -225,6 +225,45 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Score of an allowed key in a fully left-padded query row, in log2 units.
+// The reference adds -1e9 to every key of such a row before its fp32
+// softmax.  That sum rounds the scaled score x = s * scale to the nearest
+// multiple of 64 (half to even: -1e9 and its bf16 rounding are both even
+// multiples of 64), so the row weighs its keys equally within the top
+// 64-wide band and by e^-64 or less outside it: a plain mean of V whenever
+// |x| < 32.  fma(s, scale / 64, 1.5 * 2^23) rounds x / 64 to an integer in
+// one step (|x| / 64 < 2^22).
+__device__ __forceinline__ float padded_score_log2(float s, float scale_div64) {
+  const float kRound = 12582912.f;  // 1.5 * 2^23
+  const float band = __fsub_rn(__fmaf_rn(s, scale_div64, kRound), kRound);
+  return band * 92.332482616893658f;  // 64 * log2(e)
+}
+
+// Log2-domain score of a key for one query row: s * c2 for a row with valid
+// keys, padded_score_log2(s) for a fully padded row, written as
+// (fma(s, mul, add) - add) * out so that both rows run the same instructions
+// (add = 0, out = 1 gives s * c2 bit for bit).
+struct RowScore {
+  float mul, add, out;
+  __device__ __forceinline__ RowScore(bool padded, float c2, float scale_div64)
+      : mul(padded ? scale_div64 : c2), add(padded ? 12582912.f : 0.f), out(padded ? 92.332482616893658f : 1.f) {}
+  __device__ __forceinline__ float operator()(float s) const {
+    return __fsub_rn(__fmaf_rn(s, mul, add), add) * out;
+  }
+};
+
+// 16 columns as raw 32-bit words (load and wait in one statement).
+__device__ __forceinline__ void tmem_ld16_u(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
 // Same for 32 consecutive columns.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
@@ -314,6 +353,10 @@ struct Elem<true> {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  static __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
 };
 template <>
 struct Elem<false> {
@@ -326,6 +369,10 @@ struct Elem<false> {
   static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+  }
+  static __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
   }
 };
 

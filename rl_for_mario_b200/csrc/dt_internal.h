@@ -18,6 +18,7 @@ struct PrefillParams {
   int cs_stride;
   int S, Hkv, R, PT;        // R = Hq / Hkv query heads per KV head, PT = positions per 128-row tile
   float scale_log2;         // softmax scale * log2(e)
+  float scale_div64;        // softmax scale / 64 (fully padded rows)
   int rope;                 // 1: rotate Q and K in the kernel
 };
 
@@ -48,6 +49,7 @@ struct DecodeParams {
   int cos_rows;
   int Sn, Hkv, R, page_size, max_pages, num_pages;
   float scale_log2;
+  float scale_div64;
 };
 
 // Kernel parameters of dt_kv_write.
@@ -79,6 +81,7 @@ struct PrefillF32Params {
   int cs_stride, rope;
   int S, Hkv, R;
   float scale_log2;
+  float scale_div64;
 };
 
 cudaError_t launch_prefill_f32(const PrefillF32Params& prm, int D, int B, cudaStream_t stream);

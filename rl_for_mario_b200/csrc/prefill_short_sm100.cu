@@ -338,6 +338,7 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
     const uint32_t t_s = t_lane + SS::TMEM_S + 192u * w;
     const uint32_t t_o = t_lane + SS::TMEM_O + 64u * w;
     const float c2 = prm.scale_log2;
+    const float sd64 = prm.scale_div64;
     const int h = r % R;
     const int rowpos = r / R;
     uint32_t sph = 0;
@@ -443,10 +444,11 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
         }
       }
       const float bmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      // t = s * c2 - m.  Padded rows use c2 = m = 0, so every allowed key gets
-      // exp2(0) = 1 (the reference's tie over keys 0..q); masked keys get -inf.
-      const float m = (padded || bmax == -INFINITY) ? 0.f : bmax * c2;
-      const float cr = padded ? 0.f : c2;
+      // t = s * c2 - m for rows with valid keys.  Fully padded rows score
+      // their keys in the reference's 64-wide bands (RowScore); warps without
+      // such rows keep the one-instruction form.  Masked keys get -inf.
+      const bool warp_padded = __any_sync(0xffffffffu, padded);
+      const float m = bmax == -INFINITY ? 0.f : RowScore(padded, c2, sd64)(bmax);
 
       // Pass 2: P = exp2(t), packed bf16 pairs stored over the S columns just
       // read; row sum in fp32.
@@ -467,12 +469,29 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
             pk[j >> 1] = E::from_f2(p0, p1);
             pk[(j >> 1) + 1] = E::from_f2(p2, p3);
           }
+        } else if (warp_padded) {
+          const uint32_t mk = chunk_mask(ci);
+          const RowScore rs(padded, c2, sd64);
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float e0 = rs(__uint_as_float(u[j])) - m, e1 = rs(__uint_as_float(u[j + 1])) - m;
+            const float p0 = ex2_approx(((mk >> j) & 1u) ? e0 : -INFINITY);
+            const float p1 = ex2_approx(((mk >> (j + 1)) & 1u) ? e1 : -INFINITY);
+            if (j & 2) {
+              l2 += p0;
+              l3 += p1;
+            } else {
+              l0 += p0;
+              l1 += p1;
+            }
+            pk[j >> 1] = E::from_f2(p0, p1);
+          }
         } else {
           const uint32_t mk = chunk_mask(ci);
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const float t0 = ((mk >> j) & 1u) ? fmaf(__uint_as_float(u[j]), cr, -m) : -INFINITY;
-            const float t1 = ((mk >> (j + 1)) & 1u) ? fmaf(__uint_as_float(u[j + 1]), cr, -m) : -INFINITY;
+            const float t0 = ((mk >> j) & 1u) ? fmaf(__uint_as_float(u[j]), c2, -m) : -INFINITY;
+            const float t1 = ((mk >> (j + 1)) & 1u) ? fmaf(__uint_as_float(u[j + 1]), c2, -m) : -INFINITY;
             const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
             if (j & 2) {
               l2 += p0;

@@ -18,9 +18,9 @@
 // Mask semantics (reference :206-224, left padding of `pad` tokens):
 //   valid row q >= pad : softmax over keys pad..q (keys < pad get -1e9, whose
 //                        weight underflows to exactly 0 in fp32);
-//   padded row q < pad : every key 0..q carries -1e9, the scores tie and the
-//                        reference returns mean(V[0..q]); reproduced here with
-//                        unit weights on keys 0..q.
+//   padded row q < pad : every key 0..q carries -1e9; the fp32 sum rounds the
+//                        scaled scores to 64-wide bands (padded_score_log2),
+//                        a plain mean of V[0..q] while |score| < 32.
 #include <cstdio>
 
 #include "dt_common.cuh"
@@ -254,6 +254,7 @@ __global__ void __launch_bounds__(256, PrefillShape<D>::MIN_BLOCKS)
     const int r = wq * 32 + lane;
     const uint32_t t_lane = tmem + ((uint32_t)(wq * 32) << 16);
     const float c2 = prm.scale_log2;
+    const float sd64 = prm.scale_div64;
     uint32_t s_ph = 0, o_ph = 0;
     bool ok = true;
     const int h = r % R;
@@ -291,12 +292,10 @@ __global__ void __launch_bounds__(256, PrefillShape<D>::MIN_BLOCKS)
               if (key >= lo && key <= hi) bmax = fmaxf(bmax, s[i]);
             }
           }
-          if (!padded) {
-            const float m_new = fmaxf(m, bmax * c2);
-            m_use = (m_new == -INFINITY) ? 0.f : m_new;
-            alpha = ex2_approx(m - m_use);  // m = -inf -> 0
-            m = m_new;
-          }
+          const float m_new = fmaxf(m, padded ? padded_score_log2(bmax, sd64) : bmax * c2);
+          m_use = (m_new == -INFINITY) ? 0.f : m_new;
+          alpha = ex2_approx(m - m_use);  // m = -inf -> 0
+          m = m_new;
         }
         float bsum = 0.f;
         for (int c = 0; c < n; c += 16) {
@@ -310,8 +309,8 @@ __global__ void __launch_bounds__(256, PrefillShape<D>::MIN_BLOCKS)
             const bool a1 = key + 1 >= lo && key + 1 <= hi;
             float p0, p1;
             if (padded) {
-              p0 = a0 ? 1.f : 0.f;
-              p1 = a1 ? 1.f : 0.f;
+              p0 = a0 ? ex2_approx(padded_score_log2(s[i], sd64) - m_use) : 0.f;
+              p1 = a1 ? ex2_approx(padded_score_log2(s[i + 1], sd64) - m_use) : 0.f;
             } else {
               p0 = a0 ? ex2_approx(fmaf(s[i], c2, -m_use)) : 0.f;
               p1 = a1 ? ex2_approx(fmaf(s[i + 1], c2, -m_use)) : 0.f;

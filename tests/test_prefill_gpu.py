@@ -121,3 +121,29 @@ def test_prefill_rejects_bad_arguments():
     k = torch.zeros(1, 16, 1, 32, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(DTKernelError, match="rows"):
         attn_prefill(q, k, k.clone(), cos, sin)  # cos has 8 rows < S = 16
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("direction", ["rising", "falling"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_prefill_wide_logit_range(direction, dtype):
+    """Scores that climb (or fall) by ~16 log2 units per 32 keys: a running row
+    maximum has to move many times along the row, and the padded rows still take
+    the plain mean of their keys."""
+    from rl_for_mario_b200.kernels import attn_prefill, device_status
+
+    B, S, Hq, Hkv, D = 3, 192, 8, 2, 32
+    g = torch.Generator().manual_seed(11)
+    ramp = torch.arange(S, dtype=torch.float32) * 0.06
+    if direction == "falling":
+        ramp = ramp.flip(0)
+    if dtype == torch.float16:
+        ramp = ramp * 0.25  # fp16 scores stay inside its range at any reference
+    q32 = (1.0 + 0.1 * torch.randn(B, S, Hq, D, generator=g)).to(dtype).float()
+    k32 = (ramp.view(1, S, 1, 1) * (1.0 + 0.1 * torch.randn(B, S, Hkv, D, generator=g))).to(dtype).float()
+    v32 = torch.randn(B, S, Hkv, D, generator=g).to(dtype).float()
+    pad_t = torch.tensor([0, 37, 100], dtype=torch.int32)
+    ref = attention_prefill_ref(q32, k32, v32, None, None, mask_from_pad_len(pad_t, S), rope=False)
+    out = attn_prefill(*(t.to(dtype).cuda() for t in (q32, k32, v32)), None, None, pad_t.cuda(), apply_rope=False)
+    assert device_status() == 0
+    _check(out.float().cpu(), ref, dtype)
