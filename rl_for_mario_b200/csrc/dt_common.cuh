@@ -239,6 +239,16 @@ __device__ __forceinline__ float padded_score_log2(float s, float scale_div64) {
   return band * 92.332482616893658f;  // 64 * log2(e)
 }
 
+// Lowest raw score s whose scaled value shares the top 64-wide band with
+// smax (the row's largest allowed score); exact up to one ulp at the band
+// edge.  In a fully padded row the keys at or above it weigh 1 each and all
+// others at most e^-64 relative to them, which bf16/fp16 kernels drop.
+__device__ __forceinline__ float padded_band_floor(float smax, float scale_div64) {
+  const float kRound = 12582912.f;  // 1.5 * 2^23
+  const float band = __fsub_rn(__fmaf_rn(smax, scale_div64, kRound), kRound);
+  return __fdiv_rn(band - 0.5f, scale_div64);
+}
+
 // Log2-domain score of a key for one query row: s * c2 for a row with valid
 // keys, padded_score_log2(s) for a fully padded row, written as
 // (fma(s, mul, add) - add) * out so that both rows run the same instructions

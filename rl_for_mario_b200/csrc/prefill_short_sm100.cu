@@ -444,11 +444,14 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
         }
       }
       const float bmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      // t = s * c2 - m for rows with valid keys.  Fully padded rows score
-      // their keys in the reference's 64-wide bands (RowScore); warps without
-      // such rows keep the one-instruction form.  Masked keys get -inf.
+      // t = s * c2 - m; masked keys get -inf.  Fully padded rows use c2 = m = 0
+      // (weight 1) on the keys of the reference's top 64-wide -1e9 band
+      // (s >= thr) and drop the rest (weights <= e^-64 there); only warps
+      // holding such rows pay for the threshold test.
+      const float m = (padded || bmax == -INFINITY) ? 0.f : bmax * c2;
+      const float cr = padded ? 0.f : c2;
+      const float thr = padded ? padded_band_floor(bmax, sd64) : -INFINITY;
       const bool warp_padded = __any_sync(0xffffffffu, padded);
-      const float m = bmax == -INFINITY ? 0.f : RowScore(padded, c2, sd64)(bmax);
 
       // Pass 2: P = exp2(t), packed bf16 pairs stored over the S columns just
       // read; row sum in fp32.
@@ -471,12 +474,12 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
           }
         } else if (warp_padded) {
           const uint32_t mk = chunk_mask(ci);
-          const RowScore rs(padded, c2, sd64);
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const float e0 = rs(__uint_as_float(u[j])) - m, e1 = rs(__uint_as_float(u[j + 1])) - m;
-            const float p0 = ex2_approx(((mk >> j) & 1u) ? e0 : -INFINITY);
-            const float p1 = ex2_approx(((mk >> (j + 1)) & 1u) ? e1 : -INFINITY);
+            const float s0 = __uint_as_float(u[j]), s1 = __uint_as_float(u[j + 1]);
+            const float t0 = (((mk >> j) & 1u) && s0 >= thr) ? fmaf(s0, cr, -m) : -INFINITY;
+            const float t1 = (((mk >> (j + 1)) & 1u) && s1 >= thr) ? fmaf(s1, cr, -m) : -INFINITY;
+            const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
             if (j & 2) {
               l2 += p0;
               l3 += p1;
@@ -490,8 +493,9 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
           const uint32_t mk = chunk_mask(ci);
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const float t0 = ((mk >> j) & 1u) ? fmaf(__uint_as_float(u[j]), c2, -m) : -INFINITY;
-            const float t1 = ((mk >> (j + 1)) & 1u) ? fmaf(__uint_as_float(u[j + 1]), c2, -m) : -INFINITY;
+            const float s0 = __uint_as_float(u[j]), s1 = __uint_as_float(u[j + 1]);
+            const float t0 = ((mk >> j) & 1u) ? fmaf(s0, cr, -m) : -INFINITY;
+            const float t1 = ((mk >> (j + 1)) & 1u) ? fmaf(s1, cr, -m) : -INFINITY;
             const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
             if (j & 2) {
               l2 += p0;

@@ -140,3 +140,32 @@ def test_decode_device_check_flags_bad_page_ids():
     cos, sin = (t.cuda() for t in precompute_freqs_cis(D, 3))
     attn_decode(x, kv, kv, layer, cos, sin)
     assert device_status() != 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_decode_wide_logit_range(dtype):
+    """Cached keys whose scores climb by ~16 log2 units per 32 positions: new
+    tokens inside the left padding weigh their keys in the reference's 64-wide
+    -1e9 bands, the others need a moving running maximum."""
+    from rl_for_mario_b200.kernels import attn_decode, device_status, kv_write
+
+    B, L, Sn, Hq, Hkv, D = 3, 150, 3, 8, 2, 32
+    g = torch.Generator().manual_seed(5)
+    layer = _make_cache(B, Hkv, D, L + Sn, 64, dtype, True, g)
+    ramp = torch.arange(L + Sn, dtype=torch.float32) * 0.06
+    k_all = (ramp.view(1, -1, 1, 1) * (1.0 + 0.1 * torch.randn(B, L + Sn, Hkv, D, generator=g))).to(dtype)
+    v_all = torch.randn(B, L + Sn, Hkv, D, generator=g).to(dtype)
+    q = (1.0 + 0.1 * torch.randn(B, Sn, Hq, D, generator=g)).to(dtype)
+    kv_write(k_all[:, :L].cuda(), v_all[:, :L].cuda(), layer, None, None, apply_rope=False)
+    layer.advance(L)
+    pads = torch.tensor([0, 60, L + 2], dtype=torch.int32)  # last sample: two new tokens still padded
+    mask = mask_from_pad_len(pads, L + Sn)
+    past_k = k_all[:, :L].float().transpose(1, 2)
+    past_v = v_all[:, :L].float().transpose(1, 2)
+    ref, _, _ = attention_decode_ref(q.float(), k_all[:, L:].float(), v_all[:, L:].float(), past_k, past_v,
+                                     None, None, mask, rope=False)
+    out = attn_decode(q.cuda(), k_all[:, L:].cuda(), v_all[:, L:].cuda(), layer, None, None, pads.cuda(),
+                      apply_rope=False)
+    assert device_status() == 0
+    _check(out.float().cpu(), ref, dtype)

@@ -125,20 +125,22 @@ def test_prefill_rejects_bad_arguments():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("direction", ["rising", "falling"])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_prefill_wide_logit_range(direction, dtype):
-    """Scores that climb (or fall) by ~16 log2 units per 32 keys: a running row
-    maximum has to move many times along the row, and the padded rows still take
-    the plain mean of their keys."""
+@pytest.mark.parametrize("D,dtype", [(32, torch.bfloat16), (32, torch.float16), (32, torch.float32),
+                                     (64, torch.bfloat16), (64, torch.float32)],
+                         ids=["d32_bf16", "d32_fp16", "d32_fp32", "d64_bf16", "d64_fp32"])
+def test_prefill_wide_logit_range(direction, D, dtype):
+    """Scores that climb (or fall) by ~16 log2 units per 32 keys.  Fully padded
+    rows then see their keys in several of the reference's 64-wide -1e9 bands
+    (not a plain mean), and a running row maximum has to move along the row."""
     from rl_for_mario_b200.kernels import attn_prefill, device_status
 
-    B, S, Hq, Hkv, D = 3, 192, 8, 2, 32
+    B, S, Hq, Hkv = 3, 192, 8, 2
     g = torch.Generator().manual_seed(11)
-    ramp = torch.arange(S, dtype=torch.float32) * 0.06
+    ramp = torch.arange(S, dtype=torch.float32) * (0.06 * (32 / D) ** 0.5)
     if direction == "falling":
         ramp = ramp.flip(0)
     if dtype == torch.float16:
-        ramp = ramp * 0.25  # fp16 scores stay inside its range at any reference
+        ramp = ramp * 0.25  # fp16 keys stay well inside its range
     q32 = (1.0 + 0.1 * torch.randn(B, S, Hq, D, generator=g)).to(dtype).float()
     k32 = (ramp.view(1, S, 1, 1) * (1.0 + 0.1 * torch.randn(B, S, Hkv, D, generator=g))).to(dtype).float()
     v32 = torch.randn(B, S, Hkv, D, generator=g).to(dtype).float()
