@@ -315,6 +315,7 @@ def run_ours(args):
     if not args.no_decode:
         if world == 1:
             line["decode"] = bench_decode_cfg3(dev, peaks)
+            line["prefill_long"] = bench_prefill_cfg4(dev, peaks)
         line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
@@ -419,6 +420,108 @@ def bench_decode_cfg3(dev, peaks):
                             "algorithmic_bytes_per_launch": kb},
     }
     del cache, model, steps_h
+    torch.cuda.empty_cache()
+    return res
+
+
+PREFILL_LONG_CFG = dict(batch=1024, timesteps=256, hidden=768, layers=12, q_heads=12, kv_heads=4, head_dim=64,
+                        pad_max_timesteps=128)
+
+
+def _attended_pairs(S: int, pads) -> int:
+    """(query, key) pairs the masks allow, summed over samples: a valid row q >= pad
+    sees keys pad..q, a fully padded row q < pad sees keys 0..q."""
+    tot = 0
+    for p in pads:
+        p = int(p)
+        tot += p * (p + 1) // 2 + (S - p) * (S - p + 1) // 2
+    return tot
+
+
+def bench_prefill_cfg4(dev, peaks):
+    """Larger DT prefill: B=1024, 256 timesteps (768 tokens), hidden 768, 12 layers, 12/4 heads, head_dim 64.
+
+    (a) the attention op alone at that shape (RoPE applied in the kernel), timed
+    per launch against the tensor-core roofline; (b) the full DT forward (CNN
+    state encoder, embeddings, 12 blocks with fused RMSNorm + QKV, final norm,
+    action head) in tokens/s."""
+    from rl_for_mario_b200.kernels import attn_prefill, device_status
+    from rl_for_mario_b200.dt_model import DTConfig, MarioDT
+    from oracle import precompute_freqs_cis
+
+    C = PREFILL_LONG_CFG
+    B, T = C["batch"], C["timesteps"]
+    S, Hq, Hkv, D = 3 * T, C["q_heads"], C["kv_heads"], C["head_dim"]
+    g = torch.Generator(device=dev).manual_seed(4)
+    # (a) attention op
+    q = (torch.randn(B, S, Hq, D, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, S, Hkv, D, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, S, Hkv, D, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    pad_t = torch.randint(0, C["pad_max_timesteps"] + 1, (B,), device=dev, generator=g, dtype=torch.int32)
+    pad = (3 * pad_t).to(torch.int32)
+    cos, sin = (t.to(dev) for t in precompute_freqs_cis(D, S))
+    out = torch.empty_like(q)
+    for _ in range(3):
+        attn_prefill(q, k, v, cos, sin, pad, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 10
+    e0.record()
+    for _ in range(n):
+        attn_prefill(q, k, v, cos, sin, pad, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    if device_status() != 0:
+        raise SystemExit("device status error in the long-prefill benchmark")
+    kms = e0.elapsed_time(e1) / n
+    flops = 4 * Hq * D * _attended_pairs(S, pad.cpu().tolist())
+    tflops = flops / (kms * 1e-3) / 1e12
+    byts = _algorithmic_bytes(B, S, Hq, Hkv, D)
+    del q, k, v, out
+    torch.cuda.empty_cache()
+
+    # (b) full model forward
+    torch.manual_seed(4)
+    cfg = DTConfig(hidden_size=C["hidden"], num_hidden_layers=C["layers"], num_attention_heads=Hq,
+                   num_key_value_heads=Hkv, context_len=T, intermediate_size=2048, dropout=0.0)
+    model = MarioDT(cfg).to(dev, torch.bfloat16).eval().fuse_norms()
+    states = torch.randint(0, 256, (B, T) + tuple(cfg.state_shape), device=dev, generator=g, dtype=torch.uint8)
+    actions = torch.randint(0, cfg.act_dim, (B, T), device=dev, generator=g)
+    rtg = torch.rand(B, T, device=dev, generator=g) * 3000.0
+    start = torch.randint(0, cfg.max_ep_len - T, (B, 1), device=dev, generator=g)
+    ts = start + torch.arange(T, device=dev)
+    mask = (torch.arange(T, device=dev)[None, :] >= pad_t[:, None].long()).to(torch.bfloat16)
+
+    def forward():
+        with torch.no_grad():
+            h, _ = model.model(states, actions, rtg, ts, mask)
+            return model.action_head(h[:, -1, 1]).argmax(-1)
+
+    forward()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(2):
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        forward()
+        f1.record()
+        torch.cuda.synchronize()
+        times.append(f0.elapsed_time(f1))
+    fms = min(times)
+    res = {
+        "metric": "DT prefill tokens/s (full forward, 1024 x 768 tokens, hidden 768, 12 layers)", "unit": "tokens/s",
+        "value": B * S / (fms * 1e-3), "ms": fms,
+        "config": {"workload": "1024 x 256 timesteps (768 tokens), hidden 768, 12 layers, 12/4 heads, head_dim 64, "
+                               "FFN 2048, bf16, fused RMSNorm+QKV, synthetic uint8 frames, left pad U{0..128} "
+                               "timesteps, random-init weights"},
+        "attention_kernel": {"kernel": "dt_prefill_long_kernel", "ms": kms, "tokens_per_s": B * S / (kms * 1e-3),
+                             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
+                                          "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"],
+                                          "flops_per_launch": flops,
+                                          "hbm_achieved_gbs": byts / (kms * 1e-3) / 1e9,
+                                          "peak_source": peaks["source"]}},
+    }
+    del model, states
     torch.cuda.empty_cache()
     return res
 

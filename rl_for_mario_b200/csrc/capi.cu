@@ -186,7 +186,10 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
   // Short sequences with head_dim 32 (the DT's 192-token context) use the
   // persistent kernel that keeps a unit's whole K/V in shared memory.
   const bool short_path = (D == 32 && S <= 192);
-  const uint32_t kv_box = short_path ? (uint32_t)((S + 15) & ~15) : 128u;
+  // Longer sequences with head_dim 64: the persistent kernel over pairs of
+  // query tiles with 64-key blocks.
+  const bool long_path = !short_path && D == 64;
+  const uint32_t kv_box = short_path ? (uint32_t)((S + 15) & ~15) : (long_path ? 64u : 128u);
   CUtensorMap mq, mk, mv;
   if ((rc = encode_bshd(&mq, q, bf16, B, S, Hq, D, q_sb, q_ss, q_sh, (uint32_t)R, (uint32_t)PT, "q"))) return rc;
   if ((rc = encode_bshd(&mk, k, bf16, B, S, Hkv, D, k_sb, k_ss, k_sh, 1, kv_box, "k"))) return rc;
@@ -217,6 +220,12 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
     // The persistent kernel stages at most 2048 units' padding per CTA.
     if ((units + grid - 1) / grid > 2048) grid = (units + 2047) / 2048;
     e = dtk::launch_prefill_short_sm100(mq, mk, mv, prm, bf16, units, grid, static_cast<cudaStream_t>(stream));
+  } else if (long_path) {
+    const long long ntiles = (S + PT - 1) / PT;
+    const long long items = (long long)units * ((ntiles + 1) / 2);
+    if (items > 0x7fffffffLL) return fail(DT_ERR_UNSUPPORTED, "dt_attn_prefill: too many query tiles");
+    const int grid = items < g_num_sms[dev] ? (int)items : g_num_sms[dev];
+    e = dtk::launch_prefill_long_sm100(mq, mk, mv, prm, bf16, units, grid, static_cast<cudaStream_t>(stream));
   } else {
     e = dtk::launch_prefill_sm100(mq, mk, mv, prm, D, bf16, units, static_cast<cudaStream_t>(stream));
   }

@@ -30,6 +30,11 @@ cudaError_t launch_prefill_short_sm100(const CUtensorMap& q, const CUtensorMap& 
                                        const PrefillParams& prm, bool bf16, int n_units, int grid,
                                        cudaStream_t stream);
 
+// Persistent two-tile kernel for head_dim 64 with Q/K already rotated (any S).
+cudaError_t launch_prefill_long_sm100(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                                      const PrefillParams& prm, bool bf16, int n_units, int grid,
+                                      cudaStream_t stream);
+
 // Kernel parameters of the paged-cache decode (dt_attn_decode).
 struct DecodeParams {
   const void* q;             // [B, Sn, Hq, D] new queries (pre-RoPE)

@@ -149,3 +149,26 @@ def test_prefill_wide_logit_range(direction, D, dtype):
     out = attn_prefill(*(t.to(dtype).cuda() for t in (q32, k32, v32)), None, None, pad_t.cuda(), apply_rope=False)
     assert device_status() == 0
     _check(out.float().cpu(), ref, dtype)
+
+
+LONG_CASES = [
+    # B, S, Hq, Hkv, D, pads, dtype  (Q/K pre-rotated: the persistent two-tile kernel)
+    (2, 768, 12, 4, 64, [0, 384], torch.bfloat16),
+    (3, 300, 12, 4, 64, "random", torch.bfloat16),
+    (2, 129, 4, 4, 64, [0, 128], torch.bfloat16),
+    (2, 1, 8, 2, 64, None, torch.bfloat16),
+    (3, 100, 8, 2, 64, [0, 50, 99], torch.float16),
+    (2, 513, 16, 2, 64, [0, 200], torch.bfloat16),
+    (4, 256, 12, 4, 64, [0, 1, 255, 256], torch.bfloat16),
+    (1, 1024, 12, 4, 64, [100], torch.bfloat16),
+    (40, 200, 12, 4, 64, "random", torch.bfloat16),
+    (300, 64, 12, 4, 64, "random", torch.bfloat16),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", LONG_CASES,
+                         ids=lambda c: f"B{c[0]}_S{c[1]}_{c[2]}x{c[3]}_D{c[4]}_{str(c[6])[6:]}{'_rp' if c[5] == 'random' else ''}")
+def test_prefill_prerotated_matches_oracle(case):
+    out, ref = _run_case(*case, rope=False)
+    _check(out, ref, case[6])
