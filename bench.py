@@ -441,9 +441,10 @@ def _attended_pairs(S: int, pads) -> int:
 def bench_prefill_cfg4(dev, peaks):
     """Larger DT prefill: B=1024, 256 timesteps (768 tokens), hidden 768, 12 layers, 12/4 heads, head_dim 64.
 
-    (a) the attention op alone at that shape (RoPE applied in the kernel), timed
-    per launch against the tensor-core roofline; (b) the full DT forward (CNN
-    state encoder, embeddings, 12 blocks with fused RMSNorm + QKV, final norm,
+    (a) the attention op alone at that shape, with Q / K rotated upstream as in
+    the model path (the fused RMSNorm + QKV + RoPE epilogue), timed per launch
+    against the tensor-core roofline; (b) the full DT forward (CNN state
+    encoder, embeddings, 12 blocks with fused RMSNorm + QKV + RoPE, final norm,
     action head) in tokens/s."""
     from rl_for_mario_b200.kernels import attn_prefill, device_status
     from rl_for_mario_b200.dt_model import DTConfig, MarioDT
@@ -462,13 +463,13 @@ def bench_prefill_cfg4(dev, peaks):
     cos, sin = (t.to(dev) for t in precompute_freqs_cis(D, S))
     out = torch.empty_like(q)
     for _ in range(3):
-        attn_prefill(q, k, v, cos, sin, pad, out=out)
+        attn_prefill(q, k, v, cos, sin, pad, out=out, apply_rope=False)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = 10
     e0.record()
     for _ in range(n):
-        attn_prefill(q, k, v, cos, sin, pad, out=out)
+        attn_prefill(q, k, v, cos, sin, pad, out=out, apply_rope=False)
     e1.record()
     torch.cuda.synchronize()
     if device_status() != 0:
@@ -514,7 +515,8 @@ def bench_prefill_cfg4(dev, peaks):
         "config": {"workload": "1024 x 256 timesteps (768 tokens), hidden 768, 12 layers, 12/4 heads, head_dim 64, "
                                "FFN 2048, bf16, fused RMSNorm+QKV, synthetic uint8 frames, left pad U{0..128} "
                                "timesteps, random-init weights"},
-        "attention_kernel": {"kernel": "dt_prefill_long_kernel", "ms": kms, "tokens_per_s": B * S / (kms * 1e-3),
+        "attention_kernel": {"kernel": "dt_prefill_long_kernel", "inputs": "q / k rotated upstream", "ms": kms,
+                             "tokens_per_s": B * S / (kms * 1e-3),
                              "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
                                           "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"],
                                           "flops_per_launch": flops,

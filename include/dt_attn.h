@@ -121,6 +121,20 @@ int dt_rmsnorm_qkv(const void* x, int64_t x_row_stride, const void* w_fused, voi
                    int K, int N, float eps, int dtype, void* stream);
 
 /*
+ * dt_rmsnorm_qkv followed, in the same epilogue, by the rotate-half RoPE of
+ * the q and k heads (apply_rotary_pos_emb, model_decision_transformer.py:103-117,
+ * applied at :179-183): columns [0, rope_cols) of y are groups of head_dim
+ * (32 or 64) and row m is rotated with table row (m mod seq_len) of cos / sin
+ * ([>= seq_len, head_dim] fp32, row stride cos_stride, 16-byte aligned).  The
+ * v columns (>= rope_cols) are left as projected.  The result feeds the
+ * attention entry points with apply_rope = 0.
+ */
+int dt_rmsnorm_qkv_rope(const void* x, int64_t x_row_stride, const void* w_fused, void* y, int64_t y_row_stride,
+                        int M, int K, int N, float eps, const float* cos_tab, const float* sin_tab,
+                        int64_t cos_stride, int cos_rows, int seq_len, int rope_cols, int head_dim, int dtype,
+                        void* stream);
+
+/*
  * Synchronises `stream`, then returns and clears the device status word that
  * the kernels of this library write when a bounded wait runs out or a
  * device-side check fails (0 = no error).  Used by tests and debugging.

@@ -40,6 +40,7 @@ SIGNATURES = {
     "dt_kv_write": (_I, [_P, _P, _P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _L, _I, _I, _I, _I, _I,
                          _L, _L, _L, _L, _L, _L, _I, _I, _P]),
     "dt_rmsnorm_qkv": (_I, [_P, _L, _P, _P, _L, _I, _I, _I, _F, _I, _P]),
+    "dt_rmsnorm_qkv_rope": (_I, [_P, _L, _P, _P, _L, _I, _I, _I, _F, _P, _P, _L, _I, _I, _I, _I, _I, _P]),
 }
 
 

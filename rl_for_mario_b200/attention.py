@@ -105,21 +105,25 @@ class FastDTAttention(nn.Module):
             object.__setattr__(self, "_fused_key", key)
         return self._fused_w
 
-    def _project(self, x: Tensor, kd: torch.dtype, raw_input: bool):
+    def _project(self, x: Tensor, kd: torch.dtype, raw_input: bool, pe: Tuple[Tensor, Tensor]):
+        """q, k, v [B, S, H*, D] and whether q / k are already rotated.  With the
+        fused norm on 16-bit inputs one kernel does RMSNorm, the three
+        projections and the RoPE of q / k (rows s of the position tables)."""
         bsz, seq_len, _ = x.shape
         Hq, Hkv, D = self.n_local_heads, self.n_local_kv_heads, self.head_dim
         if raw_input:
             if self._fused_norm is None:
                 raise ValueError("raw_input=True needs set_fused_norm()")
             if x.dtype in (torch.bfloat16, torch.float16) and kd == x.dtype:
-                qkv = kernels.rmsnorm_qkv(x, self._fused_weight(x.dtype), self._fused_norm.eps)
+                qkv = kernels.rmsnorm_qkv(x, self._fused_weight(x.dtype), self._fused_norm.eps,
+                                          rope=(pe[0], pe[1], (Hq + Hkv) * D, D))
                 qkv = qkv.view(bsz, seq_len, Hq + 2 * Hkv, D)
-                return qkv[:, :, :Hq], qkv[:, :, Hq:Hq + Hkv], qkv[:, :, Hq + Hkv:]
+                return qkv[:, :, :Hq], qkv[:, :, Hq:Hq + Hkv], qkv[:, :, Hq + Hkv:], True
             x = self._fused_norm(x)  # fp32 models: exact RMSNorm, then the projections
         xq = self.q_proj(x).view(bsz, seq_len, Hq, D).to(kd)
         xk = self.k_proj(x).view(bsz, seq_len, Hkv, D).to(kd)
         xv = self.v_proj(x).view(bsz, seq_len, Hkv, D).to(kd)
-        return xq, xk, xv
+        return xq, xk, xv, False
 
     # ------------------------------------------------------------------ forward
     def forward(self, x: Tensor, position_embeddings: Tuple[Tensor, Tensor],
@@ -129,8 +133,9 @@ class FastDTAttention(nn.Module):
             raise ValueError("FastDTAttention runs on CUDA only (no CPU path)")
         bsz, seq_len, _ = x.shape
         kd = self._kernel_dtype(x)
-        xq, xk, xv = self._project(x, kd, raw_input)
         cos, sin = position_embeddings
+        xq, xk, xv, rotated = self._project(x, kd, raw_input, (cos, sin))
+        rope = not rotated
 
         if (isinstance(past_key_value, LayerKV) and past_key_value.length == 0 and seq_len > 1 and self.flash
                 and attention_mask is None):
@@ -142,18 +147,18 @@ class FastDTAttention(nn.Module):
                 raise TypeError(f"cache dtype {layer.k_pages.dtype} differs from compute dtype {kd}")
             if seq_len > layer.capacity:
                 raise ValueError(f"cache full: {seq_len} > capacity {layer.capacity}")
-            out = kernels.attn_prefill(xq, xk, xv, cos, sin, None)
-            kernels.kv_write(xk, xv, layer, cos, sin)
+            out = kernels.attn_prefill(xq, xk, xv, cos, sin, None, apply_rope=rope)
+            kernels.kv_write(xk, xv, layer, cos, sin, apply_rope=rope)
             layer.advance(seq_len)
             past_kv = layer if use_cache else None
         elif self.flash and seq_len > 1 and past_key_value is None:
-            out = kernels.attn_prefill(xq, xk, xv, cos, sin, self._pad_len(attention_mask, seq_len))
+            out = kernels.attn_prefill(xq, xk, xv, cos, sin, self._pad_len(attention_mask, seq_len), apply_rope=rope)
             past_kv = None
             if use_cache:
                 kc = torch.empty(bsz, self.n_local_kv_heads, seq_len, self.head_dim, dtype=kd, device=x.device)
                 vc = torch.empty_like(kc)
                 layer = dense_layer(kc, vc, 0)
-                kernels.kv_write(xk, xv, layer, cos, sin)
+                kernels.kv_write(xk, xv, layer, cos, sin, apply_rope=rope)
                 past_kv = (kc, vc)
         else:
             if isinstance(past_key_value, LayerKV):
@@ -161,7 +166,8 @@ class FastDTAttention(nn.Module):
                 if layer.k_pages.dtype != kd:
                     raise TypeError(f"cache dtype {layer.k_pages.dtype} differs from compute dtype {kd}")
                 kv_len = layer.length + seq_len
-                out = kernels.attn_decode(xq, xk, xv, layer, cos, sin, self._pad_len(attention_mask, kv_len))
+                out = kernels.attn_decode(xq, xk, xv, layer, cos, sin, self._pad_len(attention_mask, kv_len),
+                                          apply_rope=rope)
                 layer.advance(seq_len)
                 past_kv = layer if use_cache else None
             else:
@@ -175,7 +181,7 @@ class FastDTAttention(nn.Module):
                     vc[:, :, :L].copy_(past_key_value[1])
                 layer = dense_layer(kc, vc, L)
                 out = kernels.attn_decode(xq, xk, xv, layer, cos, sin,
-                                          self._pad_len(attention_mask, L + seq_len))
+                                          self._pad_len(attention_mask, L + seq_len), apply_rope=rope)
                 past_kv = (kc, vc) if use_cache else None
 
         out = out.reshape(bsz, seq_len, -1).to(x.dtype)

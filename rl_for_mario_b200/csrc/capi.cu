@@ -343,9 +343,11 @@ int encode_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uin
 }
 }  // namespace
 
-extern "C" int dt_rmsnorm_qkv(const void* x, int64_t x_row_stride, const void* w_fused, void* y,
-                              int64_t y_row_stride, int M, int K, int N, float eps, int dtype, void* stream) {
-  const char* fn = "dt_rmsnorm_qkv";
+namespace {
+int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const void* w_fused, void* y,
+                     int64_t y_row_stride, int M, int K, int N, float eps, const float* cos_tab, const float* sin_tab,
+                     int64_t cos_stride, int cos_rows, int seq_len, int rope_cols, int head_dim, int dtype,
+                     void* stream) {
   if (!x || !w_fused || !y) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
   if (M < 1 || K < 1 || N < 1) return fail(DT_ERR_INVALID, "%s: sizes must be positive", fn);
   if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
@@ -367,7 +369,34 @@ extern "C" int dt_rmsnorm_qkv(const void* x, int64_t x_row_stride, const void* w
   if ((rc = encode_2d(&mw, w_fused, bf16, (uint64_t)K, (uint64_t)N, (uint64_t)K, 64, (uint32_t)nsub, "w"))) return rc;
   dtk::RmsQkvParams p;
   p.y = y; p.status = status; p.y_stride = y_row_stride; p.M = M; p.K = K; p.N = N; p.bf16 = bf16 ? 1 : 0; p.eps = eps;
+  p.cos = cos_tab; p.sin = sin_tab; p.rope_cols = rope_cols; p.head_dim = head_dim; p.seq_len = seq_len;
+  p.cs_stride = (int)cos_stride;
   cudaError_t e = dtk::launch_rmsnorm_qkv_sm100(mx, mw, p, ncta, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "dt_rmsnorm_qkv launch");
+  if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
   return DT_OK;
+}
+}  // namespace
+
+extern "C" int dt_rmsnorm_qkv(const void* x, int64_t x_row_stride, const void* w_fused, void* y,
+                              int64_t y_row_stride, int M, int K, int N, float eps, int dtype, void* stream) {
+  return rmsnorm_qkv_impl("dt_rmsnorm_qkv", x, x_row_stride, w_fused, y, y_row_stride, M, K, N, eps, nullptr,
+                          nullptr, 0, 0, 1, 0, 0, dtype, stream);
+}
+
+extern "C" int dt_rmsnorm_qkv_rope(const void* x, int64_t x_row_stride, const void* w_fused, void* y,
+                                   int64_t y_row_stride, int M, int K, int N, float eps, const float* cos_tab,
+                                   const float* sin_tab, int64_t cos_stride, int cos_rows, int seq_len,
+                                   int rope_cols, int head_dim, int dtype, void* stream) {
+  const char* fn = "dt_rmsnorm_qkv_rope";
+  if (!cos_tab || !sin_tab) return fail(DT_ERR_INVALID, "%s: null cos / sin", fn);
+  if (head_dim != 32 && head_dim != 64) return fail(DT_ERR_UNSUPPORTED, "%s: head_dim %d not in {32, 64}", fn, head_dim);
+  if (rope_cols < 0 || rope_cols > N || rope_cols % head_dim)
+    return fail(DT_ERR_INVALID, "%s: rope_cols must be a multiple of head_dim within N", fn);
+  if (seq_len < 1 || M % seq_len) return fail(DT_ERR_INVALID, "%s: M must be a multiple of seq_len", fn);
+  if (cos_rows < seq_len) return fail(DT_ERR_INVALID, "%s: cos / sin have %d rows < seq_len %d", fn, cos_rows, seq_len);
+  if (cos_stride < head_dim || cos_stride % 4 || cos_stride > 0x7fffffffLL || !aligned16(cos_tab) ||
+      !aligned16(sin_tab))
+    return fail(DT_ERR_INVALID, "%s: cos / sin must be 16-byte aligned with row stride >= head_dim, %% 4", fn);
+  return rmsnorm_qkv_impl(fn, x, x_row_stride, w_fused, y, y_row_stride, M, K, N, eps, cos_tab, sin_tab, cos_stride,
+                          cos_rows, seq_len, rope_cols, head_dim, dtype, stream);
 }

@@ -96,8 +96,11 @@ cudaError_t launch_decode_f32(const DecodeParams& prm, int D, int B, cudaStream_
 struct RmsQkvParams {
   void* y;            // [M, N] output rows, row stride y_stride elements
   int* status;
+  const float* cos;   // RoPE tables (rope_cols > 0): row (m mod seq_len), stride cs_stride
+  const float* sin;
   long long y_stride;
   int M, K, N, bf16;
+  int rope_cols, head_dim, seq_len, cs_stride;  // rope_cols = 0: no rotation
   float eps;
 };
 

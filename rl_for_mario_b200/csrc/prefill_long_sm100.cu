@@ -197,6 +197,15 @@ __global__ void __launch_bounds__(kLongThreads, 1)
     tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
+  // Rows q_rows..127 of the Q buffers are never loaded (R * PT < 128 when R
+  // does not divide 128): zero them once so their scores stay finite.
+  for (int e = tid; e < 2 * SH::NQB * (128 - q_rows) * (SH::ROWB / 16); e += kLongThreads) {
+    const int per = (128 - q_rows) * (SH::ROWB / 16);
+    const int buf = e / per, rem = e - buf * per;
+    *reinterpret_cast<uint4*>(q_s + buf * SH::Q_BYTES + (q_rows + rem / (SH::ROWB / 16)) * SH::ROWB +
+                              (rem % (SH::ROWB / 16)) * 16) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -250,14 +259,21 @@ __global__ void __launch_bounds__(kLongThreads, 1)
             if (uses > 0) mbar_wait(&q_full[s * SH::NQB + j], (uses - 1) & 1, nullptr, nullptr);
           }
       }
-    } else if ((warp == 1 || warp == 2) && lane == 0) {
+    } else if (warp == 1 || warp == 2) {
       // ------------------------------------------------------------ MMA issuers
-      // One thread per slot (warps 1 and 2 sit on different SM sub-partitions,
-      // so the two slots' MMAs issue in parallel).  They share only the K/V
-      // ring: kv_empty completes when both have released a block, by an MMA
-      // commit after their last use of it or by a plain arrive when their
-      // slot does not use it.
-      const int s = warp - 1;
+      // One warp per slot (warps 1 and 2 sit on different SM sub-partitions,
+      // so the two slots' MMAs issue in parallel).  The whole warp runs the
+      // loop with warp-uniform values, lane 0 waits and issues.  The issuers
+      // share only the K/V ring: kv_empty completes when both have released a
+      // block, by an MMA commit after their last use of it or by a plain
+      // arrive when their slot does not use it.
+      const int s = __shfl_sync(0xffffffffu, warp - 1, 0);
+      const bool leader = lane == 0;
+      auto wait1 = [&](uint64_t* bar, uint32_t parity) -> bool {
+        int w = 1;
+        if (leader) w = mbar_wait(bar, parity, abort_flag, prm.status) ? 1 : 0;
+        return __shfl_sync(0xffffffffu, w, 0) != 0;
+      };
       // With RoPE inputs the MMAs wait for the rotated tiles.
       uint64_t* const q_avail = prm.rope ? q_ready : q_full;
       uint64_t* const kv_avail = prm.rope ? kv_ready : kv_full;
@@ -277,53 +293,50 @@ __global__ void __launch_bounds__(kLongThreads, 1)
         const bool act = (s ? it.tile[1] : it.tile[0]) >= 0;
         const int first = s ? it.first[1] : it.first[0], last = s ? it.last[1] : it.last[0];
         const int qb = qc % SH::NQB;
-        if (act && !(ok = mbar_wait(&q_avail[s * SH::NQB + qb], (qc / SH::NQB) & 1, abort_flag, prm.status))) break;
+        if (act && !(ok = wait1(&q_avail[s * SH::NQB + qb], (qc / SH::NQB) & 1))) break;
         const uint64_t qd = q_desc0 + (uint64_t)((qb * SH::Q_BYTES) >> 4);
         for (int j = 0; j <= it.nblocks && ok; ++j) {
           const int st = (kvc + j) % SH::NKV;
           const int stp = (kvc + j + SH::NKV - 1) % SH::NKV;  // stage of block j - 1
-          if (j < it.nblocks && !(ok = mbar_wait(&kv_avail[st], ((kvc + j) / SH::NKV) & 1, abort_flag, prm.status)))
-            break;
+          if (j < it.nblocks && !(ok = wait1(&kv_avail[st], ((kvc + j) / SH::NKV) & 1))) break;
           if (act && j >= first && j <= last) {
             // S = Q K^T of block j into the slot's next S buffer.  That buffer
             // last held the P of two blocks back, whose P V is already issued.
-            tc_fence_after();
             const int sb = sc & 1;
             const uint64_t kd = k_desc0 + (uint64_t)((st * SH::KV_BYTES) >> 4);
+            if (leader) {
+              tc_fence_after();
 #pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-              umma_f16_ss(t_s0 + (uint32_t)(sb * kBK), qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
-            umma_commit(&s_full[s * 2 + sb]);
-            ++sc;
-            if (j == last) {
-              umma_commit(&q_empty[s * SH::NQB + qb]);
-              ++qc;
+              for (int kk = 0; kk < D / 16; ++kk)
+                umma_f16_ss(t_s0 + (uint32_t)(sb * kBK), qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+              umma_commit(&s_full[s * 2 + sb]);
+              if (j == last) umma_commit(&q_empty[s * SH::NQB + qb]);
             }
+            ++sc;
+            if (j == last) ++qc;
           }
           if (act && j - 1 >= first && j - 1 <= last) {
             // O += P V of block j - 1.
             const int pb = pc & 1;
-            if (!(ok = mbar_wait(&p_full[s * 2 + pb], (pc >> 1) & 1, abort_flag, prm.status))) break;
+            if (!(ok = wait1(&p_full[s * 2 + pb], (pc >> 1) & 1))) break;
             ++pc;
             const int ob = oc & 1;
-            if (j - 1 == first &&
-                !(ok = mbar_wait(&o_empty[s * 2 + ob], ((oc >> 1) & 1) ^ 1, abort_flag, prm.status)))
-              break;
-            tc_fence_after();
+            if (j - 1 == first && !(ok = wait1(&o_empty[s * 2 + ob], ((oc >> 1) & 1) ^ 1))) break;
             const uint64_t vd = v_desc0 + (uint64_t)((stp * SH::KV_BYTES) >> 4);
             const uint32_t t_p = t_s0 + (uint32_t)(pb * kBK);
             const uint32_t acc0 = (j - 1 > first) ? 1u : 0u;
+            if (leader) {
+              tc_fence_after();
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)  // 16 keys = 16 rows of 128 bytes per K step
-              umma_f16_ts(t_o0 + (uint32_t)(ob * D), t_p + kk * 8, vd + (uint64_t)(kk * 16 * SH::ROWB >> 4), idesc_pv,
-                          kk > 0 ? 1u : acc0);
-            umma_commit(&pv_done[s]);
-            if (j - 1 == last) {
-              umma_commit(&o_full[s * 2 + ob]);
-              ++oc;
+              for (int kk = 0; kk < kBK / 16; ++kk)  // 16 keys = 16 rows of 128 bytes per K step
+                umma_f16_ts(t_o0 + (uint32_t)(ob * D), t_p + kk * 8, vd + (uint64_t)(kk * 16 * SH::ROWB >> 4),
+                            idesc_pv, kk > 0 ? 1u : acc0);
+              umma_commit(&pv_done[s]);
+              if (j - 1 == last) umma_commit(&o_full[s * 2 + ob]);
             }
+            if (j - 1 == last) ++oc;
           }
-          if (j >= 1) {
+          if (j >= 1 && leader) {
             // Release block j - 1 (its kv_full was waited at step j - 1).
             if (act && j - 1 >= first && j - 1 <= last)
               umma_commit(&kv_empty[stp]);
@@ -333,8 +346,11 @@ __global__ void __launch_bounds__(kLongThreads, 1)
         }
         kvc += it.nblocks;
       }
-      umma_commit(drain + s);
-      mbar_wait(drain + s, 0, nullptr, nullptr);
+      if (leader) {
+        umma_commit(drain + s);
+        mbar_wait(drain + s, 0, nullptr, nullptr);
+      }
+      __syncwarp();
     } else if (warp == 3 && prm.rope) {
       // ------------------------------------------------------------ RoPE
       // Follows the producer's order: each item's Q tiles, then its K blocks.
@@ -441,10 +457,13 @@ __global__ void __launch_bounds__(kLongThreads, 1)
       const int first = s ? it.first[1] : it.first[0], last = s ? it.last[1] : it.last[0];
       const int pos = tile * PT + rowpos;
       const bool valid_row = r < q_rows && pos < S;
-      const bool padded = pos < it.pad;
-      const int lo = padded ? 0 : it.pad;
-      const int hi = valid_row ? pos : -1;
-      const bool warp_band = __any_sync(0xffffffffu, padded && valid_row);
+      const bool padded = valid_row && pos < it.pad;
+      // Rows without a query (past the packed heads or the sequence end) are
+      // never stored: they take every key so that they never force the
+      // masked path on their warp.
+      const int lo = !valid_row ? -(1 << 30) : (padded ? 0 : it.pad);
+      const int hi = valid_row ? pos : (1 << 30);
+      const bool warp_band = __any_sync(0xffffffffu, padded);
       const RowScore rs(padded, c2, sd64);
       const int ob = oc & 1;
       float m = -INFINITY, l0 = 0.f, l1 = 0.f;

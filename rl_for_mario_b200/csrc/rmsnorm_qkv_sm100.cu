@@ -16,6 +16,9 @@
 // and run the epilogue (TMEM -> scale -> bf16 -> HBM).  Output row layout is
 // the fused [q | k | v] of the projections: a [tokens, (Hq + 2 Hkv) * D] row
 // is the [B, S, Hq + 2 Hkv, D] view the attention kernels take directly.
+// With rope_cols > 0 the epilogue also applies the rotate-half RoPE to the q
+// and k heads (apply_rotary_pos_emb, :103-117), so the attention kernels can
+// take them pre-rotated.
 #include "dt_common.cuh"
 #include "dt_internal.h"
 
@@ -41,6 +44,27 @@ struct GemmShape {
 };
 
 }  // namespace
+
+// Rotate-half RoPE of one head held in v[lo0, lo0 + 2 HALF):
+//   y[d] = x[d] cos[d] - x[d + HALF] sin[d],  y[d + HALF] = x[d + HALF] cos[d + HALF] + x[d] sin[d + HALF]
+template <int HALF>
+__device__ __forceinline__ void rope_pairs(float (&v)[64], int lo0, const float* crow, const float* srow) {
+#pragma unroll
+  for (int d = 0; d < HALF; d += 4) {
+    const float4 ca = *reinterpret_cast<const float4*>(crow + d);
+    const float4 cb = *reinterpret_cast<const float4*>(crow + d + HALF);
+    const float4 sa = *reinterpret_cast<const float4*>(srow + d);
+    const float4 sb = *reinterpret_cast<const float4*>(srow + d + HALF);
+    const float cav[4] = {ca.x, ca.y, ca.z, ca.w}, cbv[4] = {cb.x, cb.y, cb.z, cb.w};
+    const float sav[4] = {sa.x, sa.y, sa.z, sa.w}, sbv[4] = {sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float x0 = v[lo0 + d + e], x1 = v[lo0 + d + e + HALF];
+      v[lo0 + d + e] = x0 * cav[e] - x1 * sav[e];
+      v[lo0 + d + e + HALF] = x1 * cbv[e] + x0 * sbv[e];
+    }
+  }
+}
 
 template <int NCTA>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -154,25 +178,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const float rs = rsqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / (float)p.K + p.eps);
       const int row_g = m0 + r;
-      for (int c = 0; c < NCTA; c += 32) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + c, v);
+      // RoPE table row of this token (rows are [batch, seq_len] flattened).
+      const int pos = p.rope_cols > 0 ? row_g % p.seq_len : 0;
+      const float* crow = p.cos + (size_t)pos * p.cs_stride;
+      const float* srow = p.sin + (size_t)pos * p.cs_stride;
+      // 64 columns at a time: one head of 64 or two of 32, both halves of
+      // every rotate-half pair in registers.
+      for (int c = 0; c < NCTA; c += 64) {
+        float v[64];
+        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + c, *reinterpret_cast<float(*)[32]>(&v[0]));
+        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + c + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] *= rs;
+        if (n0 + c < p.rope_cols && row_g < p.M) {
+          if (p.head_dim == 64)
+            rope_pairs<32>(v, 0, crow, srow);
+          else {
+            rope_pairs<16>(v, 0, crow, srow);
+            rope_pairs<16>(v, 32, crow, srow);
+          }
+        }
         if (row_g < p.M) {
           uint8_t* yrow = reinterpret_cast<uint8_t*>(p.y) + ((size_t)row_g * p.y_stride + n0 + c) * 2;
 #pragma unroll
-          for (int c8 = 0; c8 < 32; c8 += 8) {
+          for (int c8 = 0; c8 < 64; c8 += 8) {
             if (n0 + c + c8 + 8 > p.N) break;
             uint4 o;
             if (p.bf16) {
-              o.x = Elem<true>::from_f2(v[c8] * rs, v[c8 + 1] * rs);
-              o.y = Elem<true>::from_f2(v[c8 + 2] * rs, v[c8 + 3] * rs);
-              o.z = Elem<true>::from_f2(v[c8 + 4] * rs, v[c8 + 5] * rs);
-              o.w = Elem<true>::from_f2(v[c8 + 6] * rs, v[c8 + 7] * rs);
+              o.x = Elem<true>::from_f2(v[c8], v[c8 + 1]);
+              o.y = Elem<true>::from_f2(v[c8 + 2], v[c8 + 3]);
+              o.z = Elem<true>::from_f2(v[c8 + 4], v[c8 + 5]);
+              o.w = Elem<true>::from_f2(v[c8 + 6], v[c8 + 7]);
             } else {
-              o.x = Elem<false>::from_f2(v[c8] * rs, v[c8 + 1] * rs);
-              o.y = Elem<false>::from_f2(v[c8 + 2] * rs, v[c8 + 3] * rs);
-              o.z = Elem<false>::from_f2(v[c8 + 4] * rs, v[c8 + 5] * rs);
-              o.w = Elem<false>::from_f2(v[c8 + 6] * rs, v[c8 + 7] * rs);
+              o.x = Elem<false>::from_f2(v[c8], v[c8 + 1]);
+              o.y = Elem<false>::from_f2(v[c8 + 2], v[c8 + 3]);
+              o.z = Elem<false>::from_f2(v[c8 + 4], v[c8 + 5]);
+              o.w = Elem<false>::from_f2(v[c8 + 6], v[c8 + 7]);
             }
             *reinterpret_cast<uint4*>(yrow + c8 * 2) = o;
           }

@@ -6,7 +6,7 @@ library itself never allocates), and launches on torch's current CUDA stream.
 from __future__ import annotations
 
 import math
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
 
@@ -189,12 +189,18 @@ def fold_norm_weight(w_q: Tensor, w_k: Tensor, w_v: Tensor, w_norm: Tensor, dtyp
     return w.to(dtype).contiguous()
 
 
-def rmsnorm_qkv(x: Tensor, w_fused: Tensor, eps: float, out: Optional[Tensor] = None) -> Tensor:
+def rmsnorm_qkv(x: Tensor, w_fused: Tensor, eps: float, out: Optional[Tensor] = None,
+                rope: Optional[Tuple[Tensor, Tensor, int, int]] = None) -> Tensor:
     """y = RMSNorm(x) @ [Wq; Wk; Wv]^T with the norm weight folded into ``w_fused`` [N, K].
 
     x [..., K] bf16/fp16 (last dim contiguous) -> y [..., N] (the fused q|k|v rows).
+    ``rope = (cos, sin, rope_cols, head_dim)`` also rotates the first rope_cols
+    columns (the q and k heads) in the epilogue; x is then [B, S, K] and row
+    (b, s) uses table row s.
     """
     _require_cuda(x, w_fused, out)
+    if rope is not None:
+        _require_cuda(rope[0], rope[1])
     K = x.shape[-1]
     N = w_fused.shape[0]
     if w_fused.shape[1] != K or w_fused.dtype != x.dtype or not w_fused.is_contiguous():
@@ -206,7 +212,17 @@ def rmsnorm_qkv(x: Tensor, w_fused: Tensor, eps: float, out: Optional[Tensor] = 
     if out is None:
         out = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
     o2 = out.view(-1, N)
-    rc = _lib.load().dt_rmsnorm_qkv(_ptr(x2), x2.stride(0), _ptr(w_fused), _ptr(o2), o2.stride(0), M, K, N,
-                                    float(eps), _dtype_code(x), _stream_ptr(x.device))
-    _lib.check("dt_rmsnorm_qkv", rc)
+    if rope is None:
+        rc = _lib.load().dt_rmsnorm_qkv(_ptr(x2), x2.stride(0), _ptr(w_fused), _ptr(o2), o2.stride(0), M, K, N,
+                                        float(eps), _dtype_code(x), _stream_ptr(x.device))
+        _lib.check("dt_rmsnorm_qkv", rc)
+        return out
+    if x.dim() != 3:
+        raise ValueError("rmsnorm_qkv with rope needs x of shape [B, S, K]")
+    cos, sin = _prep_tables(rope[0], rope[1])
+    rope_cols, head_dim = int(rope[2]), int(rope[3])
+    rc = _lib.load().dt_rmsnorm_qkv_rope(_ptr(x2), x2.stride(0), _ptr(w_fused), _ptr(o2), o2.stride(0), M, K, N,
+                                         float(eps), _ptr(cos), _ptr(sin), cos.stride(0), cos.shape[0], x.shape[1],
+                                         rope_cols, head_dim, _dtype_code(x), _stream_ptr(x.device))
+    _lib.check("dt_rmsnorm_qkv_rope", rc)
     return out

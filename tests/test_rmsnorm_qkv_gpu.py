@@ -44,3 +44,53 @@ def test_fused_block_matches_unfused_block():
         out, _ = blk(x, (cos, sin), attention_mask=mask)
     err = (out.float() - ref.float()).abs().max().item()
     assert err < 6e-2, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,S,K,Hq,Hkv,D", [(2, 96, 256, 8, 2, 32), (3, 50, 768, 12, 4, 64), (1, 7, 128, 4, 4, 32),
+                                            (2, 130, 512, 8, 8, 64)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rmsnorm_qkv_rope_matches_reference(B, S, K, Hq, Hkv, D, dtype):
+    """RMSNorm -> q/k/v projections -> rotate-half RoPE of q and k, fused in one kernel."""
+    from oracle import apply_rotary_pos_emb, precompute_freqs_cis
+    from rl_for_mario_b200.kernels import device_status, fold_norm_weight, rmsnorm_qkv
+
+    g = torch.Generator().manual_seed(B * S + K + D)
+    x = (torch.randn(B, S, K, generator=g) * 2).to(dtype)
+    wn = 1 + 0.1 * torch.randn(K, generator=g)
+    wq, wk, wv = (torch.randn(h * D, K, generator=g) / K ** 0.5 for h in (Hq, Hkv, Hkv))
+    wf = fold_norm_weight(wq, wk, wv, wn, dtype).cuda()
+    cos, sin = precompute_freqs_cis(D, S + 5)
+    y = rmsnorm_qkv(x.cuda(), wf, 1e-5, rope=(cos[:S].cuda(), sin[:S].cuda(), (Hq + Hkv) * D, D))
+    assert device_status() == 0
+    xn = rmsnorm_ref(x.float(), wn)
+    q = (xn @ wq.t()).view(B, S, Hq, D)
+    k = (xn @ wk.t()).view(B, S, Hkv, D)
+    v = (xn @ wv.t()).view(B, S, Hkv, D)
+    q, k = apply_rotary_pos_emb(q, k, cos[:S], sin[:S])
+    ref = torch.cat([q, k, v], dim=2).reshape(B, S, -1)
+    err = (y.float().cpu() - ref).abs()
+    tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
+    assert (err <= tol + tol * ref.abs()).all(), f"max err {err.max().item():.3e}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("hidden,heads,kv_heads,S", [(256, 8, 2, 96), (768, 12, 4, 300)])
+def test_fused_block_with_rope_epilogue_matches_unfused_block(hidden, heads, kv_heads, S):
+    """A block whose RMSNorm + QKV + RoPE run in one kernel and whose attention
+    takes pre-rotated q / k (short and long prefill kernels) equals the unfused block."""
+    from rl_for_mario_b200.dt_model import DTConfig, DTBlock, rope_tables
+
+    cfg = DTConfig(hidden_size=hidden, num_attention_heads=heads, num_key_value_heads=kv_heads,
+                   context_len=(S + 2) // 3, dropout=0.0)
+    torch.manual_seed(1)
+    blk = DTBlock(cfg).cuda().to(torch.bfloat16).eval()
+    x = torch.randn(3, S, hidden, device="cuda").to(torch.bfloat16)
+    cos, sin = (t.cuda() for t in rope_tables(hidden // heads, S, 1e4))
+    mask = (torch.arange(S, device="cuda")[None] >= torch.tensor([0, 5, S // 2], device="cuda")[:, None]).float()
+    with torch.no_grad():
+        ref, _ = blk(x, (cos, sin), attention_mask=mask)
+        blk.fuse_norm(True)
+        out, _ = blk(x, (cos, sin), attention_mask=mask)
+    err = (out.float() - ref.float()).abs().max().item()
+    assert err < 6e-2, err
