@@ -285,6 +285,7 @@ int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o,
   p.vn_sb = vn_sb; p.vn_ss = vn_ss; p.vn_sh = vn_sh; p.o_sb = o_sb; p.o_ss = o_ss; p.o_sh = o_sh;
   p.cs_stride = (int)cos_stride; p.rope = apply_rope ? 1 : 0; p.rope_abs = rope_abs ? 1 : 0; p.cos_rows = cos_rows;
   p.Sn = Sn; p.Hkv = Hkv; p.R = Hq / Hkv; p.page_size = page_size; p.max_pages = max_pages; p.num_pages = num_pages;
+  p.o_pairs = ((reinterpret_cast<uintptr_t>(o) & 3u) == 0 && o_sb % 2 == 0 && o_ss % 2 == 0 && o_sh % 2 == 0) ? 1 : 0;
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   p.scale_log2 = sc * 1.4426950408889634f;
   p.scale_div64 = sc / 64.f;

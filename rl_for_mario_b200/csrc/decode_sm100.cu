@@ -13,7 +13,11 @@
 // KMAX keys; each warp takes a quarter of the keys of a block and runs the
 // R x Sn query rows (<= 16 per row group) against them with mma.sync
 // m16n8k16 (bf16/fp16 in, fp32 accumulate) and an online softmax; the four
-// partial (max, sum, O) are merged through shared memory (split-K).
+// partial (max, sum, O) are merged through shared memory (split-K).  The
+// copies of the cached prefix of the first block are issued before the new
+// tokens are rotated and appended, and (for up to 16 new tokens) the new rows
+// reach shared memory straight from registers, so a CTA waits for one round
+// trip to HBM after reading its block table.
 //
 // Cache layout: k_pages / v_pages [num_pages, Hkv, page_size, D], a page
 // holding page_size consecutive positions of one KV head contiguously;
@@ -31,6 +35,7 @@ namespace {
 constexpr int kDecThreads = 128;
 constexpr int kDecWarps = 4;
 constexpr int kKMax = 256;  // keys staged per block
+constexpr int kSnSmem = 16;  // new tokens staged from registers (more: re-read from the cache)
 
 template <int D>
 struct DecShape {
@@ -39,9 +44,14 @@ struct DecShape {
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + kKMax * ROWB;
   static constexpr int OFF_Q = OFF_V + kKMax * ROWB;  // 16 rows
-  static constexpr int OFF_RED = OFF_Q + 16 * ROWB;   // [warps][16][D + 2] floats
+  static constexpr int OFF_KN = OFF_Q + 16 * ROWB;    // new keys (rotated), kSnSmem rows
+  static constexpr int OFF_VN = OFF_KN + kSnSmem * ROWB;
+  static constexpr int SMEM = OFF_VN + kSnSmem * ROWB;
+  // Split-K partials [warps][16][D + 2] floats, over the K rows once a row
+  // group's blocks are consumed.
+  static constexpr int OFF_RED = OFF_K;
   static constexpr int RED_STRIDE = D + 2;
-  static constexpr int SMEM = OFF_RED + kDecWarps * 16 * RED_STRIDE * 4;
+  static_assert((kDecWarps * 16 * RED_STRIDE + kDecWarps * 16) * 4 <= kKMax * ROWB, "partials fit over the K rows");
 };
 
 // Swizzled byte offset of 16-byte chunk c of row r (64-byte rows: XOR with
@@ -128,7 +138,10 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
   uint8_t* ks = smem + SH::OFF_K;
   uint8_t* vs = smem + SH::OFF_V;
   uint8_t* qs = smem + SH::OFF_Q;
+  uint8_t* kns = smem + SH::OFF_KN;
+  uint8_t* vns = smem + SH::OFF_VN;
   float* red = reinterpret_cast<float*>(smem + SH::OFF_RED);
+  const bool new_in_smem = Sn <= kSnSmem;
   const size_t page_stride = (size_t)p.Hkv * p.page_size * D;  // elements per page
   auto cache_off = [&](int pos) -> size_t {
     return (size_t)bt[pos / p.page_size] * page_stride + ((size_t)g * p.page_size + pos % p.page_size) * D;
@@ -139,6 +152,29 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
   auto sin_row = [&](int i) -> const float* {
     return p.sin + (size_t)(p.rope_abs ? L + i : i) * p.cs_stride;
   };
+
+  // Cached positions [kb, min(kb + nk, L)) of a block: 16-byte copies, page
+  // by page (a page holds its positions of one KV head contiguously).
+  auto stage_prefix = [&](int kb, int nk) {
+    const int pend = kb + max(0, min(nk, L - kb));  // one past the last cached position
+    for (int pos0 = kb; pos0 < pend;) {
+      const int pg = pos0 / p.page_size;
+      const int pos1 = min(pend, (pg + 1) * p.page_size);
+      const size_t base = cache_off(pos0);
+      const T* ksrc = reinterpret_cast<const T*>(p.k_pages) + base;
+      const T* vsrc = reinterpret_cast<const T*>(p.v_pages) + base;
+      const int key0 = pos0 - kb;
+      for (int e = tid; e < (pos1 - pos0) * SH::CH; e += kDecThreads) {
+        const int key = key0 + e / SH::CH, c = e % SH::CH;
+        cp_async16(smem_u32(ks + dswz<D>(key, c)), ksrc + (size_t)e * 8);
+        cp_async16(smem_u32(vs + dswz<D>(key, c)), vsrc + (size_t)e * 8);
+      }
+      pos0 = pos1;
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  // The first block's prefix is in flight while the new tokens are processed.
+  stage_prefix(0, min(kKMax, kv_len));
 
   // ---- append: rotate the new keys, write new K/V into the paged cache.
   for (int e = tid; e < Sn * (D / 2); e += kDecThreads) {
@@ -163,6 +199,12 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
     kc[d + D / 2] = (T)k1;
     vc[d] = vn[d];
     vc[d + D / 2] = vn[d + D / 2];
+    if (new_in_smem) {
+      reinterpret_cast<T*>(kns + dswz<D>(i, d / 8))[d % 8] = (T)k0;
+      reinterpret_cast<T*>(kns + dswz<D>(i, (d + D / 2) / 8))[(d + D / 2) % 8] = (T)k1;
+      reinterpret_cast<T*>(vns + dswz<D>(i, d / 8))[d % 8] = vn[d];
+      reinterpret_cast<T*>(vns + dswz<D>(i, (d + D / 2) / 8))[(d + D / 2) % 8] = vn[d + D / 2];
+    }
   }
   // ---- queries: rows r = i * R + h (i < Sn), rotated, into shared memory.
   const int nrows = Sn * R;
@@ -216,9 +258,11 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
       const bool valid = row < nrows;
       const int i = valid ? row / R : 0;
       rpos[k] = L + i;  // absolute position of this query
-      rpad[k] = rpos[k] < pad;
-      rlo[k] = rpad[k] ? 0 : pad;
-      rhi[k] = valid ? rpos[k] : -1;
+      rpad[k] = valid && rpos[k] < pad;
+      // Rows past the query rows are never stored: they take every key so
+      // that they never force the masked path.
+      rlo[k] = !valid ? -(1 << 30) : (rpad[k] ? 0 : pad);
+      rhi[k] = valid ? rpos[k] : (1 << 30);
     }
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
     float oacc[D / 8][4];
@@ -227,13 +271,28 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
 
     for (int kb = 0; kb < kv_len; kb += kKMax) {
       const int nk = min(kKMax, kv_len - kb);
-      // ---- stage keys [kb, kb + nk) of K and V (16-byte cp.async, swizzled rows).
-      if (rg > 0 || kb > 0) __syncthreads();  // previous block fully consumed
-      for (int e = tid; e < nk * SH::CH; e += kDecThreads) {
-        const int key = e / SH::CH, c = e - key * SH::CH;
-        const size_t off = cache_off(kb + key) + (size_t)c * 8;
-        cp_async16(smem_u32(ks + dswz<D>(key, c)), reinterpret_cast<const T*>(p.k_pages) + off);
-        cp_async16(smem_u32(vs + dswz<D>(key, c)), reinterpret_cast<const T*>(p.v_pages) + off);
+      // ---- stage keys [kb, kb + nk) of K and V (swizzled rows): the cached
+      // prefix by 16-byte cp.async (issued before the append for the first
+      // block), the new tokens from shared memory or, past kSnSmem of them,
+      // from the cache this CTA has just written.
+      if (rg > 0 || kb > 0) {
+        __syncthreads();  // previous block fully consumed
+        stage_prefix(kb, nk);
+      }
+      {
+        const int n0 = max(kb, L), n1 = kb + nk;  // new positions in this block
+        for (int e = tid; e < max(0, n1 - n0) * SH::CH; e += kDecThreads) {
+          const int pos = n0 + e / SH::CH, c = e % SH::CH;
+          const int key = pos - kb;
+          if (new_in_smem) {
+            *reinterpret_cast<uint4*>(ks + dswz<D>(key, c)) = *reinterpret_cast<const uint4*>(kns + dswz<D>(pos - L, c));
+            *reinterpret_cast<uint4*>(vs + dswz<D>(key, c)) = *reinterpret_cast<const uint4*>(vns + dswz<D>(pos - L, c));
+          } else {
+            const size_t off = cache_off(pos) + (size_t)c * 8;
+            cp_async16(smem_u32(ks + dswz<D>(key, c)), reinterpret_cast<const T*>(p.k_pages) + off);
+            cp_async16(smem_u32(vs + dswz<D>(key, c)), reinterpret_cast<const T*>(p.v_pages) + off);
+          }
+        }
       }
       // zero-fill the tail of the last 16-key chunk so masked keys hold finite data
       const int nk16 = (nk + 15) & ~15;
@@ -267,6 +326,38 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
         }
         // Online softmax over these 16 keys (rows g8 / g8 + 8; cols 2 t4 + {0,1} per key block).
         float pv[2][4];
+        const int kabs = kb + key0;
+        const bool plain = __all_sync(0xffffffffu, !rpad[0] && !rpad[1] && kabs >= rlo[0] && kabs >= rlo[1] &&
+                                                       kabs + 15 <= rhi[0] && kabs + 15 <= rhi[1]);
+        if (plain) {
+          // Every key of the chunk is allowed for every row of the warp.
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            float cmax = fmaxf(fmaxf(sc[0][2 * k], sc[0][2 * k + 1]), fmaxf(sc[1][2 * k], sc[1][2 * k + 1]));
+            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
+            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
+            const float m_new = fmaxf(m_run[k], cmax * c2);
+            const float alpha = ex2_approx(m_run[k] - m_new);  // m_run = -inf -> 0
+            float lsum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+              for (int e2 = 0; e2 < 2; ++e2) {
+                const float pe = ex2_approx(fmaf(sc[j][2 * k + e2], c2, -m_new));
+                pv[j][2 * k + e2] = pe;
+                lsum += pe;
+              }
+            lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+            lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+            l_run[k] = l_run[k] * alpha + lsum;
+            m_run[k] = m_new;
+#pragma unroll
+            for (int jd = 0; jd < D / 8; ++jd) {
+              oacc[jd][2 * k] *= alpha;
+              oacc[jd][2 * k + 1] *= alpha;
+            }
+          }
+        } else {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
           float cmax = -INFINITY;
@@ -308,6 +399,7 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
             oacc[jd][2 * k + 1] *= alpha;
           }
         }
+        }
         // O += P V: P (16 rows x 16 keys) as the A fragment, V via ldmatrix.trans.
         uint32_t pa[4];
         pa[0] = E::from_f2(pv[0][0], pv[0][1]);
@@ -327,6 +419,7 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
       }
     }
     // ---- merge the four warps' partials (m, l, O) per row and store.
+    __syncthreads();  // the partials go over the K rows
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int rr = g8 + 8 * k;
@@ -342,26 +435,46 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
       }
     }
     __syncthreads();
-    for (int e = tid; e < 16 * D; e += kDecThreads) {
-      const int rr = e / D, d = e - rr * D;
-      const int row = rg * 16 + rr;
-      if (row >= nrows) continue;
+    // Per row: weights of the four partials, f_w / sum_w f_w l_w with
+    // f_w = 2^(m_w - max m) (a warp that saw no allowed key contributes 0).
+    float* wt = red + kDecWarps * 16 * SH::RED_STRIDE;  // [warps][16]
+    if (tid < 16) {
       float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, red[(w * 16 + rr) * SH::RED_STRIDE + D]);
+      for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, red[(w * 16 + tid) * SH::RED_STRIDE + D]);
       const float Mu = (M == -INFINITY) ? 0.f : M;
-      float lt = 0.f, ot = 0.f;
+      float f[kDecWarps], lt = 0.f;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) {
+        const float mw = red[(w * 16 + tid) * SH::RED_STRIDE + D];
+        f[w] = (mw == -INFINITY) ? (M == -INFINITY ? 1.f : 0.f) : ex2_approx(mw - Mu);
+        lt += f[w] * red[(w * 16 + tid) * SH::RED_STRIDE + D + 1];
+      }
+      const float inv = 1.f / lt;
+#pragma unroll
+      for (int w = 0; w < kDecWarps; ++w) wt[w * 16 + tid] = f[w] * inv;
+    }
+    __syncthreads();
+    for (int e = tid; e < 16 * (D / 2); e += kDecThreads) {
+      const int rr = e / (D / 2), d = 2 * (e - rr * (D / 2));
+      const int row = rg * 16 + rr;
+      if (row >= nrows) continue;
+      float o0 = 0.f, o1 = 0.f;
 #pragma unroll
       for (int w = 0; w < kDecWarps; ++w) {
         const float* rw = red + (w * 16 + rr) * SH::RED_STRIDE;
-        const float sc = ex2_approx(rw[D] - Mu);
-        const float f = (rw[D] == -INFINITY) ? (M == -INFINITY ? 1.f : 0.f) : sc;
-        lt += f * rw[D + 1];
-        ot += f * rw[d];
+        const float ww = wt[w * 16 + rr];
+        o0 = fmaf(ww, rw[d], o0);
+        o1 = fmaf(ww, rw[d + 1], o1);
       }
       const int i = row / R, h = row - (row / R) * R;
       T* orow = reinterpret_cast<T*>(p.o) + (size_t)b * p.o_sb + (size_t)i * p.o_ss + (size_t)(g * R + h) * p.o_sh;
-      orow[d] = (T)(ot / lt);
+      if (p.o_pairs) {
+        *reinterpret_cast<uint32_t*>(orow + d) = E::from_f2(o0, o1);
+      } else {
+        orow[d] = (T)o0;
+        orow[d + 1] = (T)o1;
+      }
     }
     __syncthreads();
   }

@@ -53,6 +53,7 @@ struct DecodeParams {
   int cs_stride, rope, rope_abs;
   int cos_rows;
   int Sn, Hkv, R, page_size, max_pages, num_pages;
+  int o_pairs;               // 1: o and its strides allow 4-byte stores of element pairs
   float scale_log2;
   float scale_div64;
 };
