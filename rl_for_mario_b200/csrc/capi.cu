@@ -101,6 +101,24 @@ int encode_bshd(CUtensorMap* map, const void* base, bool is16, int B, int S, int
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// 2-D map over the rows of a paged cache ([num_pages * Hkv * page_size, D]),
+// box = one page of one KV head, swizzled like the decode kernel's rows.
+int encode_pages(CUtensorMap* map, const void* base, bool is16, int D, uint64_t rows, uint32_t page_size,
+                 const char* name) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)D, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  cuuint32_t box[2] = {(cuuint32_t)D, page_size};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle swz = D == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  CUresult r = enc(map, is16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(DT_ERR_INVALID, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name, (int)r);
+  return DT_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -286,13 +304,34 @@ int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o,
   p.cs_stride = (int)cos_stride; p.rope = apply_rope ? 1 : 0; p.rope_abs = rope_abs ? 1 : 0; p.cos_rows = cos_rows;
   p.Sn = Sn; p.Hkv = Hkv; p.R = Hq / Hkv; p.page_size = page_size; p.max_pages = max_pages; p.num_pages = num_pages;
   p.o_pairs = ((reinterpret_cast<uintptr_t>(o) & 3u) == 0 && o_sb % 2 == 0 && o_ss % 2 == 0 && o_sh % 2 == 0) ? 1 : 0;
+  {
+    const int hc = D / 16;
+    const bool rows_ok = aligned16(q) && aligned16(k_new) && aligned16(v_new) && q_sb % 8 == 0 && q_ss % 8 == 0 &&
+                         q_sh % 8 == 0 && kn_sb % 8 == 0 && kn_ss % 8 == 0 && kn_sh % 8 == 0 && vn_sb % 8 == 0 &&
+                         vn_ss % 8 == 0 && vn_sh % 8 == 0;
+    const bool tabs_ok = !apply_rope || (!rope_abs && aligned16(cos_tab) && aligned16(sin_tab) && cos_stride % 4 == 0);
+    p.vec_front = (dtype != DT_DTYPE_FP32 && Sn * (Hq / Hkv) <= 16 && Sn <= 16 && 16 * hc + 2 * Sn * hc <= 128 &&
+                   max_pages <= 128 && rows_ok && tabs_ok) ? 1 : 0;
+  }
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   p.scale_log2 = sc * 1.4426950408889634f;
   p.scale_div64 = sc / 64.f;
   if ((long long)B * Hkv > 0x7fffffffLL) return fail(DT_ERR_UNSUPPORTED, "%s: B*Hkv too large", fn);
+  CUtensorMap kmap, vmap;
+  memset(&kmap, 0, sizeof(kmap));
+  memset(&vmap, 0, sizeof(vmap));
+  const long long cache_rows = (long long)num_pages * Hkv * page_size;
+  p.tma_pages = (dtype != DT_DTYPE_FP32 && page_size >= 16 && page_size <= 256 && (page_size & (page_size - 1)) == 0 &&
+                 cache_rows <= 0x7fffffffLL) ? 1 : 0;
+  if (p.tma_pages) {
+    const bool is16 = dtype == DT_DTYPE_BF16;
+    if ((rc = encode_pages(&kmap, k_pages, is16, D, (uint64_t)cache_rows, (uint32_t)page_size, "k_pages"))) return rc;
+    if ((rc = encode_pages(&vmap, v_pages, is16, D, (uint64_t)cache_rows, (uint32_t)page_size, "v_pages"))) return rc;
+  }
   cudaError_t e = dtype == DT_DTYPE_FP32
                       ? dtk::launch_decode_f32(p, D, B, static_cast<cudaStream_t>(stream))
-                      : dtk::launch_decode_sm100(p, D, dtype == DT_DTYPE_BF16, B * Hkv, static_cast<cudaStream_t>(stream));
+                      : dtk::launch_decode_sm100(p, kmap, vmap, D, dtype == DT_DTYPE_BF16, B * Hkv,
+                                                      static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dt_attn_decode launch");
   return DT_OK;
 }

@@ -46,7 +46,9 @@ struct DecShape {
   static constexpr int OFF_Q = OFF_V + kKMax * ROWB;  // 16 rows
   static constexpr int OFF_KN = OFF_Q + 16 * ROWB;    // new keys (rotated), kSnSmem rows
   static constexpr int OFF_VN = OFF_KN + kSnSmem * ROWB;
-  static constexpr int SMEM = OFF_VN + kSnSmem * ROWB;
+  static constexpr int OFF_BT = OFF_VN + kSnSmem * ROWB;  // block-table row (vectorised front, <= 128 pages)
+  static constexpr int OFF_BAR = OFF_BT + 128 * 4;        // page-copy barrier
+  static constexpr int SMEM = OFF_BAR + 16 + 1024;        // + alignment of the K/V rows for TMA swizzle
   // Split-K partials [warps][16][D + 2] floats, over the K rows once a row
   // group's blocks are consumed.
   static constexpr int OFF_RED = OFF_K;
@@ -107,20 +109,93 @@ __device__ __forceinline__ void rope_pair(float x0, float x1, float c0, float s0
 }  // namespace
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const __grid_constant__ CUtensorMap tmKp,
+                                                                const __grid_constant__ CUtensorMap tmVp,
+                                                                const DecodeParams p) {
   using SH = DecShape<D>;
   using E = Elem<BF16>;
   using T = typename E::T;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.x / p.Hkv;
   const int g = blockIdx.x - b * p.Hkv;
   const int R = p.R, Sn = p.Sn;
+  constexpr int HC = D / 16;  // 16-byte chunk pairs (d, d + D/2) per row
+  uint8_t* ks = smem + SH::OFF_K;
+  uint8_t* vs = smem + SH::OFF_V;
+  uint8_t* qs = smem + SH::OFF_Q;
+  uint8_t* kns = smem + SH::OFF_KN;
+  uint8_t* vns = smem + SH::OFF_VN;
+  int* bt_s = reinterpret_cast<int*>(smem + SH::OFF_BT);
+  uint64_t* pbar = reinterpret_cast<uint64_t*>(smem + SH::OFF_BAR);
+  // Page copies by TMA (flag set by the host for page sizes 16..256 that
+  // divide the 256-key block): one bulk tensor copy per page and tensor.
+  const bool tma = p.tma_pages != 0;
+  if (tma && tid == 0) {
+    mbar_init(pbar, 1);
+    fence_mbar_init();
+  }
+  float* red = reinterpret_cast<float*>(smem + SH::OFF_RED);
+
+  // Vectorised front (flag set by the host when the inputs allow it): every
+  // input that does not depend on the cache length -- the length itself,
+  // the block-table row, the new q / k / v rows and their RoPE table rows --
+  // is requested in one round trip, 16 bytes per load.  Roles: threads
+  // [0, 16 HC) one q chunk pair of the 16-row tile, then Sn HC k chunk pairs,
+  // then Sn HC v chunk pairs.
+  const bool vec = p.vec_front != 0;
+  uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
+  float4 cra[2], crb[2], sra[2], srb[2];
+  bool have = false;  // this thread loaded a row chunk pair
+  int role = 3, rrow = 0, rch = 0;  // 0 q, 1 k, 2 v, 3 none
+  int btv = 0;
+  if (vec) {
+    const int e = tid;
+    if (e < 16 * HC) {
+      role = 0; rrow = e / HC; rch = e % HC;
+    } else if (e < 16 * HC + Sn * HC) {
+      role = 1; rrow = (e - 16 * HC) / HC; rch = (e - 16 * HC) % HC;
+    } else if (e < 16 * HC + 2 * Sn * HC) {
+      role = 2; rrow = (e - 16 * HC - Sn * HC) / HC; rch = (e - 16 * HC - Sn * HC) % HC;
+    }
+    const T* src = nullptr;  // stays null for rows past Sn * R: they are zero
+    int tab_row = 0;
+    if (role == 0 && rrow < Sn * R) {
+      const int i = rrow / R, h = rrow - i * R;
+      src = reinterpret_cast<const T*>(p.q) + (size_t)b * p.q_sb + (size_t)i * p.q_ss + (size_t)(g * R + h) * p.q_sh;
+      tab_row = i;
+    } else if (role == 1) {
+      src = reinterpret_cast<const T*>(p.k_new) + (size_t)b * p.kn_sb + (size_t)rrow * p.kn_ss + (size_t)g * p.kn_sh;
+      tab_row = rrow;
+    } else if (role == 2) {
+      src = reinterpret_cast<const T*>(p.v_new) + (size_t)b * p.vn_sb + (size_t)rrow * p.vn_ss + (size_t)g * p.vn_sh;
+    }
+    if (src) {
+      have = true;
+      xa = __ldg(reinterpret_cast<const uint4*>(src + rch * 8));
+      xb = __ldg(reinterpret_cast<const uint4*>(src + (rch + HC) * 8));
+      if (p.rope && role != 2) {
+        const float* cr = p.cos + (size_t)tab_row * p.cs_stride + rch * 8;
+        const float* sr = p.sin + (size_t)tab_row * p.cs_stride + rch * 8;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          cra[u] = __ldg(reinterpret_cast<const float4*>(cr) + u);
+          crb[u] = __ldg(reinterpret_cast<const float4*>(cr + D / 2) + u);
+          sra[u] = __ldg(reinterpret_cast<const float4*>(sr) + u);
+          srb[u] = __ldg(reinterpret_cast<const float4*>(sr + D / 2) + u);
+        }
+      }
+    }
+    if (tid < p.max_pages) btv = p.block_table[(size_t)b * p.max_pages + tid];
+  }
   const int L = p.seq_lens[b];
   const int kv_len = L + Sn;
   int pad = p.pad_len ? p.pad_len[b] : 0;
   pad = max(0, min(pad, kv_len));
-  const int32_t* bt = p.block_table + (size_t)b * p.max_pages;
+  if (vec && tid < p.max_pages) bt_s[tid] = btv;
+  if (vec) __syncthreads();
+  const int32_t* bt = vec ? bt_s : p.block_table + (size_t)b * p.max_pages;
 
   // Device-side bounds: capacity and page ids of every position touched.
   bool bad = L < 0 || kv_len > p.max_pages * p.page_size || (p.rope && p.rope_abs && kv_len > p.cos_rows);
@@ -135,12 +210,6 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
     return;
   }
 
-  uint8_t* ks = smem + SH::OFF_K;
-  uint8_t* vs = smem + SH::OFF_V;
-  uint8_t* qs = smem + SH::OFF_Q;
-  uint8_t* kns = smem + SH::OFF_KN;
-  uint8_t* vns = smem + SH::OFF_VN;
-  float* red = reinterpret_cast<float*>(smem + SH::OFF_RED);
   const bool new_in_smem = Sn <= kSnSmem;
   const size_t page_stride = (size_t)p.Hkv * p.page_size * D;  // elements per page
   auto cache_off = [&](int pos) -> size_t {
@@ -153,10 +222,25 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
     return p.sin + (size_t)(p.rope_abs ? L + i : i) * p.cs_stride;
   };
 
-  // Cached positions [kb, min(kb + nk, L)) of a block: 16-byte copies, page
-  // by page (a page holds its positions of one KV head contiguously).
+  // Cached positions [kb, min(kb + nk, L)) of a block: whole pages by TMA
+  // (rows past L are rewritten or zero-filled once the copy has landed), or
+  // 16-byte copies page by page (a page holds its positions of one KV head
+  // contiguously).
   auto stage_prefix = [&](int kb, int nk) {
     const int pend = kb + max(0, min(nk, L - kb));  // one past the last cached position
+    if (tma) {
+      if (tid == 0) {
+        const int pg0 = kb / p.page_size, pg1 = (pend + p.page_size - 1) / p.page_size;
+        mbar_arrive_expect_tx(pbar, (uint32_t)(2 * max(0, pg1 - pg0) * p.page_size * SH::ROWB));
+        for (int pg = pg0; pg < pg1; ++pg) {
+          const int row = (bt[pg] * p.Hkv + g) * p.page_size;
+          const int key = pg * p.page_size - kb;
+          tma_load_2d(ks + key * SH::ROWB, &tmKp, pbar, 0, row);
+          tma_load_2d(vs + key * SH::ROWB, &tmVp, pbar, 0, row);
+        }
+      }
+      return;
+    }
     for (int pos0 = kb; pos0 < pend;) {
       const int pg = pos0 / p.page_size;
       const int pos1 = min(pend, (pg + 1) * p.page_size);
@@ -176,8 +260,44 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
   // The first block's prefix is in flight while the new tokens are processed.
   stage_prefix(0, min(kKMax, kv_len));
 
+  if (vec) {
+    // Rotate (q, k) and place the rows: q into the query tile, new k / v into
+    // the cache and into their staging rows.
+    if (have && role <= 1 && p.rope) {
+      const uint32_t wa[4] = {xa.x, xa.y, xa.z, xa.w}, wb[4] = {xb.x, xb.y, xb.z, xb.w};
+      const float ca[8] = {cra[0].x, cra[0].y, cra[0].z, cra[0].w, cra[1].x, cra[1].y, cra[1].z, cra[1].w};
+      const float cb[8] = {crb[0].x, crb[0].y, crb[0].z, crb[0].w, crb[1].x, crb[1].y, crb[1].z, crb[1].w};
+      const float sa[8] = {sra[0].x, sra[0].y, sra[0].z, sra[0].w, sra[1].x, sra[1].y, sra[1].z, sra[1].w};
+      const float sb[8] = {srb[0].x, srb[0].y, srb[0].z, srb[0].w, srb[1].x, srb[1].y, srb[1].z, srb[1].w};
+      uint32_t ya[4], yb[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 a2 = E::to_f2(wa[u]), b2 = E::to_f2(wb[u]);
+        float y0, y1, z0, z1;
+        rope_pair(a2.x, b2.x, ca[2 * u], sa[2 * u], cb[2 * u], sb[2 * u], y0, z0);
+        rope_pair(a2.y, b2.y, ca[2 * u + 1], sa[2 * u + 1], cb[2 * u + 1], sb[2 * u + 1], y1, z1);
+        ya[u] = E::from_f2(y0, y1);
+        yb[u] = E::from_f2(z0, z1);
+      }
+      xa = make_uint4(ya[0], ya[1], ya[2], ya[3]);
+      xb = make_uint4(yb[0], yb[1], yb[2], yb[3]);
+    }
+    if (role == 0) {
+      *reinterpret_cast<uint4*>(qs + dswz<D>(rrow, rch)) = xa;  // rows past Sn * R stay zero
+      *reinterpret_cast<uint4*>(qs + dswz<D>(rrow, rch + HC)) = xb;
+    } else if (role <= 2) {
+      const size_t off = cache_off(L + rrow);
+      T* dst = reinterpret_cast<T*>(role == 1 ? p.k_pages : p.v_pages) + off;
+      *reinterpret_cast<uint4*>(dst + rch * 8) = xa;
+      *reinterpret_cast<uint4*>(dst + (rch + HC) * 8) = xb;
+      uint8_t* st = role == 1 ? kns : vns;
+      *reinterpret_cast<uint4*>(st + dswz<D>(rrow, rch)) = xa;
+      *reinterpret_cast<uint4*>(st + dswz<D>(rrow, rch + HC)) = xb;
+    }
+  }
+
   // ---- append: rotate the new keys, write new K/V into the paged cache.
-  for (int e = tid; e < Sn * (D / 2); e += kDecThreads) {
+  for (int e = tid; !vec && e < Sn * (D / 2); e += kDecThreads) {
     const int i = e / (D / 2), d = e - i * (D / 2);
     const T* kn = reinterpret_cast<const T*>(p.k_new) + (size_t)b * p.kn_sb + (size_t)i * p.kn_ss +
                   (size_t)g * p.kn_sh;
@@ -211,12 +331,14 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
   const int ngroups = (nrows + 15) / 16;
   const float c2 = p.scale_log2;
   const float sd64 = p.scale_div64;
-  // Make this CTA's cache writes visible to its own loads below.
-  __threadfence_block();
+  // Make this CTA's cache writes visible to its own loads below (only the
+  // path that re-reads new rows from the cache needs it).
+  if (!new_in_smem) __threadfence_block();
   __syncthreads();
+  uint32_t pphase = 0;  // page-copy barrier phase
 
   for (int rg = 0; rg < ngroups; ++rg) {
-    for (int e = tid; e < 16 * (D / 2); e += kDecThreads) {
+    for (int e = tid; !vec && e < 16 * (D / 2); e += kDecThreads) {
       const int rr = e / (D / 2), d = e - rr * (D / 2);
       const int row = rg * 16 + rr;
       float y0 = 0.f, y1 = 0.f;
@@ -279,6 +401,14 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
         __syncthreads();  // previous block fully consumed
         stage_prefix(kb, nk);
       }
+      if (tma) {
+        // The pages of this block have landed before any row of it is rewritten.
+        const bool ok = mbar_wait(pbar, pphase, nullptr, p.status);
+        pphase ^= 1u;
+        if (__syncthreads_or(!ok)) return;
+      } else {
+        cp_async_wait_all();
+      }
       {
         const int n0 = max(kb, L), n1 = kb + nk;  // new positions in this block
         for (int e = tid; e < max(0, n1 - n0) * SH::CH; e += kDecThreads) {
@@ -330,33 +460,40 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
         const bool plain = __all_sync(0xffffffffu, !rpad[0] && !rpad[1] && kabs >= rlo[0] && kabs >= rlo[1] &&
                                                        kabs + 15 <= rhi[0] && kabs + 15 <= rhi[1]);
         if (plain) {
-          // Every key of the chunk is allowed for every row of the warp.
+          // Every key of the chunk is allowed for every row of the warp.  The
+          // row reference m only moves (a quad max and a rescale of O) when a
+          // score exceeds it by more than 2^8; P <= 256 otherwise.
+          float x[2];
 #pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            float cmax = fmaxf(fmaxf(sc[0][2 * k], sc[0][2 * k + 1]), fmaxf(sc[1][2 * k], sc[1][2 * k + 1]));
-            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 1));
-            cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
-            const float m_new = fmaxf(m_run[k], cmax * c2);
-            const float alpha = ex2_approx(m_run[k] - m_new);  // m_run = -inf -> 0
-            float lsum = 0.f;
+          for (int k = 0; k < 2; ++k)
+            x[k] = fmaxf(fmaxf(sc[0][2 * k], sc[0][2 * k + 1]), fmaxf(sc[1][2 * k], sc[1][2 * k + 1])) * c2;
+          if (__any_sync(0xffffffffu, x[0] > m_run[0] + 8.f || x[1] > m_run[1] + 8.f)) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              float cmax = fmaxf(x[k], __shfl_xor_sync(0xffffffffu, x[k], 1));
+              cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, 2));
+              if (cmax > m_run[k] + 8.f) {  // quad-uniform
+                const float alpha = ex2_approx(m_run[k] - cmax);  // m_run = -inf -> 0
+                l_run[k] *= alpha;
+#pragma unroll
+                for (int jd = 0; jd < D / 8; ++jd) {
+                  oacc[jd][2 * k] *= alpha;
+                  oacc[jd][2 * k + 1] *= alpha;
+                }
+                m_run[k] = cmax;
+              }
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 2; ++k)
 #pragma unroll
             for (int j = 0; j < 2; ++j)
 #pragma unroll
               for (int e2 = 0; e2 < 2; ++e2) {
-                const float pe = ex2_approx(fmaf(sc[j][2 * k + e2], c2, -m_new));
+                const float pe = ex2_approx(fmaf(sc[j][2 * k + e2], c2, -m_run[k]));
                 pv[j][2 * k + e2] = pe;
-                lsum += pe;
+                l_run[k] += pe;  // this thread's keys; the quad sum is taken at the end
               }
-            lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
-            lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
-            l_run[k] = l_run[k] * alpha + lsum;
-            m_run[k] = m_new;
-#pragma unroll
-            for (int jd = 0; jd < D / 8; ++jd) {
-              oacc[jd][2 * k] *= alpha;
-              oacc[jd][2 * k + 1] *= alpha;
-            }
-          }
         } else {
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
@@ -389,9 +526,7 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
               pv[j][2 * k + e2] = pe;
               lsum += pe;
             }
-          lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
-          lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
-          l_run[k] = l_run[k] * alpha + lsum;
+          l_run[k] = l_run[k] * alpha + lsum;  // this thread's keys
           m_run[k] = m_new;
 #pragma unroll
           for (int jd = 0; jd < D / 8; ++jd) {
@@ -419,6 +554,11 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
       }
     }
     // ---- merge the four warps' partials (m, l, O) per row and store.
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      l_run[k] += __shfl_xor_sync(0xffffffffu, l_run[k], 1);
+      l_run[k] += __shfl_xor_sync(0xffffffffu, l_run[k], 2);
+    }
     __syncthreads();  // the partials go over the K rows
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
@@ -480,11 +620,12 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const DecodePara
   }
 }
 
-cudaError_t launch_decode_sm100(const DecodeParams& prm, int D, bool bf16, int grid, cudaStream_t stream) {
+cudaError_t launch_decode_sm100(const DecodeParams& prm, const CUtensorMap& kmap, const CUtensorMap& vmap, int D,
+                                bool bf16, int grid, cudaStream_t stream) {
   auto go = [&](auto kfn, int smem) -> cudaError_t {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    kfn<<<grid, kDecThreads, smem, stream>>>(prm);
+    kfn<<<grid, kDecThreads, smem, stream>>>(kmap, vmap, prm);
     return cudaGetLastError();
   };
   if (D == 32) return bf16 ? go(dt_decode_kernel<32, true>, DecShape<32>::SMEM)

@@ -54,6 +54,8 @@ struct DecodeParams {
   int cos_rows;
   int Sn, Hkv, R, page_size, max_pages, num_pages;
   int o_pairs;               // 1: o and its strides allow 4-byte stores of element pairs
+  int vec_front;             // 1: 16-byte loads of the new rows in one round trip (see the kernel)
+  int tma_pages;             // 1: cache pages copied by TMA (page_size a power of two in 16..256)
   float scale_log2;
   float scale_div64;
 };
@@ -112,6 +114,7 @@ cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w,
 // dtype: 0 bf16, 1 fp16, 2 fp32
 cudaError_t launch_kv_write_sm100(const KvWriteParams& prm, int D, int dtype, int B, cudaStream_t stream);
 
-cudaError_t launch_decode_sm100(const DecodeParams& prm, int D, bool bf16, int grid, cudaStream_t stream);
+cudaError_t launch_decode_sm100(const DecodeParams& prm, const CUtensorMap& kmap, const CUtensorMap& vmap, int D,
+                                bool bf16, int grid, cudaStream_t stream);
 
 }  // namespace dtk
