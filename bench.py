@@ -438,7 +438,7 @@ def _attended_pairs(S: int, pads) -> int:
     return tot
 
 
-def bench_prefill_cfg4(dev, peaks):
+def bench_prefill_cfg4(dev, peaks, batch=None, model=True):
     """Larger DT prefill: B=1024, 256 timesteps (768 tokens), hidden 768, 12 layers, 12/4 heads, head_dim 64.
 
     (a) the attention op alone at that shape, with Q / K rotated upstream as in
@@ -451,7 +451,7 @@ def bench_prefill_cfg4(dev, peaks):
     from oracle import precompute_freqs_cis
 
     C = PREFILL_LONG_CFG
-    B, T = C["batch"], C["timesteps"]
+    B, T = batch or C["batch"], C["timesteps"]
     S, Hq, Hkv, D = 3 * T, C["q_heads"], C["kv_heads"], C["head_dim"]
     g = torch.Generator(device=dev).manual_seed(4)
     # (a) attention op
@@ -480,6 +480,13 @@ def bench_prefill_cfg4(dev, peaks):
     byts = _algorithmic_bytes(B, S, Hq, Hkv, D)
     del q, k, v, out
     torch.cuda.empty_cache()
+    kernel_res = {"kernel": "dt_prefill_long_kernel", "inputs": "q / k rotated upstream", "batch": B, "ms": kms,
+                  "tokens_per_s": B * S / (kms * 1e-3),
+                  "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
+                               "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"], "flops_per_launch": flops,
+                               "hbm_achieved_gbs": byts / (kms * 1e-3) / 1e9, "peak_source": peaks["source"]}}
+    if not model:
+        return {"attention_kernel": kernel_res}
 
     # (b) full model forward
     torch.manual_seed(4)
@@ -515,13 +522,7 @@ def bench_prefill_cfg4(dev, peaks):
         "config": {"workload": "1024 x 256 timesteps (768 tokens), hidden 768, 12 layers, 12/4 heads, head_dim 64, "
                                "FFN 2048, bf16, fused RMSNorm+QKV, synthetic uint8 frames, left pad U{0..128} "
                                "timesteps, random-init weights"},
-        "attention_kernel": {"kernel": "dt_prefill_long_kernel", "inputs": "q / k rotated upstream", "ms": kms,
-                             "tokens_per_s": B * S / (kms * 1e-3),
-                             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
-                                          "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"],
-                                          "flops_per_launch": flops,
-                                          "hbm_achieved_gbs": byts / (kms * 1e-3) / 1e9,
-                                          "peak_source": peaks["source"]}},
+        "attention_kernel": kernel_res,
     }
     del model, states
     torch.cuda.empty_cache()
@@ -602,7 +603,23 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / rollout sub-benchmarks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
+    ap.add_argument("--only", choices=["decode", "prefill_long"], default=None,
+                    help="run one sub-benchmark alone and print its JSON (profiling)")
+    ap.add_argument("--long-batch", type=int, default=None,
+                    help="with --only prefill_long: batch of the attention-kernel case, model forward skipped")
     args = ap.parse_args()
+    if args.only:
+        if not torch.cuda.is_available():
+            raise SystemExit("bench.py needs a CUDA device (there is no CPU path)")
+        from rl_for_mario_b200 import _lib
+        _lib.load()
+        dev = torch.device("cuda", 0)
+        if args.only == "decode":
+            emit({"only": "decode", **bench_decode_cfg3(dev, _peaks())})
+        else:
+            emit({"only": "prefill_long", **bench_prefill_cfg4(dev, _peaks(), batch=args.long_batch,
+                                                                model=args.long_batch is None)})
+        return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.batch:
