@@ -502,10 +502,8 @@ __global__ void __launch_bounds__(kLongThreads, 1)
           for (int c = 0; c < 2; ++c)
 #pragma unroll
             for (int jj = 0; jj < 32; jj += 4) {
-              x0 = fmaxf(x0, __uint_as_float(u[c][jj]));
-              x1 = fmaxf(x1, __uint_as_float(u[c][jj + 1]));
-              x2 = fmaxf(x2, __uint_as_float(u[c][jj + 2]));
-              x3 = fmaxf(x3, __uint_as_float(u[c][jj + 3]));
+              x0 = fmax3(x0, __uint_as_float(u[c][jj]), __uint_as_float(u[c][jj + 1]));
+              x1 = fmax3(x1, __uint_as_float(u[c][jj + 2]), __uint_as_float(u[c][jj + 3]));
             }
         }
         const float bmax = rs(fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)));
@@ -545,14 +543,18 @@ __global__ void __launch_bounds__(kLongThreads, 1)
         for (int c = 0; c < 2; ++c) {
           uint32_t pk[16];
           if (!masked) {
+            const float2 c2v = make_float2(c2, c2), nmv = make_float2(-mm, -mm);
+            float2 lv = make_float2(0.f, 0.f);
 #pragma unroll
             for (int jj = 0; jj < 32; jj += 2) {
-              const float p0 = ex2_approx(fmaf(__uint_as_float(u[c][jj]), c2, -mm));
-              const float p1 = ex2_approx(fmaf(__uint_as_float(u[c][jj + 1]), c2, -mm));
-              l0 += p0;
-              l1 += p1;
-              pk[jj >> 1] = E::from_f2(p0, p1);
+              // two lanes of scale-and-shift / row-sum work per f32x2 instruction
+              const float2 t = ffma2(make_float2(__uint_as_float(u[c][jj]), __uint_as_float(u[c][jj + 1])), c2v, nmv);
+              const float2 pp = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+              lv = fadd2(lv, pp);
+              pk[jj >> 1] = E::from_f2(pp.x, pp.y);
             }
+            l0 += lv.x;
+            l1 += lv.y;
           } else if (warp_band) {
 #pragma unroll
             for (int jj = 0; jj < 32; jj += 2) {

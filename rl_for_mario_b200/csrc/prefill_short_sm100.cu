@@ -416,10 +416,8 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
         if (chunk_clean(ci)) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
-            mx0 = fmaxf(mx0, __uint_as_float(u[j]));
-            mx1 = fmaxf(mx1, __uint_as_float(u[j + 1]));
-            mx2 = fmaxf(mx2, __uint_as_float(u[j + 2]));
-            mx3 = fmaxf(mx3, __uint_as_float(u[j + 3]));
+            mx0 = fmax3(mx0, __uint_as_float(u[j]), __uint_as_float(u[j + 1]));
+            mx1 = fmax3(mx1, __uint_as_float(u[j + 2]), __uint_as_float(u[j + 3]));
           }
         } else {
           const uint32_t mk = chunk_mask(ci);
@@ -456,21 +454,22 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
       // Pass 2: P = exp2(t), packed bf16 pairs stored over the S columns just
       // read; row sum in fp32.
       float l0 = 0.f, l1 = 0.f, l2 = 0.f, l3 = 0.f;
+      float2 l01 = make_float2(0.f, 0.f), l23 = make_float2(0.f, 0.f);  // clean chunks
+      const float2 c2v = make_float2(c2, c2), nmv = make_float2(-m, -m);
       auto chunk_p = [&](const uint32_t (&u)[32], int ci) {
         uint32_t pk[16];
         if (chunk_clean(ci)) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(u[j]), c2, -m));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(u[j + 1]), c2, -m));
-            const float p2 = ex2_approx(fmaf(__uint_as_float(u[j + 2]), c2, -m));
-            const float p3 = ex2_approx(fmaf(__uint_as_float(u[j + 3]), c2, -m));
-            l0 += p0;
-            l1 += p1;
-            l2 += p2;
-            l3 += p3;
-            pk[j >> 1] = E::from_f2(p0, p1);
-            pk[(j >> 1) + 1] = E::from_f2(p2, p3);
+            // two lanes of scale-and-shift / row-sum work per f32x2 instruction
+            const float2 t01 = ffma2(make_float2(__uint_as_float(u[j]), __uint_as_float(u[j + 1])), c2v, nmv);
+            const float2 t23 = ffma2(make_float2(__uint_as_float(u[j + 2]), __uint_as_float(u[j + 3])), c2v, nmv);
+            const float2 p01 = make_float2(ex2_approx(t01.x), ex2_approx(t01.y));
+            const float2 p23 = make_float2(ex2_approx(t23.x), ex2_approx(t23.y));
+            l01 = fadd2(l01, p01);
+            l23 = fadd2(l23, p23);
+            pk[j >> 1] = E::from_f2(p01.x, p01.y);
+            pk[(j >> 1) + 1] = E::from_f2(p23.x, p23.y);
           }
         } else if (warp_padded) {
           const uint32_t mk = chunk_mask(ci);
@@ -527,7 +526,7 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
       // previous tile of this warpgroup (other O slot).
       if (prev.i >= 0 && !(ok = epilogue(prev, done - 1, l_prev))) break;
       prev = cur;
-      l_prev = (l0 + l1) + (l2 + l3);
+      l_prev = ((l0 + l1) + (l2 + l3)) + ((l01.x + l01.y) + (l23.x + l23.y));
       ++done;
     }
     if (ok && prev.i >= 0) epilogue(prev, done - 1, l_prev);
