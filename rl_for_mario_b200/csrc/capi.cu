@@ -310,8 +310,8 @@ int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o,
                          q_sh % 8 == 0 && kn_sb % 8 == 0 && kn_ss % 8 == 0 && kn_sh % 8 == 0 && vn_sb % 8 == 0 &&
                          vn_ss % 8 == 0 && vn_sh % 8 == 0;
     const bool tabs_ok = !apply_rope || (!rope_abs && aligned16(cos_tab) && aligned16(sin_tab) && cos_stride % 4 == 0);
-    p.vec_front = (dtype != DT_DTYPE_FP32 && Sn * (Hq / Hkv) <= 16 && Sn <= 16 && 16 * hc + 2 * Sn * hc <= 128 &&
-                   max_pages <= 128 && rows_ok && tabs_ok) ? 1 : 0;
+    p.vec_front = (dtype != DT_DTYPE_FP32 && Sn * (Hq / Hkv) <= 16 && Sn <= 16 && 16 * hc + 2 * Sn * hc <= dtk::kDecodeThreads &&
+                   max_pages <= dtk::kDecodeThreads && rows_ok && tabs_ok) ? 1 : 0;
   }
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   p.scale_log2 = sc * 1.4426950408889634f;
@@ -321,7 +321,7 @@ int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o,
   memset(&kmap, 0, sizeof(kmap));
   memset(&vmap, 0, sizeof(vmap));
   const long long cache_rows = (long long)num_pages * Hkv * page_size;
-  p.tma_pages = (dtype != DT_DTYPE_FP32 && page_size >= 16 && page_size <= 256 && (page_size & (page_size - 1)) == 0 &&
+  p.tma_pages = (dtype != DT_DTYPE_FP32 && page_size >= 16 && page_size <= dtk::kDecodeKeyBlock && (page_size & (page_size - 1)) == 0 &&
                  cache_rows <= 0x7fffffffLL) ? 1 : 0;
   if (p.tma_pages) {
     const bool is16 = dtype == DT_DTYPE_BF16;

@@ -8,11 +8,12 @@
 // columns (:230-237), the optional padding mask (:238-242) and an fp32
 // softmax (:243).
 //
-// One CTA per (sample b, KV head g), 4 warps.  The cached K/V of the unit are
-// staged into shared memory (swizzled, 16-byte cp.async) in blocks of up to
-// KMAX keys; each warp takes a quarter of the keys of a block and runs the
+// One CTA per (sample b, KV head g), 2 warps (small CTAs: ~21 KB of shared
+// memory, so many units' copies are in flight per SM).  The cached K/V of the
+// unit are staged into shared memory (swizzled) in blocks of up to KMAX keys;
+// each warp takes half of the keys of a block and runs the
 // R x Sn query rows (<= 16 per row group) against them with mma.sync
-// m16n8k16 (bf16/fp16 in, fp32 accumulate) and an online softmax; the four
+// m16n8k16 (bf16/fp16 in, fp32 accumulate) and an online softmax; the
 // partial (max, sum, O) are merged through shared memory (split-K).  The
 // copies of the cached prefix of the first block are issued before the new
 // tokens are rotated and appended, and (for up to 16 new tokens) the new rows
@@ -32,9 +33,9 @@ namespace dtk {
 
 namespace {
 
-constexpr int kDecThreads = 128;
-constexpr int kDecWarps = 4;
-constexpr int kKMax = 256;  // keys staged per block
+constexpr int kDecThreads = kDecodeThreads;
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kKMax = kDecodeKeyBlock;  // keys staged per block
 constexpr int kSnSmem = 16;  // new tokens staged from registers (more: re-read from the cache)
 
 template <int D>
@@ -46,14 +47,14 @@ struct DecShape {
   static constexpr int OFF_Q = OFF_V + kKMax * ROWB;  // 16 rows
   static constexpr int OFF_KN = OFF_Q + 16 * ROWB;    // new keys (rotated), kSnSmem rows
   static constexpr int OFF_VN = OFF_KN + kSnSmem * ROWB;
-  static constexpr int OFF_BT = OFF_VN + kSnSmem * ROWB;  // block-table row (vectorised front, <= 128 pages)
-  static constexpr int OFF_BAR = OFF_BT + 128 * 4;        // page-copy barrier
+  static constexpr int OFF_BT = OFF_VN + kSnSmem * ROWB;  // block-table row (vectorised front, <= one page per thread)
+  static constexpr int OFF_BAR = OFF_BT + kDecThreads * 4;  // page-copy barrier
   static constexpr int SMEM = OFF_BAR + 16 + 1024;        // + alignment of the K/V rows for TMA swizzle
-  // Split-K partials [warps][16][D + 2] floats, over the K rows once a row
+  // Split-K partials [warps][16][D + 2] floats, over the K / V rows once a row
   // group's blocks are consumed.
   static constexpr int OFF_RED = OFF_K;
   static constexpr int RED_STRIDE = D + 2;
-  static_assert((kDecWarps * 16 * RED_STRIDE + kDecWarps * 16) * 4 <= kKMax * ROWB, "partials fit over the K rows");
+  static_assert((kDecWarps * 16 * RED_STRIDE + kDecWarps * 16) * 4 <= 2 * kKMax * ROWB, "partials fit over the K and V rows");
 };
 
 // Swizzled byte offset of 16-byte chunk c of row r (64-byte rows: XOR with
@@ -130,7 +131,7 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const __grid_con
   int* bt_s = reinterpret_cast<int*>(smem + SH::OFF_BT);
   uint64_t* pbar = reinterpret_cast<uint64_t*>(smem + SH::OFF_BAR);
   // Page copies by TMA (flag set by the host for page sizes 16..256 that
-  // divide the 256-key block): one bulk tensor copy per page and tensor.
+  // divide the key block): one bulk tensor copy per page and tensor.
   const bool tma = p.tma_pages != 0;
   if (tma && tid == 0) {
     mbar_init(pbar, 1);
@@ -553,13 +554,13 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const __grid_con
         }
       }
     }
-    // ---- merge the four warps' partials (m, l, O) per row and store.
+    // ---- merge the warps' partials (m, l, O) per row and store.
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       l_run[k] += __shfl_xor_sync(0xffffffffu, l_run[k], 1);
       l_run[k] += __shfl_xor_sync(0xffffffffu, l_run[k], 2);
     }
-    __syncthreads();  // the partials go over the K rows
+    __syncthreads();  // the partials go over the K / V rows
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int rr = g8 + 8 * k;

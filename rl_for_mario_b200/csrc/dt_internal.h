@@ -35,6 +35,10 @@ cudaError_t launch_prefill_long_sm100(const CUtensorMap& q, const CUtensorMap& k
                                       const PrefillParams& prm, bool bf16, int n_units, int grid,
                                       cudaStream_t stream);
 
+// Decode CTA shape: threads (warps split the keys) and keys staged per block.
+constexpr int kDecodeThreads = 64;
+constexpr int kDecodeKeyBlock = 128;
+
 // Kernel parameters of the paged-cache decode (dt_attn_decode).
 struct DecodeParams {
   const void* q;             // [B, Sn, Hq, D] new queries (pre-RoPE)
