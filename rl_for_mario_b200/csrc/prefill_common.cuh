@@ -96,6 +96,38 @@ __device__ __forceinline__ void rope_row_inplace_smem(uint8_t* tile, int r, cons
   }
 }
 
+// Same rotation from a shared-memory cos / sin row whose sin entries of the
+// first half are stored negated, in packed fp32 pairs (one multiply and one
+// fused multiply-add instruction per two outputs).
+template <int D, bool BF16>
+__device__ __forceinline__ void rope_row_inplace_f2(uint8_t* tile, int r, const float* cr, const float* sr) {
+  constexpr int NCH = D / 8;
+  constexpr int HALF = NCH / 2;
+  using E = Elem<BF16>;
+#pragma unroll
+  for (int c = 0; c < HALF; ++c) {
+    uint4* pa = reinterpret_cast<uint4*>(tile + swz<D * 2>(r, c));
+    uint4* pb = reinterpret_cast<uint4*>(tile + swz<D * 2>(r, c + HALF));
+    const uint4 a = *pa, b = *pb;
+    const uint32_t au[4] = {a.x, a.y, a.z, a.w}, bu[4] = {b.x, b.y, b.z, b.w};
+    uint32_t ya[4], yb[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 xa = E::to_f2(au[i]), xb = E::to_f2(bu[i]);
+      const float2 ca = *reinterpret_cast<const float2*>(cr + c * 8 + 2 * i);
+      const float2 cb = *reinterpret_cast<const float2*>(cr + (c + HALF) * 8 + 2 * i);
+      const float2 sa = *reinterpret_cast<const float2*>(sr + c * 8 + 2 * i);  // negated
+      const float2 sb = *reinterpret_cast<const float2*>(sr + (c + HALF) * 8 + 2 * i);
+      const float2 y = ffma2(xa, ca, fmul2(xb, sa));
+      const float2 z = ffma2(xb, cb, fmul2(xa, sb));
+      ya[i] = E::from_f2(y.x, y.y);
+      yb[i] = E::from_f2(z.x, z.y);
+    }
+    *pa = make_uint4(ya[0], ya[1], ya[2], ya[3]);
+    *pb = make_uint4(yb[0], yb[1], yb[2], yb[3]);
+  }
+}
+
 // Per-tile schedule, computed identically by every role.
 struct TilePlan {
   int pos0, pos_end, kstart, kend, nblocks;

@@ -164,12 +164,14 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
     pads_s[j] = max(0, min(pad, S));
   }
   if (prm.rope) {
+    // The first half of each sin row is stored negated (rope_row_inplace_f2).
     for (int j = tid; j < S * (SS::D / 4); j += SS::NTHREADS) {
       const int row = j / (SS::D / 4), c4 = j % (SS::D / 4);
       *reinterpret_cast<float4*>(cos_s + row * SS::CS_STRIDE + c4 * 4) =
           __ldg(reinterpret_cast<const float4*>(prm.cos + (size_t)row * prm.cs_stride) + c4);
-      *reinterpret_cast<float4*>(sin_s + row * SS::CS_STRIDE + c4 * 4) =
-          __ldg(reinterpret_cast<const float4*>(prm.sin + (size_t)row * prm.cs_stride) + c4);
+      float4 sv = __ldg(reinterpret_cast<const float4*>(prm.sin + (size_t)row * prm.cs_stride) + c4);
+      if (c4 * 4 < SS::D / 2) sv = make_float4(-sv.x, -sv.y, -sv.z, -sv.w);
+      *reinterpret_cast<float4*>(sin_s + row * SS::CS_STRIDE + c4 * 4) = sv;
     }
   }
   if (warp == 1) {
@@ -309,7 +311,7 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
       if (prm.rope) {
         uint8_t* kt = k_s + kvb * SS::KV_BYTES;
         for (int row = rt; row < S; row += SS::NROPE)
-          rope_row_inplace_smem<32, BF16>(kt, row, cos_s + row * SS::CS_STRIDE, sin_s + row * SS::CS_STRIDE);
+          rope_row_inplace_f2<32, BF16>(kt, row, cos_s + row * SS::CS_STRIDE, sin_s + row * SS::CS_STRIDE);
         fence_proxy_async_smem();
       }
       mbar_arrive(&kv_ready[kvb]);
@@ -320,8 +322,8 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
           for (int row = rt; row < PT * R; row += SS::NROPE) {
             const int pos = t * PT + row / R;
             if (pos < S)
-              rope_row_inplace_smem<32, BF16>(q_s + qs * SS::Q_BYTES, row, cos_s + pos * SS::CS_STRIDE,
-                                              sin_s + pos * SS::CS_STRIDE);
+              rope_row_inplace_f2<32, BF16>(q_s + qs * SS::Q_BYTES, row, cos_s + pos * SS::CS_STRIDE,
+                                            sin_s + pos * SS::CS_STRIDE);
           }
           fence_proxy_async_smem();
         }
