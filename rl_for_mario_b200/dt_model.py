@@ -134,11 +134,27 @@ class MarioStateEncoder(nn.Module):
         if states.ndim != 5:
             raise ValueError(f"states must be [B,T,C,H,W], got {tuple(states.shape)}")
         B, T, C, H, W = states.shape
-        x = states.to(self.cnn[0].weight.dtype)
-        # The reference rescales when max > 1 (:338); the same test is done on
-        # the device here, so no host synchronisation per call.
-        x = torch.where(x.max() > 1.0, x / 255.0, x)
-        return self.cnn(x.reshape(B * T, C, H, W)).reshape(B, T, -1)
+        conv0, conv1, conv2, lin = self.cnn[0], self.cnn[2], self.cnn[4], self.cnn[7]
+        dt = conv0.weight.dtype
+        s = states.reshape(B * T, C, H, W)
+        # The reference divides by 255 when the frames' max exceeds 1 (:338).
+        # The test stays on the device (no host synchronisation) and the 1/255
+        # goes into the first convolution's weight instead of a pass over the
+        # frames.
+        big = (s.amax() > 1) if s.dtype == torch.uint8 else (s.to(dt).amax() > 1.0)
+        w0 = torch.where(big, conv0.weight / 255.0, conv0.weight)
+        # One pass: frames -> compute dtype, channels-last (the layout the
+        # convolution kernels run in, so no layout conversions per layer).
+        x = torch.empty(s.shape, dtype=dt, device=s.device, memory_format=torch.channels_last)
+        x.copy_(s)
+        cl = torch.channels_last
+        x = F.relu(F.conv2d(x, w0.contiguous(memory_format=cl), conv0.bias, stride=conv0.stride), inplace=True)
+        x = F.relu(F.conv2d(x, conv1.weight.contiguous(memory_format=cl), conv1.bias, stride=conv1.stride),
+                   inplace=True)
+        x = F.relu(F.conv2d(x, conv2.weight.contiguous(memory_format=cl), conv2.bias, stride=conv2.stride),
+                   inplace=True)
+        # Flatten in the reference's (C, H, W) order.
+        return lin(x.contiguous().flatten(1)).reshape(B, T, -1)
 
 
 class DTBackbone(nn.Module):
