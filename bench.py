@@ -316,6 +316,7 @@ def run_ours(args):
         if world == 1:
             line["decode"] = bench_decode_cfg3(dev, peaks)
             line["prefill_long"] = bench_prefill_cfg4(dev, peaks)
+            line["prefill_long"]["rmsnorm_qkv_kernel"] = bench_rmsnorm_qkv_cfg4(dev, peaks)
         line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
@@ -529,6 +530,44 @@ def bench_prefill_cfg4(dev, peaks, batch=None, model=True):
     return res
 
 
+def bench_rmsnorm_qkv_cfg4(dev, peaks, batch=None):
+    """The fused RMSNorm + Q/K/V projection + RoPE kernel at a cfg4 layer's shape:
+    M = batch x 768 tokens, K = hidden 768, N = (12 + 2 x 4) x 64 = 1280."""
+    from rl_for_mario_b200.kernels import device_status, fold_norm_weight, rmsnorm_qkv
+    from oracle import precompute_freqs_cis
+
+    C = PREFILL_LONG_CFG
+    B, S, H = batch or C["batch"], 3 * C["timesteps"], C["hidden"]
+    Hq, Hkv, D = C["q_heads"], C["kv_heads"], C["head_dim"]
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(B, S, H, device=dev, generator=g).to(torch.bfloat16)
+    wq, wk, wv = (torch.randn(h * D, H, device=dev, generator=g) / H ** 0.5 for h in (Hq, Hkv, Hkv))
+    wf = fold_norm_weight(wq, wk, wv, torch.ones(H, device=dev), torch.bfloat16)
+    cos, sin = (t.to(dev) for t in precompute_freqs_cis(D, S))
+    rope = (cos, sin, (Hq + Hkv) * D, D)
+    out = torch.empty(B, S, (Hq + 2 * Hkv) * D, device=dev, dtype=torch.bfloat16)
+    for _ in range(3):
+        rmsnorm_qkv(x, wf, 1e-5, out=out, rope=rope)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 10
+    e0.record()
+    for _ in range(n):
+        rmsnorm_qkv(x, wf, 1e-5, out=out, rope=rope)
+    e1.record()
+    torch.cuda.synchronize()
+    if device_status() != 0:
+        raise SystemExit("device status error in the RMSNorm + QKV benchmark")
+    ms = e0.elapsed_time(e1) / n
+    M, N = B * S, (Hq + 2 * Hkv) * D
+    flops = 2 * M * H * N
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"kernel": "dt_rmsnorm_qkv_persist_kernel", "shape": {"M": M, "K": H, "N": N}, "ms": ms,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tf / peaks["bf16_tflops"], "flops_per_launch": flops,
+                         "peak_source": peaks["source"]}}
+
+
 def bench_rollout_cfg5(dev, world, rank, pg):
     """8,192 environments per GPU, 64 cached steps, CNN on synthetic frames, all-gather of logits."""
     from rl_for_mario_b200.dt_model import DTConfig, MarioDT
@@ -603,7 +642,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / rollout sub-benchmarks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
-    ap.add_argument("--only", choices=["decode", "prefill_long"], default=None,
+    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv"], default=None,
                     help="run one sub-benchmark alone and print its JSON (profiling)")
     ap.add_argument("--long-batch", type=int, default=None,
                     help="with --only prefill_long: batch of the attention-kernel case, model forward skipped")
@@ -616,6 +655,8 @@ def main():
         dev = torch.device("cuda", 0)
         if args.only == "decode":
             emit({"only": "decode", **bench_decode_cfg3(dev, _peaks())})
+        elif args.only == "rmsnorm_qkv":
+            emit({"only": "rmsnorm_qkv", **bench_rmsnorm_qkv_cfg4(dev, _peaks(), batch=args.long_batch)})
         else:
             emit({"only": "prefill_long", **bench_prefill_cfg4(dev, _peaks(), batch=args.long_batch,
                                                                 model=args.long_batch is None)})

@@ -402,16 +402,21 @@ int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const 
   if (rc) return rc;
   if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
   const bool bf16 = dtype == DT_DTYPE_BF16;
-  const int ncta = dtk::rmsnorm_qkv_ncta(N);
-  const int nsub = ncta <= 256 ? ncta : ncta / 2;
-  CUtensorMap mx, mw;
+  const int ncta = dtk::rmsnorm_qkv_ncta(N);  // 0: persistent kernel, 256-column tiles
+  const int nsub = ncta == 0 ? 256 : (ncta <= 256 ? ncta : ncta / 2);
+  CUtensorMap mx, mw, my;
   if ((rc = encode_2d(&mx, x, bf16, (uint64_t)K, (uint64_t)M, (uint64_t)x_row_stride, 64, 128, "x"))) return rc;
   if ((rc = encode_2d(&mw, w_fused, bf16, (uint64_t)K, (uint64_t)N, (uint64_t)K, 64, (uint32_t)nsub, "w"))) return rc;
+  memset(&my, 0, sizeof(my));
+  // The persistent kernel stores 32 x 64 output slices (one per epilogue warp) by TMA.
+  if (ncta == 0 && (rc = encode_2d(&my, y, bf16, (uint64_t)N, (uint64_t)M, (uint64_t)y_row_stride, 64, 32, "y")))
+    return rc;
   dtk::RmsQkvParams p;
   p.y = y; p.status = status; p.y_stride = y_row_stride; p.M = M; p.K = K; p.N = N; p.bf16 = bf16 ? 1 : 0; p.eps = eps;
   p.cos = cos_tab; p.sin = sin_tab; p.rope_cols = rope_cols; p.head_dim = head_dim; p.seq_len = seq_len;
   p.cs_stride = (int)cos_stride;
-  cudaError_t e = dtk::launch_rmsnorm_qkv_sm100(mx, mw, p, ncta, static_cast<cudaStream_t>(stream));
+  cudaError_t e = dtk::launch_rmsnorm_qkv_sm100(mx, mw, my, p, ncta, x, x_row_stride, g_num_sms[dev],
+                                                static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
   return DT_OK;
 }

@@ -229,6 +229,242 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// Persistent variant for wide outputs (N > 512, e.g. hidden 768 with 12/4
+// heads: N = 1280): a CTA owns 128-row blocks of x and runs all of a block's
+// 256-column tiles back to back, so the block's x rows stay hot in L2 and its
+// row scale is computed once.  The accumulator is double-buffered in TMEM (2 x
+// 256 columns): the epilogue of one tile overlaps the main loop of the next.
+// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-5 epilogue, 6-9 row
+// sums of squares (read from global memory, one warp per row at a time).
+namespace {
+constexpr int kPersistThreads = 320;
+constexpr int kPN = 256;        // columns per tile
+constexpr int kPStages = 4;
+struct PShape {
+  static constexpr int A_BYTES = 128 * kKC * 2;
+  static constexpr int B_BYTES = kPN * kKC * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int OFF_ST = kPStages * STAGE;            // output staging: [2][4 warps][32 rows][64 cols]
+  static constexpr int ST_WARP = 32 * 64 * 2;                // one warp's slice (4 swizzle atoms)
+  static constexpr int OFF_SS = OFF_ST + 2 * 4 * ST_WARP;    // [2][128] floats
+  static constexpr int OFF_BAR = OFF_SS + 2 * 128 * 4;
+  // full[S], empty[S], acc_full[2], acc_empty[2], ss_full[2], ss_empty[2], drain
+  static constexpr int NBAR = 2 * kPStages + 9;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+}  // namespace
+
+__global__ void __launch_bounds__(kPersistThreads, 1)
+    dt_rmsnorm_qkv_persist_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                                  const __grid_constant__ CUtensorMap tmY, const __nv_bfloat16* __restrict__ xg,
+                                  long long x_stride, const RmsQkvParams p) {
+  using SH = PShape;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* ss_s = reinterpret_cast<float*>(smem + SH::OFF_SS);
+  uint8_t* st_s = smem + SH::OFF_ST;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + SH::OFF_BAR);
+  uint64_t* empty = full + kPStages;
+  uint64_t* acc_full = empty + kPStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* ss_full = acc_empty + 2;
+  uint64_t* ss_empty = ss_full + 2;
+  uint64_t* drain = ss_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nk = (p.K + kKC - 1) / kKC;
+  const int nrb = (p.M + 127) / 128;
+  const int nt = (p.N + kPN - 1) / kPN;
+
+  if (tid == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&acc_full[j], 1);
+      mbar_init(&acc_empty[j], 4);  // one arrival per epilogue warp
+      mbar_init(&ss_full[j], 4);    // one per sum-of-squares warp
+      mbar_init(&ss_empty[j], 4);   // one per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmX);
+      prefetch_tmap(&tmW);
+      int cnt = 0;
+      bool ok = true;
+      for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x)
+        for (int ct = 0; ct < nt && ok; ++ct)
+          for (int kc = 0; kc < nk; ++kc, ++cnt) {
+            const int s = cnt % kPStages;
+            if (!(ok = mbar_wait(&empty[s], ((cnt / kPStages) & 1) ^ 1, abort_flag, p.status))) break;
+            uint8_t* st = smem + s * SH::STAGE;
+            mbar_arrive_expect_tx(&full[s], (uint32_t)SH::STAGE);
+            tma_load_2d(st, &tmX, &full[s], kc * kKC, rb * 128);
+            tma_load_2d(st + SH::A_BYTES, &tmW, &full[s], kc * kKC, ct * kPN);
+          }
+      if (!ok) {
+        for (int s = 0; s < kPStages; ++s) {
+          const int uses = cnt / kPStages + (s < cnt % kPStages ? 1 : 0);
+          if (uses > 0) mbar_wait(&full[s], (uses - 1) & 1, nullptr, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(p.bf16 != 0, 128, kPN, 0, 0);
+      int cnt = 0, tc = 0;
+      bool ok = true;
+      for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x)
+        for (int ct = 0; ct < nt && ok; ++ct, ++tc) {
+          const int buf = tc & 1;
+          if (!(ok = mbar_wait(&acc_empty[buf], ((tc >> 1) & 1) ^ 1, abort_flag, p.status))) break;
+          for (int kc = 0; kc < nk; ++kc, ++cnt) {
+            const int s = cnt % kPStages;
+            if (!(ok = mbar_wait(&full[s], (cnt / kPStages) & 1, abort_flag, p.status))) break;
+            tc_fence_after();
+            const uint32_t a = smem_u32(smem + s * SH::STAGE);
+            const uint64_t ad = umma_smem_desc(a, 16, 1024, kSw128);
+            const uint64_t bd = umma_smem_desc(a + SH::A_BYTES, 16, 1024, kSw128);
+#pragma unroll
+            for (int kk = 0; kk < kKC / 16; ++kk)  // 32 bytes per K step inside the 128-byte atom
+              umma_f16_ss(tmem + buf * kPN, ad + 2 * kk, bd + 2 * kk, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&empty[s]);
+          }
+          if (ok) umma_commit(&acc_full[buf]);
+        }
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, nullptr);
+    }
+  } else if (warp < 6) {
+    // Epilogue: TMEM -> row scale -> (RoPE) -> 16-bit -> HBM.
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;  // tile row = TMEM lane
+    const uint32_t t_row = tmem + ((uint32_t)(wq * 32) << 16);
+    int tc = 0, bc = 0, sc = 0;  // tiles, row blocks, staged output chunks
+    bool ok = true;
+    for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++bc) {
+      const int sb = bc & 1;
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&ss_full[sb], (bc >> 1) & 1, abort_flag, p.status)))) break;
+      const float rs = rsqrtf(ss_s[sb * 128 + r] / (float)p.K + p.eps);
+      const int row_g = rb * 128 + r;
+      const int pos = p.rope_cols > 0 ? row_g % p.seq_len : 0;
+      const float* crow = p.cos + (size_t)pos * p.cs_stride;
+      const float* srow = p.sin + (size_t)pos * p.cs_stride;
+      for (int ct = 0; ct < nt && ok; ++ct, ++tc) {
+        const int buf = tc & 1;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (tc >> 1) & 1, abort_flag, p.status)))) break;
+        tc_fence_after();
+        const int n0 = ct * kPN;
+        for (int c = 0; c < kPN; c += 64) {
+          float v[64];
+          tmem_ld32(t_row + buf * kPN + c, *reinterpret_cast<float(*)[32]>(&v[0]));
+          tmem_ld32(t_row + buf * kPN + c + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+#pragma unroll
+          for (int i = 0; i < 64; ++i) v[i] *= rs;
+          if (n0 + c < p.rope_cols && row_g < p.M) {
+            if (p.head_dim == 64)
+              rope_pairs<32>(v, 0, crow, srow);
+            else {
+              rope_pairs<16>(v, 0, crow, srow);
+              rope_pairs<16>(v, 32, crow, srow);
+            }
+          }
+          // Each warp stages its 32 x 64 slice in shared memory (128-byte
+          // swizzle) and stores it with one TMA copy: whole rows per copy
+          // instead of one line per thread.  Rows past M and columns past N
+          // are clipped by the copy.
+          uint8_t* stb = st_s + ((sc & 1) * 4 + wq) * SH::ST_WARP;
+          if (lane == 0 && sc >= 2) bulk_wait_read<1>();  // the copy that last read this buffer is done
+          __syncwarp();
+#pragma unroll
+          for (int c8 = 0; c8 < 64; c8 += 8) {
+            uint4 o;
+            if (p.bf16) {
+              o.x = Elem<true>::from_f2(v[c8], v[c8 + 1]);
+              o.y = Elem<true>::from_f2(v[c8 + 2], v[c8 + 3]);
+              o.z = Elem<true>::from_f2(v[c8 + 4], v[c8 + 5]);
+              o.w = Elem<true>::from_f2(v[c8 + 6], v[c8 + 7]);
+            } else {
+              o.x = Elem<false>::from_f2(v[c8], v[c8 + 1]);
+              o.y = Elem<false>::from_f2(v[c8 + 2], v[c8 + 3]);
+              o.z = Elem<false>::from_f2(v[c8 + 4], v[c8 + 5]);
+              o.w = Elem<false>::from_f2(v[c8 + 6], v[c8 + 7]);
+            }
+            *reinterpret_cast<uint4*>(stb + lane * 128 + (((c8 >> 3) ^ (lane & 7)) << 4)) = o;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && n0 + c < p.N) {
+            tma_store_2d(&tmY, stb, n0 + c, rb * 128 + wq * 32);
+            bulk_commit();
+          }
+          ++sc;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ss_empty[sb]);
+    }
+    if (lane == 0) bulk_wait<0>();  // output copies complete before the CTA exits
+  } else {
+    // Row sums of squares of a 128-row block, one warp per row at a time
+    // (16-byte loads spread over the lanes, then a warp sum).
+    const int nw = warp - 6;  // 0..3: rows nw, nw + 4, ...
+    int bc = 0;
+    bool ok = true;
+    for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++bc) {
+      const int sb = bc & 1;
+      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&ss_empty[sb], ((bc >> 1) & 1) ^ 1, abort_flag, p.status))))
+        break;
+      for (int rr = nw; rr < 128; rr += 4) {
+        const int row_g = rb * 128 + rr;
+        float ss = 0.f;
+        if (row_g < p.M) {
+          const uint4* xr = reinterpret_cast<const uint4*>(xg + (size_t)row_g * x_stride);
+          for (int c = lane; c < p.K / 8; c += 32) {
+            const uint4 u = __ldg(xr + c);
+            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = p.bf16 ? Elem<true>::to_f2(w4[i]) : Elem<false>::to_f2(w4[i]);
+              ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+            }
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) ss_s[sb * 128 + rr] = ss;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ss_full[sb]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 template <int NCTA>
 static cudaError_t launch_rq(const CUtensorMap& x, const CUtensorMap& w, const RmsQkvParams& p, cudaStream_t st) {
   using SH = GemmShape<NCTA>;
@@ -241,15 +477,27 @@ static cudaError_t launch_rq(const CUtensorMap& x, const CUtensorMap& w, const R
 }
 
 int rmsnorm_qkv_ncta(int N) {
-  // Widest accumulator that covers N in one pass when possible (x read once).
+  // Widest accumulator that covers N in one pass when possible (x read once);
+  // wider outputs use the persistent kernel (0) with 256-column tiles.
   if (N <= 128) return 128;
   if (N <= 256) return 256;
   if (N <= 384) return 384;
-  return 512;
+  if (N <= 512) return 512;
+  return 0;
 }
 
-cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w, const RmsQkvParams& p, int ncta,
-                                     cudaStream_t st) {
+cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w, const CUtensorMap& y,
+                                     const RmsQkvParams& p, int ncta, const void* x_ptr, long long x_stride,
+                                     int num_sms, cudaStream_t st) {
+  if (ncta == 0) {
+    auto k = dt_rmsnorm_qkv_persist_kernel;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PShape::SMEM);
+    if (e != cudaSuccess) return e;
+    const int nrb = (p.M + 127) / 128;
+    const int grid = nrb < num_sms ? nrb : num_sms;
+    k<<<grid, kPersistThreads, PShape::SMEM, st>>>(x, w, y, static_cast<const __nv_bfloat16*>(x_ptr), x_stride, p);
+    return cudaGetLastError();
+  }
   switch (ncta) {
     case 128: return launch_rq<128>(x, w, p, st);
     case 256: return launch_rq<256>(x, w, p, st);

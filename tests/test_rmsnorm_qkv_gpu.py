@@ -7,7 +7,8 @@ from oracle import rmsnorm_ref
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("M,K,N", [(1, 256, 384), (300, 256, 384), (4096, 256, 384), (777, 768, 1280),
-                                   (130, 128, 192), (64, 64, 128), (257, 512, 512), (1000, 256, 96)])
+                                   (130, 128, 192), (64, 64, 128), (257, 512, 512), (1000, 256, 96),
+                                   (200, 256, 520), (130, 128, 776), (1, 64, 1024)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_rmsnorm_qkv_matches_reference(M, K, N, dtype):
     from rl_for_mario_b200.kernels import device_status, fold_norm_weight, rmsnorm_qkv
@@ -26,6 +27,25 @@ def test_rmsnorm_qkv_matches_reference(M, K, N, dtype):
     err = (y.float().cpu() - ref).abs()
     tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
     assert (err <= tol + tol * ref.abs()).all(), f"max err {err.max().item():.3e}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N", [384, 1280])
+def test_rmsnorm_qkv_strided_rows(N):
+    """x rows with a padded stride (a column slice of a wider buffer)."""
+    from rl_for_mario_b200.kernels import device_status, rmsnorm_qkv
+
+    g = torch.Generator().manual_seed(N)
+    M, K = 300, 256
+    xb = (torch.randn(M, K + 64, generator=g) * 2).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) / K ** 0.5).to(torch.bfloat16)
+    x = xb.cuda()[:, :K]
+    assert x.stride(0) == K + 64
+    y = rmsnorm_qkv(x, w.cuda(), 1e-5)
+    assert device_status() == 0
+    ref = rmsnorm_ref(xb[:, :K].float(), torch.ones(K)) @ w.float().t()
+    err = (y.float().cpu() - ref).abs()
+    assert (err <= 2e-2 + 2e-2 * ref.abs()).all(), f"max err {err.max().item():.3e}"
 
 
 @pytest.mark.gpu
