@@ -415,7 +415,7 @@ int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const 
   p.y = y; p.status = status; p.y_stride = y_row_stride; p.M = M; p.K = K; p.N = N; p.bf16 = bf16 ? 1 : 0; p.eps = eps;
   p.cos = cos_tab; p.sin = sin_tab; p.rope_cols = rope_cols; p.head_dim = head_dim; p.seq_len = seq_len;
   p.cs_stride = (int)cos_stride;
-  cudaError_t e = dtk::launch_rmsnorm_qkv_sm100(mx, mw, my, p, ncta, x, x_row_stride, g_num_sms[dev],
+  cudaError_t e = dtk::launch_rmsnorm_qkv_sm100(mx, mw, my, p, ncta, g_num_sms[dev],
                                                 static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
   return DT_OK;

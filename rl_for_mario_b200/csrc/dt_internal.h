@@ -113,9 +113,7 @@ struct RmsQkvParams {
 
 int rmsnorm_qkv_ncta(int N);
 cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w, const CUtensorMap& y,
-                                     const RmsQkvParams& p, int ncta,
-                                     const void* x_ptr, long long x_stride, int num_sms,
-                                     cudaStream_t st);
+                                     const RmsQkvParams& p, int ncta, int num_sms, cudaStream_t st);
 
 // dtype: 0 bf16, 1 fp16, 2 fp32
 cudaError_t launch_kv_write_sm100(const KvWriteParams& prm, int D, int dtype, int B, cudaStream_t stream);

@@ -257,8 +257,7 @@ struct PShape {
 
 __global__ void __launch_bounds__(kPersistThreads, 1)
     dt_rmsnorm_qkv_persist_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                                  const __grid_constant__ CUtensorMap tmY, const __nv_bfloat16* __restrict__ xg,
-                                  long long x_stride, const RmsQkvParams p) {
+                                  const __grid_constant__ CUtensorMap tmY, const RmsQkvParams p) {
   using SH = PShape;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -282,7 +281,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < kPStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], 5);  // MMA commit + one arrival per sum-of-squares warp
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&acc_full[j], 1);
@@ -426,36 +425,51 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     }
     if (lane == 0) bulk_wait<0>();  // output copies complete before the CTA exits
   } else {
-    // Row sums of squares of a 128-row block, one warp per row at a time
-    // (16-byte loads spread over the lanes, then a warp sum).
-    const int nw = warp - 6;  // 0..3: rows nw, nw + 4, ...
-    int bc = 0;
+    // Row sums of squares of a 128-row block, read from the x chunks that the
+    // ring stages for the block's first column tile (no extra pass over x).
+    // These warps take part in every stage's release: empty[s] completes on
+    // the MMA commit plus one arrival per warp.
+    const int rr = (warp - 6) * 32 + lane;  // row of the block
+    int cnt = 0, bc = 0;
     bool ok = true;
     for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++bc) {
       const int sb = bc & 1;
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&ss_empty[sb], ((bc >> 1) & 1) ^ 1, abort_flag, p.status))))
-        break;
-      for (int rr = nw; rr < 128; rr += 4) {
-        const int row_g = rb * 128 + rr;
-        float ss = 0.f;
-        if (row_g < p.M) {
-          const uint4* xr = reinterpret_cast<const uint4*>(xg + (size_t)row_g * x_stride);
-          for (int c = lane; c < p.K / 8; c += 32) {
-            const uint4 u = __ldg(xr + c);
-            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+      float ss0 = 0.f, ss1 = 0.f;
+      for (int ct = 0; ct < nt && ok; ++ct) {
+        for (int kc = 0; kc < nk; ++kc, ++cnt) {
+          const int s = cnt % kPStages;
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (cnt / kPStages) & 1, abort_flag, p.status))))
+            break;
+          if (ct == 0) {
+            // Row rr of the chunk is the 128 bytes at rr * 128 (the swizzle
+            // permutes 16-byte pieces inside the row); start each lane at a
+            // different piece so a quarter warp covers all banks.
+            const uint8_t* row = smem + s * SH::STAGE + rr * 128;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float2 f = p.bf16 ? Elem<true>::to_f2(w4[i]) : Elem<false>::to_f2(w4[i]);
-              ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+            for (int q = 0; q < 8; ++q) {
+              const uint4 u = *reinterpret_cast<const uint4*>(row + (((q + lane) & 7) << 4));
+              const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = p.bf16 ? Elem<true>::to_f2(w4[e]) : Elem<false>::to_f2(w4[e]);
+                ss0 = fmaf(f.x, f.x, ss0);
+                ss1 = fmaf(f.y, f.y, ss1);
+              }
             }
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) ss_s[sb * 128 + rr] = ss;
+        if (ok && ct == 0) {
+          // Publish once the epilogue has released this buffer (row block bc - 2).
+          if (!(ok = __all_sync(0xffffffffu,
+                                mbar_wait(&ss_empty[sb], ((bc >> 1) & 1) ^ 1, abort_flag, p.status))))
+            break;
+          ss_s[sb * 128 + rr] = ss0 + ss1;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ss_full[sb]);
+        }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ss_full[sb]);
     }
   }
   __syncthreads();
@@ -487,15 +501,14 @@ int rmsnorm_qkv_ncta(int N) {
 }
 
 cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w, const CUtensorMap& y,
-                                     const RmsQkvParams& p, int ncta, const void* x_ptr, long long x_stride,
-                                     int num_sms, cudaStream_t st) {
+                                     const RmsQkvParams& p, int ncta, int num_sms, cudaStream_t st) {
   if (ncta == 0) {
     auto k = dt_rmsnorm_qkv_persist_kernel;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PShape::SMEM);
     if (e != cudaSuccess) return e;
     const int nrb = (p.M + 127) / 128;
     const int grid = nrb < num_sms ? nrb : num_sms;
-    k<<<grid, kPersistThreads, PShape::SMEM, st>>>(x, w, y, static_cast<const __nv_bfloat16*>(x_ptr), x_stride, p);
+    k<<<grid, kPersistThreads, PShape::SMEM, st>>>(x, w, y, p);
     return cudaGetLastError();
   }
   switch (ncta) {
