@@ -66,6 +66,38 @@ __device__ __forceinline__ void rope_pairs(float (&v)[64], int lo0, const float*
   }
 }
 
+// The same rotation with duplicated-half tables (cos[d] == cos[d + HALF], the
+// rotate-half layout) staged as fp16 in shared memory: a 128-byte row holds
+// cos[0, HALF) at halves [0, HALF) and sin[0, HALF) at halves [32, 32 + HALF),
+// its 16-byte pieces XOR-swizzled by (row & 7) so the 32 rows of a warp read
+// without bank conflicts.
+template <int HALF>
+__device__ __forceinline__ void rope_pairs_tab(float (&v)[64], int lo0, const uint8_t* trow, int sw) {
+  constexpr int NP = HALF / 8;  // 16-byte pieces per half table
+  uint4 cp[NP], sp[NP];
+#pragma unroll
+  for (int q = 0; q < NP; ++q) {
+    cp[q] = *reinterpret_cast<const uint4*>(trow + ((q ^ sw) << 4));
+    sp[q] = *reinterpret_cast<const uint4*>(trow + (((4 + q) ^ sw) << 4));
+  }
+#pragma unroll
+  for (int q = 0; q < NP; ++q) {
+    const uint32_t cw[4] = {cp[q].x, cp[q].y, cp[q].z, cp[q].w};
+    const uint32_t sw4[4] = {sp[q].x, sp[q].y, sp[q].z, sp[q].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 c2 = __half22float2(*reinterpret_cast<const __half2*>(&cw[e]));
+      const float2 s2 = __half22float2(*reinterpret_cast<const __half2*>(&sw4[e]));
+      const int d = lo0 + q * 8 + 2 * e;
+      const float x0 = v[d], x1 = v[d + HALF], y0 = v[d + 1], y1 = v[d + 1 + HALF];
+      v[d] = x0 * c2.x - x1 * s2.x;
+      v[d + HALF] = x1 * c2.x + x0 * s2.x;
+      v[d + 1] = y0 * c2.y - y1 * s2.y;
+      v[d + 1 + HALF] = y1 * c2.y + y0 * s2.y;
+    }
+  }
+}
+
 template <int NCTA>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     dt_rmsnorm_qkv_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
@@ -244,9 +276,11 @@ struct PShape {
   static constexpr int A_BYTES = 128 * kKC * 2;
   static constexpr int B_BYTES = kPN * kKC * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int OFF_ST = kPStages * STAGE;            // output staging: [2][4 warps][32 rows][64 cols]
+  static constexpr int OFF_ST = kPStages * STAGE;            // output staging: [4 warps][32 rows][64 cols]
   static constexpr int ST_WARP = 32 * 64 * 2;                // one warp's slice (4 swizzle atoms)
-  static constexpr int OFF_SS = OFF_ST + 2 * 4 * ST_WARP;    // [2][128] floats
+  static constexpr int OFF_TAB = OFF_ST + 4 * ST_WARP;       // RoPE tables: [4 warps][32 rows][128 B]
+  static constexpr int TAB_WARP = 32 * 128;
+  static constexpr int OFF_SS = OFF_TAB + 4 * TAB_WARP;      // [2][128] floats
   static constexpr int OFF_BAR = OFF_SS + 2 * 128 * 4;
   // full[S], empty[S], acc_full[2], acc_empty[2], ss_full[2], ss_empty[2], drain
   static constexpr int NBAR = 2 * kPStages + 9;
@@ -263,6 +297,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* ss_s = reinterpret_cast<float*>(smem + SH::OFF_SS);
   uint8_t* st_s = smem + SH::OFF_ST;
+  uint8_t* tab_s = smem + SH::OFF_TAB;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SH::OFF_BAR);
   uint64_t* empty = full + kPStages;
   uint64_t* acc_full = empty + kPStages;
@@ -366,6 +401,32 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       const int pos = p.rope_cols > 0 ? row_g % p.seq_len : 0;
       const float* crow = p.cos + (size_t)pos * p.cs_stride;
       const float* srow = p.sin + (size_t)pos * p.cs_stride;
+      // Stage this warp's 32 table rows once per row block (coalesced reads,
+      // fp16).  Tables whose halves are not duplicated keep the direct path.
+      bool tab_ok = false;
+      if (p.rope_cols > 0) {
+        const int half = p.head_dim >> 1;  // 16 or 32
+        const int rpi = 32 / half;         // rows per pass
+        const int dl = lane & (half - 1);
+        bool dup = true;
+        for (int i0 = 0; i0 < 32; i0 += rpi) {
+          const int i = i0 + lane / half;  // row of the warp slice
+          const int pi = (rb * 128 + wq * 32 + i) % p.seq_len;
+          const float* cr = p.cos + (size_t)pi * p.cs_stride;
+          const float* sr = p.sin + (size_t)pi * p.cs_stride;
+          const float c0 = __ldg(cr + dl), c1 = __ldg(cr + dl + half);
+          const float s0 = __ldg(sr + dl), s1 = __ldg(sr + dl + half);
+          dup = dup && c0 == c1 && s0 == s1;
+          uint8_t* trow = tab_s + wq * SH::TAB_WARP + i * 128;
+          const int sw = i & 7;
+          // halves dl of the cos table (pieces 0..3) and of the sin table (4..7)
+          *reinterpret_cast<__half*>(trow + (((dl >> 3) ^ sw) << 4) + (dl & 7) * 2) = __float2half_rn(c0);
+          *reinterpret_cast<__half*>(trow + (((4 + (dl >> 3)) ^ sw) << 4) + (dl & 7) * 2) = __float2half_rn(s0);
+        }
+        tab_ok = __all_sync(0xffffffffu, dup);
+        __syncwarp();
+      }
+      const uint8_t* my_tab = tab_s + wq * SH::TAB_WARP + lane * 128;
       for (int ct = 0; ct < nt && ok; ++ct, ++tc) {
         const int buf = tc & 1;
         if (!(ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (tc >> 1) & 1, abort_flag, p.status)))) break;
@@ -378,9 +439,16 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 #pragma unroll
           for (int i = 0; i < 64; ++i) v[i] *= rs;
           if (n0 + c < p.rope_cols && row_g < p.M) {
-            if (p.head_dim == 64)
+            if (tab_ok) {
+              if (p.head_dim == 64)
+                rope_pairs_tab<32>(v, 0, my_tab, lane & 7);
+              else {
+                rope_pairs_tab<16>(v, 0, my_tab, lane & 7);
+                rope_pairs_tab<16>(v, 32, my_tab, lane & 7);
+              }
+            } else if (p.head_dim == 64) {
               rope_pairs<32>(v, 0, crow, srow);
-            else {
+            } else {
               rope_pairs<16>(v, 0, crow, srow);
               rope_pairs<16>(v, 32, crow, srow);
             }
@@ -389,8 +457,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
           // swizzle) and stores it with one TMA copy: whole rows per copy
           // instead of one line per thread.  Rows past M and columns past N
           // are clipped by the copy.
-          uint8_t* stb = st_s + ((sc & 1) * 4 + wq) * SH::ST_WARP;
-          if (lane == 0 && sc >= 2) bulk_wait_read<1>();  // the copy that last read this buffer is done
+          uint8_t* stb = st_s + wq * SH::ST_WARP;
+          if (lane == 0 && sc >= 1) bulk_wait_read<0>();  // the previous copy has read the slice
           __syncwarp();
 #pragma unroll
           for (int c8 = 0; c8 < 64; c8 += 8) {

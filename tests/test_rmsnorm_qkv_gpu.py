@@ -70,8 +70,12 @@ def test_fused_block_matches_unfused_block():
 @pytest.mark.parametrize("B,S,K,Hq,Hkv,D", [(2, 96, 256, 8, 2, 32), (3, 50, 768, 12, 4, 64), (1, 7, 128, 4, 4, 32),
                                             (2, 130, 512, 8, 8, 64)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_rmsnorm_qkv_rope_matches_reference(B, S, K, Hq, Hkv, D, dtype):
-    """RMSNorm -> q/k/v projections -> rotate-half RoPE of q and k, fused in one kernel."""
+@pytest.mark.parametrize("tables", ["rotate_half", "arbitrary"])
+def test_rmsnorm_qkv_rope_matches_reference(B, S, K, Hq, Hkv, D, dtype, tables):
+    """RMSNorm -> q/k/v projections -> rotate-half RoPE of q and k, fused in one kernel.
+
+    "rotate_half" tables repeat their halves (the reference's cat([cos, cos]));
+    "arbitrary" tables do not, and take the kernels' general table path."""
     from oracle import apply_rotary_pos_emb, precompute_freqs_cis
     from rl_for_mario_b200.kernels import device_status, fold_norm_weight, rmsnorm_qkv
 
@@ -81,6 +85,8 @@ def test_rmsnorm_qkv_rope_matches_reference(B, S, K, Hq, Hkv, D, dtype):
     wq, wk, wv = (torch.randn(h * D, K, generator=g) / K ** 0.5 for h in (Hq, Hkv, Hkv))
     wf = fold_norm_weight(wq, wk, wv, wn, dtype).cuda()
     cos, sin = precompute_freqs_cis(D, S + 5)
+    if tables == "arbitrary":
+        cos, sin = (torch.rand(S + 5, D, generator=g) * 2 - 1 for _ in range(2))
     y = rmsnorm_qkv(x.cuda(), wf, 1e-5, rope=(cos[:S].cuda(), sin[:S].cuda(), (Hq + Hkv) * D, D))
     assert device_status() == 0
     xn = rmsnorm_ref(x.float(), wn)
