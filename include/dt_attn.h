@@ -135,6 +135,21 @@ int dt_rmsnorm_qkv_rope(const void* x, int64_t x_row_stride, const void* w_fused
                         void* stream);
 
 /*
+ * Fused post-attention RMSNorm + SwiGLU up-projection:
+ *   y[m, j] = silu(g[m, j]) * u[m, j],  [g | u] = rsqrt(mean(x[m, :]^2) + eps) * (x[m, :] @ W^T)
+ * Replaces post_attention_layernorm (RMSNorm, model_decision_transformer.py:76-86,
+ * called at :302-303) and FeedForward's gate_proj / up_proj / silu / product
+ * (:256-271, before down_proj).  w_fused ([2 N, K], K contiguous) holds the
+ * gate and up rows, each scaled by the norm weight, interleaved in blocks of
+ * 64 rows: rows [128 b, 128 b + 64) are gate rows [64 b, 64 b + 64) and rows
+ * [128 b + 64, 128 b + 128) the matching up rows.  x [M, K], y [M, N]; N (the
+ * FFN width) a multiple of 64 and >= 128; bf16 or fp16; K and row strides
+ * multiples of 8, 16-byte aligned pointers.
+ */
+int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, void* y, int64_t y_row_stride,
+                      int M, int K, int N, float eps, int dtype, void* stream);
+
+/*
  * Synchronises `stream`, then returns and clears the device status word that
  * the kernels of this library write when a bounded wait runs out or a
  * device-side check fails (0 = no error).  Used by tests and debugging.

@@ -128,7 +128,9 @@ class FastDTAttention(nn.Module):
     # ------------------------------------------------------------------ forward
     def forward(self, x: Tensor, position_embeddings: Tuple[Tensor, Tensor],
                 past_key_value=None, use_cache: bool = False, attention_mask: Optional[Tensor] = None,
-                raw_input: bool = False):
+                raw_input: bool = False, residual: Optional[Tensor] = None):
+        """``residual`` (the block input, [B, S, H]) is added to the output: one
+        GEMM with the residual as its accumulator input when dropout is off."""
         if not x.is_cuda:
             raise ValueError("FastDTAttention runs on CUDA only (no CPU path)")
         bsz, seq_len, _ = x.shape
@@ -185,7 +187,14 @@ class FastDTAttention(nn.Module):
                 past_kv = (kc, vc) if use_cache else None
 
         out = out.reshape(bsz, seq_len, -1).to(x.dtype)
-        return self.resid_dropout(self.o_proj(out)), past_kv
+        if residual is None:
+            return self.resid_dropout(self.o_proj(out)), past_kv
+        w = self.o_proj.weight
+        if ((not self.training or self.resid_dropout.p == 0) and self.o_proj.bias is None
+                and residual.dtype == out.dtype == w.dtype):
+            r2 = residual.reshape(-1, residual.shape[-1])
+            return torch.addmm(r2, out.reshape(-1, out.shape[-1]), w.t()).view(residual.shape), past_kv
+        return residual + self.resid_dropout(self.o_proj(out)), past_kv
 
 
 def swap_attention(model: nn.Module, config, **kw) -> int:

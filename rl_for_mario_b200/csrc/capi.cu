@@ -387,12 +387,14 @@ namespace {
 int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const void* w_fused, void* y,
                      int64_t y_row_stride, int M, int K, int N, float eps, const float* cos_tab, const float* sin_tab,
                      int64_t cos_stride, int cos_rows, int seq_len, int rope_cols, int head_dim, int dtype,
-                     void* stream) {
+                     void* stream, int swiglu = 0) {
+  // N counts rows of w_fused; with swiglu, y has N / 2 columns.
   if (!x || !w_fused || !y) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
   if (M < 1 || K < 1 || N < 1) return fail(DT_ERR_INVALID, "%s: sizes must be positive", fn);
   if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
     return fail(DT_ERR_UNSUPPORTED, "%s: dtype %d not supported (bf16 / fp16)", fn, dtype);
-  if (K % 8 || N % 8 || x_row_stride % 8 || y_row_stride % 8 || x_row_stride < K || y_row_stride < N)
+  const int y_cols = swiglu ? N / 2 : N;
+  if (K % 8 || N % 8 || x_row_stride % 8 || y_row_stride % 8 || x_row_stride < K || y_row_stride < y_cols)
     return fail(DT_ERR_INVALID, "%s: K, N and row strides must be multiples of 8 (strides >= K / N)", fn);
   if (!aligned16(x) || !aligned16(w_fused) || !aligned16(y)) return fail(DT_ERR_INVALID, "%s: 16-byte alignment", fn);
   if (!(eps > 0.f)) return fail(DT_ERR_INVALID, "%s: eps must be positive", fn);
@@ -402,19 +404,22 @@ int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const 
   if (rc) return rc;
   if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
   const bool bf16 = dtype == DT_DTYPE_BF16;
-  const int ncta = dtk::rmsnorm_qkv_ncta(N);  // 0: persistent kernel, 256-column tiles
+  // 0: persistent kernel, 256-column tiles (the only one with the SwiGLU epilogue)
+  const int ncta = swiglu ? 0 : dtk::rmsnorm_qkv_ncta(N);
   const int nsub = ncta == 0 ? 256 : (ncta <= 256 ? ncta : ncta / 2);
   CUtensorMap mx, mw, my;
   if ((rc = encode_2d(&mx, x, bf16, (uint64_t)K, (uint64_t)M, (uint64_t)x_row_stride, 64, 128, "x"))) return rc;
   if ((rc = encode_2d(&mw, w_fused, bf16, (uint64_t)K, (uint64_t)N, (uint64_t)K, 64, (uint32_t)nsub, "w"))) return rc;
   memset(&my, 0, sizeof(my));
   // The persistent kernel stores 32 x 64 output slices (one per epilogue warp) by TMA.
-  if (ncta == 0 && (rc = encode_2d(&my, y, bf16, (uint64_t)N, (uint64_t)M, (uint64_t)y_row_stride, 64, 32, "y")))
+  if (ncta == 0 &&
+      (rc = encode_2d(&my, y, bf16, (uint64_t)y_cols, (uint64_t)M, (uint64_t)y_row_stride, 64, 32, "y")))
     return rc;
   dtk::RmsQkvParams p;
   p.y = y; p.status = status; p.y_stride = y_row_stride; p.M = M; p.K = K; p.N = N; p.bf16 = bf16 ? 1 : 0; p.eps = eps;
   p.cos = cos_tab; p.sin = sin_tab; p.rope_cols = rope_cols; p.head_dim = head_dim; p.seq_len = seq_len;
   p.cs_stride = (int)cos_stride;
+  p.swiglu = swiglu;
   cudaError_t e = dtk::launch_rmsnorm_qkv_sm100(mx, mw, my, p, ncta, g_num_sms[dev],
                                                 static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
@@ -444,4 +449,13 @@ extern "C" int dt_rmsnorm_qkv_rope(const void* x, int64_t x_row_stride, const vo
     return fail(DT_ERR_INVALID, "%s: cos / sin must be 16-byte aligned with row stride >= head_dim, %% 4", fn);
   return rmsnorm_qkv_impl(fn, x, x_row_stride, w_fused, y, y_row_stride, M, K, N, eps, cos_tab, sin_tab, cos_stride,
                           cos_rows, seq_len, rope_cols, head_dim, dtype, stream);
+}
+
+extern "C" int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, void* y,
+                                 int64_t y_row_stride, int M, int K, int N, float eps, int dtype, void* stream) {
+  const char* fn = "dt_rmsnorm_swiglu";
+  if (N < 128 || N % 64) return fail(DT_ERR_INVALID, "%s: the output width must be a multiple of 64, >= 128", fn);
+  if (N > (1 << 29)) return fail(DT_ERR_INVALID, "%s: output width too large", fn);
+  return rmsnorm_qkv_impl(fn, x, x_row_stride, w_fused, y, y_row_stride, M, K, 2 * N, eps, nullptr, nullptr, 0, 0, 1,
+                          0, 0, dtype, stream, 1);
 }

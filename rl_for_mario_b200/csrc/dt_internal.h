@@ -108,6 +108,7 @@ struct RmsQkvParams {
   long long y_stride;
   int M, K, N, bf16;
   int rope_cols, head_dim, seq_len, cs_stride;  // rope_cols = 0: no rotation
+  int swiglu;  // 1: W rows are 64-row gate / up blocks, y[:, j] = silu(gate_j) * up_j (N / 2 columns)
   float eps;
 };
 

@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             rope_pairs<32>(v, 0, crow, srow);
           else {
             rope_pairs<16>(v, 0, crow, srow);
-            rope_pairs<16>(v, 32, crow, srow);
+            if (n0 + c + 32 < p.rope_cols) rope_pairs<16>(v, 32, crow, srow);  // second head may be a v head
           }
         }
         if (row_g < p.M) {
@@ -432,6 +432,49 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         if (!(ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (tc >> 1) & 1, abort_flag, p.status)))) break;
         tc_fence_after();
         const int n0 = ct * kPN;
+        if (p.swiglu) {
+          // Column pairs (gate block, up block) of 64: one 64-column output
+          // slice per pair, at output column (n0 + c) / 2.
+          for (int c = 0; c < kPN && n0 + c < p.N; c += 128) {
+            uint8_t* stb = st_s + wq * SH::ST_WARP;
+            if (lane == 0 && sc >= 1) bulk_wait_read<0>();
+            __syncwarp();
+#pragma unroll
+            for (int hh = 0; hh < 64; hh += 32) {
+              float gv[32], uv[32];
+              tmem_ld32(t_row + buf * kPN + c + hh, gv);
+              tmem_ld32(t_row + buf * kPN + c + 64 + hh, uv);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float gg = gv[i] * rs;
+                gv[i] = gg / (1.f + __expf(-gg)) * (uv[i] * rs);  // silu(gate) * up
+              }
+#pragma unroll
+              for (int c8 = 0; c8 < 32; c8 += 8) {
+                uint4 o;
+                if (p.bf16) {
+                  o.x = Elem<true>::from_f2(gv[c8], gv[c8 + 1]);
+                  o.y = Elem<true>::from_f2(gv[c8 + 2], gv[c8 + 3]);
+                  o.z = Elem<true>::from_f2(gv[c8 + 4], gv[c8 + 5]);
+                  o.w = Elem<true>::from_f2(gv[c8 + 6], gv[c8 + 7]);
+                } else {
+                  o.x = Elem<false>::from_f2(gv[c8], gv[c8 + 1]);
+                  o.y = Elem<false>::from_f2(gv[c8 + 2], gv[c8 + 3]);
+                  o.z = Elem<false>::from_f2(gv[c8 + 4], gv[c8 + 5]);
+                  o.w = Elem<false>::from_f2(gv[c8 + 6], gv[c8 + 7]);
+                }
+                *reinterpret_cast<uint4*>(stb + lane * 128 + ((((hh + c8) >> 3) ^ (lane & 7)) << 4)) = o;
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmY, stb, (n0 + c) >> 1, rb * 128 + wq * 32);
+              bulk_commit();
+            }
+            ++sc;
+          }
+        } else
         for (int c = 0; c < kPN; c += 64) {
           float v[64];
           tmem_ld32(t_row + buf * kPN + c, *reinterpret_cast<float(*)[32]>(&v[0]));
@@ -444,13 +487,13 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                 rope_pairs_tab<32>(v, 0, my_tab, lane & 7);
               else {
                 rope_pairs_tab<16>(v, 0, my_tab, lane & 7);
-                rope_pairs_tab<16>(v, 32, my_tab, lane & 7);
+                if (n0 + c + 32 < p.rope_cols) rope_pairs_tab<16>(v, 32, my_tab, lane & 7);
               }
             } else if (p.head_dim == 64) {
               rope_pairs<32>(v, 0, crow, srow);
             } else {
               rope_pairs<16>(v, 0, crow, srow);
-              rope_pairs<16>(v, 32, crow, srow);
+              if (n0 + c + 32 < p.rope_cols) rope_pairs<16>(v, 32, crow, srow);  // second head may be a v head
             }
           }
           // Each warp stages its 32 x 64 slice in shared memory (128-byte

@@ -4,9 +4,11 @@ A restatement of the reference model (model/model_decision_transformer.py:
 config :17-55, RMSNorm :76-86, RoPE tables :93-99, FeedForward :256-271,
 block :278-304, state encoder :315-341, backbone :348-461, wrapper :468-548)
 whose attention is ``FastDTAttention``.  Parameter names match the reference,
-so a reference state_dict loads unchanged (checkpoint compatibility).  The
-glue around the attention (CNN encoder, embeddings, norms, SwiGLU FFN, heads)
-runs as ordinary PyTorch on the GPU.
+so a reference state_dict loads unchanged (checkpoint compatibility).  With
+``fuse_norms()`` a block runs as: RMSNorm + Q/K/V + RoPE kernel, attention
+kernel, o_proj GEMM with the residual as accumulator input, RMSNorm + gate/up
++ SwiGLU kernel, down_proj GEMM with the residual; the rest (CNN encoder,
+embeddings, final norm, heads) runs as PyTorch on the GPU.
 """
 from __future__ import annotations
 
@@ -17,6 +19,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import kernels
 from .attention import FastDTAttention
 from .cache import LayerKV, PagedKVCache
 
@@ -103,14 +106,43 @@ class DTBlock(nn.Module):
         self.mlp = FeedForward(cfg)
 
     def fuse_norm(self, on: bool = True) -> None:
-        """Runs input_layernorm inside the attention's fused RMSNorm + QKV kernel."""
+        """Runs input_layernorm inside the attention's fused RMSNorm + QKV kernel,
+        the residual adds inside the o_proj / down_proj GEMMs and
+        post_attention_layernorm + gate / up + SwiGLU in one kernel (16-bit
+        weights, dropout off)."""
         self.self_attn.set_fused_norm(self.input_layernorm if on else None)
+        self._swiglu_w = None
+
+    def _swiglu_weight(self, dtype: torch.dtype) -> Tensor:
+        ps = (self.mlp.gate_proj.weight, self.mlp.up_proj.weight, self.post_attention_layernorm.weight)
+        key = tuple((p.data_ptr(), p._version) for p in ps) + (dtype,)
+        if getattr(self, "_swiglu_w", None) is None or self._swiglu_key != key:
+            self._swiglu_w = kernels.fold_swiglu_weight(*ps, dtype=dtype)
+            self._swiglu_key = key
+        return self._swiglu_w
+
+    def _fused_mlp_ok(self, h: Tensor) -> bool:
+        mlp = self.mlp
+        inter = mlp.gate_proj.weight.shape[0]
+        return (h.is_cuda and h.dtype in (torch.bfloat16, torch.float16)
+                and mlp.down_proj.weight.dtype == h.dtype and mlp.down_proj.bias is None
+                and mlp.gate_proj.bias is None and mlp.up_proj.bias is None
+                and (not self.training or mlp.dropout.p == 0) and inter % 64 == 0 and inter >= 128
+                and h.shape[-1] % 8 == 0)
 
     def forward(self, hidden_states, position_embeddings, past_key_value=None, use_cache=False,
                 attention_mask=None):
         if self.self_attn._fused_norm is not None:
             h, present = self.self_attn(hidden_states, position_embeddings, past_key_value=past_key_value,
-                                        use_cache=use_cache, attention_mask=attention_mask, raw_input=True)
+                                        use_cache=use_cache, attention_mask=attention_mask, raw_input=True,
+                                        residual=hidden_states)
+            if self._fused_mlp_ok(h):
+                a = kernels.rmsnorm_swiglu(h, self._swiglu_weight(h.dtype), self.post_attention_layernorm.eps)
+                h2 = h.reshape(-1, h.shape[-1])
+                h = torch.addmm(h2, a.reshape(-1, a.shape[-1]), self.mlp.down_proj.weight.t()).view(h.shape)
+            else:
+                h = h + self.mlp(self.post_attention_layernorm(h))
+            return h, present
         else:
             h, present = self.self_attn(self.input_layernorm(hidden_states), position_embeddings,
                                         past_key_value=past_key_value, use_cache=use_cache,
@@ -143,12 +175,30 @@ class MarioStateEncoder(nn.Module):
         # frames.
         big = (s.amax() > 1) if s.dtype == torch.uint8 else (s.to(dt).amax() > 1.0)
         w0 = torch.where(big, conv0.weight / 255.0, conv0.weight)
-        # One pass: frames -> compute dtype, channels-last (the layout the
-        # convolution kernels run in, so no layout conversions per layer).
-        x = torch.empty(s.shape, dtype=dt, device=s.device, memory_format=torch.channels_last)
-        x.copy_(s)
         cl = torch.channels_last
-        x = F.relu(F.conv2d(x, w0.contiguous(memory_format=cl), conv0.bias, stride=conv0.stride), inplace=True)
+        k0, st0 = conv0.kernel_size[0], conv0.stride[0]
+        if (conv0.kernel_size == (k0, k0) and conv0.stride == (st0, st0) and conv0.padding == (0, 0)
+                and k0 % st0 == 0 and H % st0 == 0 and W % st0 == 0):
+            # Space-to-depth: a k x k stride-st convolution over C channels is a
+            # (k/st) x (k/st) stride-1 convolution over C*st*st channels of the
+            # frames cut into st x st blocks (same products, same sums).  With
+            # 4 x 8 x 8 / 4 that turns a 4-channel input, which has no
+            # tensor-core convolution, into a 64-channel one.  One pass writes
+            # the blocked frames in the compute dtype, channels-last.
+            f = st0
+            x = torch.empty((B * T, C * f * f, H // f, W // f), dtype=dt, device=s.device, memory_format=cl)
+            x.permute(0, 2, 3, 1).view(B * T, H // f, W // f, C, f, f).copy_(
+                s.view(B * T, C, H // f, f, W // f, f).permute(0, 2, 4, 1, 3, 5))
+            kb = k0 // f
+            w0 = (w0.view(conv0.out_channels, C, kb, f, kb, f).permute(0, 1, 3, 5, 2, 4)
+                  .reshape(conv0.out_channels, C * f * f, kb, kb))
+            x = F.relu(F.conv2d(x, w0.contiguous(memory_format=cl), conv0.bias), inplace=True)
+        else:
+            # One pass: frames -> compute dtype, channels-last (the layout the
+            # convolution kernels run in, so no layout conversions per layer).
+            x = torch.empty(s.shape, dtype=dt, device=s.device, memory_format=cl)
+            x.copy_(s)
+            x = F.relu(F.conv2d(x, w0.contiguous(memory_format=cl), conv0.bias, stride=conv0.stride), inplace=True)
         x = F.relu(F.conv2d(x, conv1.weight.contiguous(memory_format=cl), conv1.bias, stride=conv1.stride),
                    inplace=True)
         x = F.relu(F.conv2d(x, conv2.weight.contiguous(memory_format=cl), conv2.bias, stride=conv2.stride),

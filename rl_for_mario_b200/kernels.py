@@ -189,6 +189,42 @@ def fold_norm_weight(w_q: Tensor, w_k: Tensor, w_v: Tensor, w_norm: Tensor, dtyp
     return w.to(dtype).contiguous()
 
 
+def fold_swiglu_weight(w_gate: Tensor, w_up: Tensor, w_norm: Tensor, dtype: torch.dtype) -> Tensor:
+    """The weight of rmsnorm_swiglu: gate and up rows scaled by the norm weight,
+    interleaved in blocks of 64 rows ([gate 0:64; up 0:64; gate 64:128; ...])."""
+    inter, hidden = w_gate.shape
+    if w_up.shape != w_gate.shape or inter % 64:
+        raise ValueError("gate / up weights must be equal [F, H] with F a multiple of 64")
+    nw = w_norm.float()[None, None, :]
+    g = w_gate.float().view(inter // 64, 64, hidden) * nw
+    u = w_up.float().view(inter // 64, 64, hidden) * nw
+    return torch.stack((g, u), dim=1).reshape(2 * inter, hidden).to(dtype).contiguous()
+
+
+def rmsnorm_swiglu(x: Tensor, w_fused: Tensor, eps: float, out: Optional[Tensor] = None) -> Tensor:
+    """silu(g) * u with [g | u] = RMSNorm(x) @ [W_gate; W_up]^T: the post-attention
+    norm and the SwiGLU up-projection of the block's MLP in one kernel.
+
+    x [..., K] bf16/fp16 -> y [..., F], ``w_fused`` = fold_swiglu_weight(...) [2F, K].
+    """
+    _require_cuda(x, w_fused, out)
+    K = x.shape[-1]
+    F2 = w_fused.shape[0]
+    if w_fused.shape[1] != K or w_fused.dtype != x.dtype or not w_fused.is_contiguous() or F2 % 128:
+        raise ValueError("w_fused must be a contiguous [2F, K] tensor of x's dtype (F a multiple of 64)")
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (F2 // 2,), dtype=x.dtype, device=x.device)
+    o2 = out.view(-1, F2 // 2)
+    rc = _lib.load().dt_rmsnorm_swiglu(_ptr(x2), x2.stride(0), _ptr(w_fused), _ptr(o2), o2.stride(0), M, K,
+                                       F2 // 2, float(eps), _dtype_code(x), _stream_ptr(x.device))
+    _lib.check("dt_rmsnorm_swiglu", rc)
+    return out
+
+
 def rmsnorm_qkv(x: Tensor, w_fused: Tensor, eps: float, out: Optional[Tensor] = None,
                 rope: Optional[Tuple[Tensor, Tensor, int, int]] = None) -> Tensor:
     """y = RMSNorm(x) @ [Wq; Wk; Wv]^T with the norm weight folded into ``w_fused`` [N, K].

@@ -172,3 +172,21 @@ def test_dt_bf16_model_argmax_agreement():
     ref = torch.from_numpy(g["logits"])
     err = (out.action_logits.float().cpu() - ref).abs().max().item()
     assert err < 5e-2, f"bf16 model logits max abs err {err:.3e}"
+
+
+@pytest.mark.gpu
+def test_dt_bf16_fused_blocks_match_reference():
+    """bf16 model with fused blocks (RMSNorm+QKV+RoPE, residual GEMMs, RMSNorm+SwiGLU):
+    logits within 5e-2 of the fp32 reference and of the unfused bf16 model."""
+    g, model, states, actions, rtg, ts = _dt(torch.bfloat16)
+    T = int(g["T"])
+    mask = (torch.arange(T)[None] >= torch.from_numpy(g["pad_steps"]).long()[:, None]).long().cuda()
+    with torch.no_grad():
+        plain = model(states[:, :T], actions[:, :T], rtg[:, :T], ts[:, :T], attention_mask=mask)
+        model.fuse_norms()
+        out = model(states[:, :T], actions[:, :T], rtg[:, :T], ts[:, :T], attention_mask=mask)
+    ref = torch.from_numpy(g["logits"])
+    err = (out.action_logits.float().cpu() - ref).abs().max().item()
+    assert err < 5e-2, f"fused bf16 model logits max abs err {err:.3e}"
+    d = (out.action_logits.float() - plain.action_logits.float()).abs().max().item()
+    assert d < 5e-2, d

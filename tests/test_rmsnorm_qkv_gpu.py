@@ -68,7 +68,7 @@ def test_fused_block_matches_unfused_block():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("B,S,K,Hq,Hkv,D", [(2, 96, 256, 8, 2, 32), (3, 50, 768, 12, 4, 64), (1, 7, 128, 4, 4, 32),
-                                            (2, 130, 512, 8, 8, 64)])
+                                            (2, 130, 512, 8, 8, 64), (2, 21, 128, 4, 1, 32), (3, 40, 256, 19, 2, 32)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("tables", ["rotate_half", "arbitrary"])
 def test_rmsnorm_qkv_rope_matches_reference(B, S, K, Hq, Hkv, D, dtype, tables):
@@ -120,3 +120,37 @@ def test_fused_block_with_rope_epilogue_matches_unfused_block(hidden, heads, kv_
         out, _ = blk(x, (cos, sin), attention_mask=mask)
     err = (out.float() - ref.float()).abs().max().item()
     assert err < 6e-2, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,F", [(1, 256, 704), (300, 256, 704), (777, 768, 2048), (130, 128, 128),
+                                   (4096, 512, 192)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rmsnorm_swiglu_matches_reference(M, K, F, dtype):
+    """post_attention_layernorm -> silu(gate_proj) * up_proj (FeedForward before down_proj)."""
+    import torch.nn.functional as Fn
+    from rl_for_mario_b200.kernels import device_status, fold_swiglu_weight, rmsnorm_swiglu
+
+    g = torch.Generator().manual_seed(M + K + F)
+    x = (torch.randn(M, K, generator=g) * 2).to(dtype)
+    wn = 1 + 0.1 * torch.randn(K, generator=g)
+    wg, wu = (torch.randn(F, K, generator=g) / K ** 0.5 for _ in range(2))
+    wf = fold_swiglu_weight(wg, wu, wn, dtype).cuda()
+    y = rmsnorm_swiglu(x.cuda(), wf, 1e-5)
+    assert device_status() == 0
+    xn = rmsnorm_ref(x.float(), wn)
+    ref = Fn.silu(xn @ wg.t()) * (xn @ wu.t())
+    err = (y.float().cpu() - ref).abs()
+    tol = 2e-2 if dtype == torch.bfloat16 else 4e-3
+    assert (err <= tol + tol * ref.abs()).all(), f"max err {err.max().item():.3e}"
+
+
+@pytest.mark.gpu
+def test_rmsnorm_swiglu_rejects_bad_widths():
+    from rl_for_mario_b200.kernels import rmsnorm_swiglu
+
+    x = torch.zeros(4, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        rmsnorm_swiglu(x, torch.zeros(2 * 96, 64, dtype=torch.bfloat16, device="cuda"), 1e-5)
+    with pytest.raises(RuntimeError):
+        rmsnorm_swiglu(x, torch.zeros(2 * 64, 64, dtype=torch.bfloat16, device="cuda"), 1e-5)
