@@ -150,6 +150,18 @@ int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, 
                       int M, int K, int N, float eps, int dtype, void* stream);
 
 /*
+ * State-encoder input: uint8 frame stacks [N, C, H, W] -> 16-bit 4 x 4
+ * space-to-depth blocks, channels-last [N, H/4, W/4, C*16] with channel
+ * c*16 + dy*4 + dx = frames[n, c, 4Y + dy, 4X + dx] (values 0..255, exact).
+ * With the first convolution's weight regrouped the same way (and scaled by
+ * 1/255), the reference's frames / 255 -> Conv2d(C, 32, 8, stride 4)
+ * (model_decision_transformer.py:315-341, division at :338) becomes a 2 x 2
+ * stride-1 convolution over C*16 channels.  H, W multiples of 4; frames
+ * 4-byte aligned, out 16-byte aligned; bf16 or fp16 output.
+ */
+int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int C, int H, int W, int dtype, void* stream);
+
+/*
  * Synchronises `stream`, then returns and clears the device status word that
  * the kernels of this library write when a bounded wait runs out or a
  * device-side check fails (0 = no error).  Used by tests and debugging.

@@ -368,7 +368,7 @@ int dt_kv_write(const void* k, const void* v, void* k_pages, void* v_pages, int 
 
 namespace {
 int encode_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t rows, uint64_t row_stride_el,
-              uint32_t box_inner, uint32_t box_rows, const char* name) {
+              uint32_t box_inner, uint32_t box_rows, const char* name, int swizzle_bytes = 128) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
   cuuint64_t dims[2] = {inner, rows};
@@ -377,7 +377,8 @@ int encode_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uin
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(DT_ERR_INVALID, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name, (int)r);
   return DT_OK;
 }
@@ -408,8 +409,12 @@ int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const 
   const int ncta = swiglu ? 0 : dtk::rmsnorm_qkv_ncta(N);
   const int nsub = ncta == 0 ? 256 : (ncta <= 256 ? ncta : ncta / 2);
   CUtensorMap mx, mw, my;
-  if ((rc = encode_2d(&mx, x, bf16, (uint64_t)K, (uint64_t)M, (uint64_t)x_row_stride, 64, 128, "x"))) return rc;
-  if ((rc = encode_2d(&mw, w_fused, bf16, (uint64_t)K, (uint64_t)N, (uint64_t)K, 64, (uint32_t)nsub, "w"))) return rc;
+  // The persistent kernel stages kPersistKChunk-wide K slices (32: 64-byte rows, 64-byte swizzle).
+  const uint32_t kbox = ncta == 0 ? dtk::kPersistKChunk : 64;
+  const int ksw = (int)kbox * 2;
+  if ((rc = encode_2d(&mx, x, bf16, (uint64_t)K, (uint64_t)M, (uint64_t)x_row_stride, kbox, 128, "x", ksw))) return rc;
+  if ((rc = encode_2d(&mw, w_fused, bf16, (uint64_t)K, (uint64_t)N, (uint64_t)K, kbox, (uint32_t)nsub, "w", ksw)))
+    return rc;
   memset(&my, 0, sizeof(my));
   // The persistent kernel stores 32 x 64 output slices (one per epilogue warp) by TMA.
   if (ncta == 0 &&
@@ -449,6 +454,28 @@ extern "C" int dt_rmsnorm_qkv_rope(const void* x, int64_t x_row_stride, const vo
     return fail(DT_ERR_INVALID, "%s: cos / sin must be 16-byte aligned with row stride >= head_dim, %% 4", fn);
   return rmsnorm_qkv_impl(fn, x, x_row_stride, w_fused, y, y_row_stride, M, K, N, eps, cos_tab, sin_tab, cos_stride,
                           cos_rows, seq_len, rope_cols, head_dim, dtype, stream);
+}
+
+extern "C" int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int C, int H, int W, int dtype,
+                                   void* stream) {
+  const char* fn = "dt_frames_to_blocks";
+  if (!frames || !out) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
+  if (N < 1 || C < 1 || H < 4 || W < 4 || H % 4 || W % 4)
+    return fail(DT_ERR_INVALID, "%s: N, C >= 1 and H, W positive multiples of 4 required", fn);
+  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
+    return fail(DT_ERR_UNSUPPORTED, "%s: dtype %d not supported (bf16 / fp16)", fn, dtype);
+  if ((reinterpret_cast<uintptr_t>(frames) & 3) || !aligned16(out))
+    return fail(DT_ERR_INVALID, "%s: frames must be 4-byte and out 16-byte aligned", fn);
+  if (N * (int64_t)(H / 4) * (W / 4) > (int64_t)0x7fffffff * 255)
+    return fail(DT_ERR_INVALID, "%s: too many frames for one launch", fn);
+  int dev = 0;
+  int* status = nullptr;
+  int rc = device_setup(&dev, &status);
+  if (rc) return rc;
+  cudaError_t e = dtk::launch_frames_to_blocks_sm100(frames, out, N, C, H, W, dtype == DT_DTYPE_BF16,
+                                                     static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
+  return DT_OK;
 }
 
 extern "C" int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, void* y,

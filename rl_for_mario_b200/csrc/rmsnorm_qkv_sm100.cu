@@ -271,10 +271,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 namespace {
 constexpr int kPersistThreads = 320;
 constexpr int kPN = 256;        // columns per tile
-constexpr int kPStages = 4;
+// 64 K elements per stage (128-byte rows, 128-byte swizzle), 4 stages.  (32-wide
+// stages x 8 keep the same bytes in flight with twice the TMA requests; they
+// measured slower.)
+constexpr int kPKC = kPersistKChunk;
+constexpr int kPStages = kPKC == 64 ? 4 : 8;
+static_assert(kPKC == 32 || kPKC == 64, "persistent K chunk");
 struct PShape {
-  static constexpr int A_BYTES = 128 * kKC * 2;
-  static constexpr int B_BYTES = kPN * kKC * 2;
+  static constexpr int RB = kPKC * 2;  // bytes per staged row
+  static constexpr uint32_t LAYOUT = kPKC == 64 ? kSw128 : kSw64;
+  static constexpr int A_BYTES = 128 * kPKC * 2;
+  static constexpr int B_BYTES = kPN * kPKC * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int OFF_ST = kPStages * STAGE;            // output staging: [4 warps][32 rows][64 cols]
   static constexpr int ST_WARP = 32 * 64 * 2;                // one warp's slice (4 swizzle atoms)
@@ -309,7 +316,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nk = (p.K + kKC - 1) / kKC;
+  const int nk = (p.K + kPKC - 1) / kPKC;
   const int nrb = (p.M + 127) / 128;
   const int nt = (p.N + kPN - 1) / kPN;
 
@@ -350,8 +357,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             if (!(ok = mbar_wait(&empty[s], ((cnt / kPStages) & 1) ^ 1, abort_flag, p.status))) break;
             uint8_t* st = smem + s * SH::STAGE;
             mbar_arrive_expect_tx(&full[s], (uint32_t)SH::STAGE);
-            tma_load_2d(st, &tmX, &full[s], kc * kKC, rb * 128);
-            tma_load_2d(st + SH::A_BYTES, &tmW, &full[s], kc * kKC, ct * kPN);
+            tma_load_2d(st, &tmX, &full[s], kc * kPKC, rb * 128);
+            tma_load_2d(st + SH::A_BYTES, &tmW, &full[s], kc * kPKC, ct * kPN);
           }
       if (!ok) {
         for (int s = 0; s < kPStages; ++s) {
@@ -374,10 +381,10 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             if (!(ok = mbar_wait(&full[s], (cnt / kPStages) & 1, abort_flag, p.status))) break;
             tc_fence_after();
             const uint32_t a = smem_u32(smem + s * SH::STAGE);
-            const uint64_t ad = umma_smem_desc(a, 16, 1024, kSw128);
-            const uint64_t bd = umma_smem_desc(a + SH::A_BYTES, 16, 1024, kSw128);
+            const uint64_t ad = umma_smem_desc(a, 16, 8 * SH::RB, SH::LAYOUT);
+            const uint64_t bd = umma_smem_desc(a + SH::A_BYTES, 16, 8 * SH::RB, SH::LAYOUT);
 #pragma unroll
-            for (int kk = 0; kk < kKC / 16; ++kk)  // 32 bytes per K step inside the 128-byte atom
+            for (int kk = 0; kk < kPKC / 16; ++kk)  // 32 bytes per K step inside the swizzle atom
               umma_f16_ss(tmem + buf * kPN, ad + 2 * kk, bd + 2 * kk, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
             umma_commit(&empty[s]);
           }
@@ -552,13 +559,14 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
           if (!(ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (cnt / kPStages) & 1, abort_flag, p.status))))
             break;
           if (ct == 0) {
-            // Row rr of the chunk is the 128 bytes at rr * 128 (the swizzle
+            // Row rr of the chunk is the RB bytes at rr * RB (the swizzle
             // permutes 16-byte pieces inside the row); start each lane at a
-            // different piece so a quarter warp covers all banks.
-            const uint8_t* row = smem + s * SH::STAGE + rr * 128;
+            // different piece to spread a quarter warp over the banks.
+            constexpr int NPc = SH::RB / 16;
+            const uint8_t* row = smem + s * SH::STAGE + rr * SH::RB;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const uint4 u = *reinterpret_cast<const uint4*>(row + (((q + lane) & 7) << 4));
+            for (int q = 0; q < NPc; ++q) {
+              const uint4 u = *reinterpret_cast<const uint4*>(row + (((q + lane) & (NPc - 1)) << 4));
               const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {

@@ -128,7 +128,7 @@ class DTBlock(nn.Module):
                 and mlp.down_proj.weight.dtype == h.dtype and mlp.down_proj.bias is None
                 and mlp.gate_proj.bias is None and mlp.up_proj.bias is None
                 and (not self.training or mlp.dropout.p == 0) and inter % 64 == 0 and inter >= 128
-                and h.shape[-1] % 8 == 0)
+                and h.shape[-1] % 8 == 0 and not (torch.is_grad_enabled() and h.requires_grad))
 
     def forward(self, hidden_states, position_embeddings, past_key_value=None, use_cache=False,
                 attention_mask=None):
@@ -138,8 +138,9 @@ class DTBlock(nn.Module):
                                         residual=hidden_states)
             if self._fused_mlp_ok(h):
                 a = kernels.rmsnorm_swiglu(h, self._swiglu_weight(h.dtype), self.post_attention_layernorm.eps)
-                h2 = h.reshape(-1, h.shape[-1])
-                h = torch.addmm(h2, a.reshape(-1, a.shape[-1]), self.mlp.down_proj.weight.t()).view(h.shape)
+                # h is this block's own intermediate: the down projection
+                # accumulates into it in place (no copy of the residual).
+                h.view(-1, h.shape[-1]).addmm_(a.reshape(-1, a.shape[-1]), self.mlp.down_proj.weight.t())
             else:
                 h = h + self.mlp(self.post_attention_layernorm(h))
             return h, present
@@ -186,9 +187,13 @@ class MarioStateEncoder(nn.Module):
             # tensor-core convolution, into a 64-channel one.  One pass writes
             # the blocked frames in the compute dtype, channels-last.
             f = st0
-            x = torch.empty((B * T, C * f * f, H // f, W // f), dtype=dt, device=s.device, memory_format=cl)
-            x.permute(0, 2, 3, 1).view(B * T, H // f, W // f, C, f, f).copy_(
-                s.view(B * T, C, H // f, f, W // f, f).permute(0, 2, 4, 1, 3, 5))
+            if (f == 4 and s.is_cuda and s.dtype == torch.uint8 and dt in (torch.bfloat16, torch.float16)
+                    and s.is_contiguous()):
+                x = kernels.frames_to_blocks(s, dt)
+            else:
+                x = torch.empty((B * T, C * f * f, H // f, W // f), dtype=dt, device=s.device, memory_format=cl)
+                x.permute(0, 2, 3, 1).view(B * T, H // f, W // f, C, f, f).copy_(
+                    s.view(B * T, C, H // f, f, W // f, f).permute(0, 2, 4, 1, 3, 5))
             kb = k0 // f
             w0 = (w0.view(conv0.out_channels, C, kb, f, kb, f).permute(0, 1, 3, 5, 2, 4)
                   .reshape(conv0.out_channels, C * f * f, kb, kb))

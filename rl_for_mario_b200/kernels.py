@@ -189,6 +189,21 @@ def fold_norm_weight(w_q: Tensor, w_k: Tensor, w_v: Tensor, w_norm: Tensor, dtyp
     return w.to(dtype).contiguous()
 
 
+def frames_to_blocks(frames: Tensor, dtype: torch.dtype) -> Tensor:
+    """uint8 frames [N, C, H, W] -> ``dtype`` 4 x 4 space-to-depth blocks as a
+    channels-last [N, C*16, H/4, W/4] tensor (channel c*16 + dy*4 + dx)."""
+    _require_cuda(frames)
+    if frames.dtype != torch.uint8 or frames.dim() != 4 or not frames.is_contiguous():
+        raise ValueError("frames must be a contiguous uint8 [N, C, H, W] tensor")
+    N, C, H, W = frames.shape
+    out = torch.empty((N, C * 16, H // 4, W // 4), dtype=dtype, device=frames.device,
+                      memory_format=torch.channels_last)
+    rc = _lib.load().dt_frames_to_blocks(_ptr(frames), _ptr(out), N, C, H, W, _dtype_code(out),
+                                         _stream_ptr(frames.device))
+    _lib.check("dt_frames_to_blocks", rc)
+    return out
+
+
 def fold_swiglu_weight(w_gate: Tensor, w_up: Tensor, w_norm: Tensor, dtype: torch.dtype) -> Tensor:
     """The weight of rmsnorm_swiglu: gate and up rows scaled by the norm weight,
     interleaved in blocks of 64 rows ([gate 0:64; up 0:64; gate 64:128; ...])."""

@@ -1,0 +1,45 @@
+"""GPU parity of the state-encoder input kernel (dt_frames_to_blocks) and of the
+space-to-depth first convolution against the reference encoder's direct one."""
+import pytest
+import torch
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N,C,H,W", [(1, 4, 84, 84), (37, 4, 84, 84), (5, 1, 8, 12), (3, 3, 16, 4)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_frames_to_blocks_exact(N, C, H, W, dtype):
+    from rl_for_mario_b200.kernels import device_status, frames_to_blocks
+
+    g = torch.Generator().manual_seed(N * C + H)
+    fr = torch.randint(0, 256, (N, C, H, W), generator=g, dtype=torch.uint8)
+    out = frames_to_blocks(fr.cuda(), dtype)
+    assert device_status() == 0
+    assert out.shape == (N, C * 16, H // 4, W // 4) and out.is_contiguous(memory_format=torch.channels_last)
+    ref = fr.view(N, C, H // 4, 4, W // 4, 4).permute(0, 1, 3, 5, 2, 4).reshape(N, C * 16, H // 4, W // 4)
+    assert torch.equal(out.cpu().to(torch.int32), ref.to(torch.int32))
+
+
+@pytest.mark.gpu
+def test_frames_to_blocks_rejects_bad_shapes():
+    from rl_for_mario_b200.kernels import frames_to_blocks
+
+    with pytest.raises(RuntimeError):
+        frames_to_blocks(torch.zeros(2, 4, 10, 84, dtype=torch.uint8, device="cuda"), torch.bfloat16)
+    with pytest.raises(ValueError):
+        frames_to_blocks(torch.zeros(2, 4, 84, 84, dtype=torch.float32, device="cuda"), torch.bfloat16)
+
+
+@pytest.mark.gpu
+def test_state_encoder_matches_direct_convolution():
+    """bf16 encoder (frame blocks + 2 x 2 convolution) vs the reference's direct
+    8 x 8 stride-4 convolution of frames / 255, in fp32."""
+    from rl_for_mario_b200.dt_model import MarioStateEncoder
+
+    torch.manual_seed(0)
+    enc = MarioStateEncoder((4, 84, 84), 256).eval()
+    s = torch.randint(0, 256, (3, 5, 4, 84, 84), dtype=torch.uint8)
+    with torch.no_grad():
+        ref = enc.cnn(s.reshape(15, 4, 84, 84).float() / 255.0).reshape(3, 5, -1)
+        out = enc.cuda().to(torch.bfloat16)(s.cuda())
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 3e-2 * max(1.0, ref.abs().max().item()), err
