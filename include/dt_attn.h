@@ -156,10 +156,24 @@ int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, 
  * With the first convolution's weight regrouped the same way (and scaled by
  * 1/255), the reference's frames / 255 -> Conv2d(C, 32, 8, stride 4)
  * (model_decision_transformer.py:315-341, division at :338) becomes a 2 x 2
- * stride-1 convolution over C*16 channels.  H, W multiples of 4; frames
- * 4-byte aligned, out 16-byte aligned; bf16 or fp16 output.
+ * stride-1 convolution over C*16 channels.  frame_max (nullable, device):
+ * raised by atomicMax to the largest byte read (the reference's x.max() > 1
+ * test, :338, without a separate pass).  H, W multiples of 4; frames 4-byte
+ * aligned, out 16-byte aligned; bf16 or fp16 output.
  */
-int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int C, int H, int W, int dtype, void* stream);
+
+/*
+ * RMSNorm with the reference's rounding: y = w * cast(x * rsqrt(mean(x^2) +
+ * eps)) with the mean and rsqrt in fp32, the normalised row cast to the
+ * activation dtype before the weight product (model_decision_transformer.py:
+ * 76-86; used for embed_norm and the final norm, :420 and :457).  x, y
+ * [M, K] with row strides; w [K]; bf16 or fp16; K and strides multiples of
+ * 8, 16-byte aligned pointers.
+ */
+int dt_rmsnorm(const void* x, int64_t x_row_stride, const void* w, void* y, int64_t y_row_stride, int M, int K,
+               float eps, int dtype, void* stream);
+int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int C, int H, int W, unsigned int* frame_max,
+                        int dtype, void* stream);
 
 /*
  * Synchronises `stream`, then returns and clears the device status word that

@@ -456,8 +456,8 @@ extern "C" int dt_rmsnorm_qkv_rope(const void* x, int64_t x_row_stride, const vo
                           cos_rows, seq_len, rope_cols, head_dim, dtype, stream);
 }
 
-extern "C" int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int C, int H, int W, int dtype,
-                                   void* stream) {
+extern "C" int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int C, int H, int W,
+                                   unsigned int* frame_max, int dtype, void* stream) {
   const char* fn = "dt_frames_to_blocks";
   if (!frames || !out) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
   if (N < 1 || C < 1 || H < 4 || W < 4 || H % 4 || W % 4)
@@ -472,8 +472,28 @@ extern "C" int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int
   int* status = nullptr;
   int rc = device_setup(&dev, &status);
   if (rc) return rc;
-  cudaError_t e = dtk::launch_frames_to_blocks_sm100(frames, out, N, C, H, W, dtype == DT_DTYPE_BF16,
+  cudaError_t e = dtk::launch_frames_to_blocks_sm100(frames, out, N, C, H, W, dtype == DT_DTYPE_BF16, frame_max,
                                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
+  return DT_OK;
+}
+
+extern "C" int dt_rmsnorm(const void* x, int64_t x_row_stride, const void* w, void* y, int64_t y_row_stride, int M,
+                          int K, float eps, int dtype, void* stream) {
+  const char* fn = "dt_rmsnorm";
+  if (!x || !w || !y) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
+  if (M < 1 || K < 8 || K % 8 || x_row_stride < K || y_row_stride < K || x_row_stride % 8 || y_row_stride % 8)
+    return fail(DT_ERR_INVALID, "%s: K a positive multiple of 8, row strides >= K and multiples of 8", fn);
+  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
+    return fail(DT_ERR_UNSUPPORTED, "%s: dtype %d not supported (bf16 / fp16)", fn, dtype);
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return fail(DT_ERR_INVALID, "%s: 16-byte alignment", fn);
+  if (!(eps > 0.f)) return fail(DT_ERR_INVALID, "%s: eps must be positive", fn);
+  int dev = 0;
+  int* status = nullptr;
+  int rc = device_setup(&dev, &status);
+  if (rc) return rc;
+  cudaError_t e = dtk::launch_rmsnorm_sm100(x, x_row_stride, w, y, y_row_stride, M, K, eps, dtype == DT_DTYPE_BF16,
+                                            g_num_sms[dev], static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
   return DT_OK;
 }

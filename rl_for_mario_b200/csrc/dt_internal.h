@@ -116,7 +116,9 @@ int rmsnorm_qkv_ncta(int N);
 constexpr int kPersistKChunk = 64;  // K elements per stage of the persistent RMSNorm GEMM (x / W box width)
 
 cudaError_t launch_frames_to_blocks_sm100(const void* frames, void* out, long long N, int C, int H, int W, bool bf16,
-                                          cudaStream_t st);
+                                          unsigned int* frame_max, cudaStream_t st);
+cudaError_t launch_rmsnorm_sm100(const void* x, long long x_stride, const void* w, void* y, long long y_stride, int M,
+                                 int K, float eps, bool bf16, int num_sms, cudaStream_t st);
 cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w, const CUtensorMap& y,
                                      const RmsQkvParams& p, int ncta, int num_sms, cudaStream_t st);
 

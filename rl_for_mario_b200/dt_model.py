@@ -66,8 +66,12 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x: Tensor) -> Tensor:
+        w = self.weight
+        if (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype and x.numel()
+                and x.shape[-1] % 8 == 0 and not (torch.is_grad_enabled() and (x.requires_grad or w.requires_grad))):
+            return kernels.rmsnorm(x, w.contiguous(), self.eps)  # one pass, same rounding
         xf = x.float()
-        return self.weight * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).type_as(x)
+        return w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).type_as(x)
 
 
 def rope_tables(dim: int, end: int, base: float) -> Tuple[Tensor, Tensor]:
@@ -174,7 +178,16 @@ class MarioStateEncoder(nn.Module):
         # The test stays on the device (no host synchronisation) and the 1/255
         # goes into the first convolution's weight instead of a pass over the
         # frames.
-        big = (s.amax() > 1) if s.dtype == torch.uint8 else (s.to(dt).amax() > 1.0)
+        use_blocks = (conv0.kernel_size == (8, 8) and conv0.stride == (4, 4) and conv0.padding == (0, 0)
+                      and H % 4 == 0 and W % 4 == 0 and s.is_cuda and s.dtype == torch.uint8
+                      and dt in (torch.bfloat16, torch.float16) and s.is_contiguous())
+        if use_blocks:
+            # The frame-block kernel also reports the largest byte.
+            fmax = torch.zeros(1, dtype=torch.int32, device=s.device)
+            xb = kernels.frames_to_blocks(s, dt, fmax)
+            big = fmax > 1
+        else:
+            big = (s.amax() > 1) if s.dtype == torch.uint8 else (s.to(dt).amax() > 1.0)
         w0 = torch.where(big, conv0.weight / 255.0, conv0.weight)
         cl = torch.channels_last
         k0, st0 = conv0.kernel_size[0], conv0.stride[0]
@@ -187,9 +200,8 @@ class MarioStateEncoder(nn.Module):
             # tensor-core convolution, into a 64-channel one.  One pass writes
             # the blocked frames in the compute dtype, channels-last.
             f = st0
-            if (f == 4 and s.is_cuda and s.dtype == torch.uint8 and dt in (torch.bfloat16, torch.float16)
-                    and s.is_contiguous()):
-                x = kernels.frames_to_blocks(s, dt)
+            if use_blocks:
+                x = xb
             else:
                 x = torch.empty((B * T, C * f * f, H // f, W // f), dtype=dt, device=s.device, memory_format=cl)
                 x.permute(0, 2, 3, 1).view(B * T, H // f, W // f, C, f, f).copy_(

@@ -189,18 +189,40 @@ def fold_norm_weight(w_q: Tensor, w_k: Tensor, w_v: Tensor, w_norm: Tensor, dtyp
     return w.to(dtype).contiguous()
 
 
-def frames_to_blocks(frames: Tensor, dtype: torch.dtype) -> Tensor:
+def frames_to_blocks(frames: Tensor, dtype: torch.dtype, frame_max: Optional[Tensor] = None) -> Tensor:
     """uint8 frames [N, C, H, W] -> ``dtype`` 4 x 4 space-to-depth blocks as a
-    channels-last [N, C*16, H/4, W/4] tensor (channel c*16 + dy*4 + dx)."""
-    _require_cuda(frames)
+    channels-last [N, C*16, H/4, W/4] tensor (channel c*16 + dy*4 + dx).
+    ``frame_max`` (an int32 [1] device tensor) is raised to the largest byte."""
+    _require_cuda(frames, frame_max)
+    if frame_max is not None and (frame_max.dtype != torch.int32 or frame_max.numel() != 1):
+        raise ValueError("frame_max must be an int32 tensor with one element")
     if frames.dtype != torch.uint8 or frames.dim() != 4 or not frames.is_contiguous():
         raise ValueError("frames must be a contiguous uint8 [N, C, H, W] tensor")
     N, C, H, W = frames.shape
     out = torch.empty((N, C * 16, H // 4, W // 4), dtype=dtype, device=frames.device,
                       memory_format=torch.channels_last)
-    rc = _lib.load().dt_frames_to_blocks(_ptr(frames), _ptr(out), N, C, H, W, _dtype_code(out),
+    rc = _lib.load().dt_frames_to_blocks(_ptr(frames), _ptr(out), N, C, H, W,
+                                         None if frame_max is None else _ptr(frame_max), _dtype_code(out),
                                          _stream_ptr(frames.device))
     _lib.check("dt_frames_to_blocks", rc)
+    return out
+
+
+def rmsnorm(x: Tensor, weight: Tensor, eps: float, out: Optional[Tensor] = None) -> Tensor:
+    """weight * cast(x * rsqrt(mean(x^2) + eps)) over the last dim (bf16 / fp16)."""
+    _require_cuda(x, weight, out)
+    K = x.shape[-1]
+    if weight.shape != (K,) or weight.dtype != x.dtype or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous [K] tensor of x's dtype")
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    o2 = out.view(-1, K)
+    rc = _lib.load().dt_rmsnorm(_ptr(x2), x2.stride(0), _ptr(weight), _ptr(o2), o2.stride(0), x2.shape[0], K,
+                                float(eps), _dtype_code(x), _stream_ptr(x.device))
+    _lib.check("dt_rmsnorm", rc)
     return out
 
 
