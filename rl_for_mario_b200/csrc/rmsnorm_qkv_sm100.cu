@@ -410,25 +410,39 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       const float* srow = p.sin + (size_t)pos * p.cs_stride;
       // Stage this warp's 32 table rows once per row block (coalesced reads,
       // fp16).  Tables whose halves are not duplicated keep the direct path.
+      // The 32 x half (row, column) entries are read in batches of 16 per
+      // lane, every load of a batch issued before its stores (one L2 round
+      // trip per batch instead of one per row).
       bool tab_ok = false;
       if (p.rope_cols > 0) {
-        const int half = p.head_dim >> 1;  // 16 or 32
-        const int rpi = 32 / half;         // rows per pass
-        const int dl = lane & (half - 1);
+        const int half = p.head_dim >> 1;       // 16 or 32
+        const int hsh = half == 32 ? 5 : 4;     // log2(half)
         bool dup = true;
-        for (int i0 = 0; i0 < 32; i0 += rpi) {
-          const int i = i0 + lane / half;  // row of the warp slice
-          const int pi = (rb * 128 + wq * 32 + i) % p.seq_len;
-          const float* cr = p.cos + (size_t)pi * p.cs_stride;
-          const float* sr = p.sin + (size_t)pi * p.cs_stride;
-          const float c0 = __ldg(cr + dl), c1 = __ldg(cr + dl + half);
-          const float s0 = __ldg(sr + dl), s1 = __ldg(sr + dl + half);
-          dup = dup && c0 == c1 && s0 == s1;
-          uint8_t* trow = tab_s + wq * SH::TAB_WARP + i * 128;
-          const int sw = i & 7;
-          // halves dl of the cos table (pieces 0..3) and of the sin table (4..7)
-          *reinterpret_cast<__half*>(trow + (((dl >> 3) ^ sw) << 4) + (dl & 7) * 2) = __float2half_rn(c0);
-          *reinterpret_cast<__half*>(trow + (((4 + (dl >> 3)) ^ sw) << 4) + (dl & 7) * 2) = __float2half_rn(s0);
+        for (int j0 = 0; j0 < half; j0 += 16) {  // half entries per lane in all
+          float c0[16], c1[16], s0[16], s1[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int e = (j0 + u) * 32 + lane;  // entry of the warp slice
+            const int i = e >> hsh, dl = e & (half - 1);
+            const int pi = (rb * 128 + wq * 32 + i) % p.seq_len;
+            const float* cr = p.cos + (size_t)pi * p.cs_stride + dl;
+            const float* sr = p.sin + (size_t)pi * p.cs_stride + dl;
+            c0[u] = __ldg(cr);
+            c1[u] = __ldg(cr + half);
+            s0[u] = __ldg(sr);
+            s1[u] = __ldg(sr + half);
+          }
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int e = (j0 + u) * 32 + lane;
+            const int i = e >> hsh, dl = e & (half - 1);
+            dup = dup && c0[u] == c1[u] && s0[u] == s1[u];
+            uint8_t* trow = tab_s + wq * SH::TAB_WARP + i * 128;
+            const int sw = i & 7;
+            // half dl of the cos table (pieces 0..3) and of the sin table (4..7)
+            *reinterpret_cast<__half*>(trow + (((dl >> 3) ^ sw) << 4) + (dl & 7) * 2) = __float2half_rn(c0[u]);
+            *reinterpret_cast<__half*>(trow + (((4 + (dl >> 3)) ^ sw) << 4) + (dl & 7) * 2) = __float2half_rn(s0[u]);
+          }
         }
         tab_ok = __all_sync(0xffffffffu, dup);
         __syncwarp();
@@ -451,10 +465,19 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
               float gv[32], uv[32];
               tmem_ld32(t_row + buf * kPN + c + hh, gv);
               tmem_ld32(t_row + buf * kPN + c + 64 + hh, uv);
+              // silu(rs g) * (rs u) = rs^2 g u / (1 + 2^(-rs log2(e) g)), two
+              // lanes per f32x2 instruction, exp2 and the quotient approximate
+              // (the result is rounded to 16 bits).
+              const float2 na2 = make_float2(-rs * 1.4426950408889634f, -rs * 1.4426950408889634f);
+              const float2 rs2 = make_float2(rs * rs, rs * rs), one2 = make_float2(1.f, 1.f);
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const float gg = gv[i] * rs;
-                gv[i] = gg / (1.f + __expf(-gg)) * (uv[i] * rs);  // silu(gate) * up
+              for (int i = 0; i < 32; i += 2) {
+                const float2 g2 = make_float2(gv[i], gv[i + 1]);
+                const float2 t = fmul2(g2, na2);
+                const float2 d = fadd2(make_float2(ex2_approx(t.x), ex2_approx(t.y)), one2);
+                const float2 gu = fmul2(fmul2(g2, make_float2(uv[i], uv[i + 1])), rs2);
+                gv[i] = __fdividef(gu.x, d.x);
+                gv[i + 1] = __fdividef(gu.y, d.y);
               }
 #pragma unroll
               for (int c8 = 0; c8 < 32; c8 += 8) {
