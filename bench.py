@@ -41,8 +41,9 @@ def _peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 def _algorithmic_bytes(B, S, Hq, Hkv, D) -> int:
@@ -317,6 +318,7 @@ def run_ours(args):
             line["decode"] = bench_decode_cfg3(dev, peaks)
             line["prefill_long"] = bench_prefill_cfg4(dev, peaks)
             line["prefill_long"]["rmsnorm_qkv_kernel"] = bench_rmsnorm_qkv_cfg4(dev, peaks)
+            line["prefill_long"]["rmsnorm_swiglu_kernel"] = bench_rmsnorm_swiglu_cfg4(dev, peaks)
         line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
@@ -426,7 +428,7 @@ def bench_decode_cfg3(dev, peaks):
 
 
 PREFILL_LONG_CFG = dict(batch=1024, timesteps=256, hidden=768, layers=12, q_heads=12, kv_heads=4, head_dim=64,
-                        pad_max_timesteps=128)
+                        ffn=2048, pad_max_timesteps=128)
 
 
 def _attended_pairs(S: int, pads) -> int:
@@ -492,7 +494,7 @@ def bench_prefill_cfg4(dev, peaks, batch=None, model=True):
     # (b) full model forward
     torch.manual_seed(4)
     cfg = DTConfig(hidden_size=C["hidden"], num_hidden_layers=C["layers"], num_attention_heads=Hq,
-                   num_key_value_heads=Hkv, context_len=T, intermediate_size=2048, dropout=0.0)
+                   num_key_value_heads=Hkv, context_len=T, intermediate_size=C["ffn"], dropout=0.0)
     model = MarioDT(cfg).to(dev, torch.bfloat16).eval().fuse_norms()
     states = torch.randint(0, 256, (B, T) + tuple(cfg.state_shape), device=dev, generator=g, dtype=torch.uint8)
     actions = torch.randint(0, cfg.act_dim, (B, T), device=dev, generator=g)
@@ -517,12 +519,25 @@ def bench_prefill_cfg4(dev, peaks, batch=None, model=True):
         torch.cuda.synchronize()
         times.append(f0.elapsed_time(f1))
     fms = min(times)
+    # Whole-forward FLOPs: per token and layer the q|k|v, o_proj, gate|up and down GEMMs
+    # (2 H ((Hq + 2 Hkv) D + Hq D + 3 F)), the attention (the kernel's count per layer), and
+    # the state encoder per frame (8x8/4, 4x4/2, 3x3 convolutions and the Linear).
+    H, F, L = C["hidden"], C["ffn"], C["layers"]
+    lin_tok = 2 * H * ((Hq + 2 * Hkv) * D + Hq * D + 3 * F)
+    enc_frame = 2 * (32 * 4 * 64 * 400 + 64 * 32 * 16 * 81 + 64 * 64 * 9 * 49 + 3136 * H)
+    fwd_flops = L * (B * S * lin_tok + flops) + B * T * enc_frame
+    ftf = fwd_flops / (fms * 1e-3) / 1e12
     res = {
         "metric": "DT prefill tokens/s (full forward, 1024 x 768 tokens, hidden 768, 12 layers)", "unit": "tokens/s",
         "value": B * S / (fms * 1e-3), "ms": fms,
         "config": {"workload": "1024 x 256 timesteps (768 tokens), hidden 768, 12 layers, 12/4 heads, head_dim 64, "
-                               "FFN 2048, bf16, fused RMSNorm+QKV, synthetic uint8 frames, left pad U{0..128} "
-                               "timesteps, random-init weights"},
+                               "FFN 2048, bf16, fused blocks (RMSNorm+QKV+RoPE, attention, o_proj+residual, "
+                               "RMSNorm+gate/up+SwiGLU, down+residual), synthetic uint8 frames, left pad "
+                               "U{0..128} timesteps, random-init weights"},
+        # a seconds-long sequence of kernels: the sustained GEMM peak is the denominator
+        "roofline": {"bound": "tensor", "achieved": ftf, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": ftf / peaks["bf16_tflops_sustained"], "flops_per_forward": fwd_flops,
+                     "peak_source": peaks["source"] + " (sustained)"},
         "attention_kernel": kernel_res,
     }
     del model, states
@@ -563,6 +578,41 @@ def bench_rmsnorm_qkv_cfg4(dev, peaks, batch=None):
     flops = 2 * M * H * N
     tf = flops / (ms * 1e-3) / 1e12
     return {"kernel": "dt_rmsnorm_qkv_persist_kernel", "shape": {"M": M, "K": H, "N": N}, "ms": ms,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tf / peaks["bf16_tflops"], "flops_per_launch": flops,
+                         "peak_source": peaks["source"]}}
+
+
+def bench_rmsnorm_swiglu_cfg4(dev, peaks, batch=None):
+    """The fused post-attention RMSNorm + gate/up + SwiGLU kernel at a cfg4 layer's
+    shape: M = batch x 768 tokens, K = hidden 768, FFN width 2048 (4096 GEMM columns)."""
+    from rl_for_mario_b200.kernels import device_status, fold_swiglu_weight, rmsnorm_swiglu
+
+    C = PREFILL_LONG_CFG
+    B, S, H, F = batch or C["batch"], 3 * C["timesteps"], C["hidden"], C["ffn"]
+    g = torch.Generator(device=dev).manual_seed(6)
+    x = torch.randn(B, S, H, device=dev, generator=g).to(torch.bfloat16)
+    wg, wu = (torch.randn(F, H, device=dev, generator=g) / H ** 0.5 for _ in range(2))
+    wf = fold_swiglu_weight(wg, wu, torch.ones(H, device=dev), torch.bfloat16)
+    out = torch.empty(B, S, F, device=dev, dtype=torch.bfloat16)
+    for _ in range(3):
+        rmsnorm_swiglu(x, wf, 1e-5, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 10
+    e0.record()
+    for _ in range(n):
+        rmsnorm_swiglu(x, wf, 1e-5, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    if device_status() != 0:
+        raise SystemExit("device status error in the RMSNorm + SwiGLU benchmark")
+    ms = e0.elapsed_time(e1) / n
+    M = B * S
+    flops = 2 * M * H * 2 * F
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"kernel": "dt_rmsnorm_qkv_persist_kernel (SwiGLU epilogue)", "shape": {"M": M, "K": H, "N": 2 * F},
+            "ms": ms,
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": tf / peaks["bf16_tflops"], "flops_per_launch": flops,
                          "peak_source": peaks["source"]}}
@@ -642,7 +692,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / rollout sub-benchmarks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
-    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv"], default=None,
+    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu"], default=None,
                     help="run one sub-benchmark alone and print its JSON (profiling)")
     ap.add_argument("--long-batch", type=int, default=None,
                     help="with --only prefill_long: batch of the attention-kernel case, model forward skipped")
@@ -657,6 +707,8 @@ def main():
             emit({"only": "decode", **bench_decode_cfg3(dev, _peaks())})
         elif args.only == "rmsnorm_qkv":
             emit({"only": "rmsnorm_qkv", **bench_rmsnorm_qkv_cfg4(dev, _peaks(), batch=args.long_batch)})
+        elif args.only == "rmsnorm_swiglu":
+            emit({"only": "rmsnorm_swiglu", **bench_rmsnorm_swiglu_cfg4(dev, _peaks(), batch=args.long_batch)})
         else:
             emit({"only": "prefill_long", **bench_prefill_cfg4(dev, _peaks(), batch=args.long_batch,
                                                                 model=args.long_batch is None)})

@@ -266,8 +266,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // 256-column tiles back to back, so the block's x rows stay hot in L2 and its
 // row scale is computed once.  The accumulator is double-buffered in TMEM (2 x
 // 256 columns): the epilogue of one tile overlaps the main loop of the next.
-// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-5 epilogue, 6-9 row
-// sums of squares (read from global memory, one warp per row at a time).
+// Warps: 0 TMA producer (also prefetches the next row block of x into L2),
+// 1 TMEM owner + MMA issuer, 2-5 epilogue (row scale, RoPE or SwiGLU, 16-bit
+// slices stored by TMA), 6-9 row sums of squares from the staged x slices of
+// each block's first tile (they take part in the ring's stage release).
 namespace {
 constexpr int kPersistThreads = 320;
 constexpr int kPN = 256;        // columns per tile
@@ -354,6 +356,26 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         for (int ct = 0; ct < nt && ok; ++ct)
           for (int kc = 0; kc < nk; ++kc, ++cnt) {
             const int s = cnt % kPStages;
+            // While the second column tile of a row block streams, pull this
+            // CTA's next row block of x from HBM into L2, so that its first
+            // tile (which reads x) runs at the L2 rate of the others.
+            if (ct == (nt > 1 ? 1 : 0) && rb + (int)gridDim.x < nrb) {
+              tma_prefetch_l2_2d(&tmX, kc * kPKC, (rb + (int)gridDim.x) * 128);
+              if (kc == 0 && p.rope_cols > 0) {
+                // and the RoPE table rows the next block's epilogue stages
+                const int rows = p.seq_len < 128 ? p.seq_len : 128;
+                const int p0 = p.seq_len < 128 ? 0 : ((rb + (int)gridDim.x) * 128) % p.seq_len;
+                const int n1 = rows < p.seq_len - p0 ? rows : p.seq_len - p0;
+                // (n rows end at the last row's head_dim entries: never past the table)
+                const uint32_t rowb = (uint32_t)p.cs_stride * 4u, tail = (uint32_t)p.head_dim * 4u;
+                bulk_prefetch_l2(p.cos + (size_t)p0 * p.cs_stride, (uint32_t)(n1 - 1) * rowb + tail);
+                bulk_prefetch_l2(p.sin + (size_t)p0 * p.cs_stride, (uint32_t)(n1 - 1) * rowb + tail);
+                if (n1 < rows) {
+                  bulk_prefetch_l2(p.cos, (uint32_t)(rows - n1 - 1) * rowb + tail);
+                  bulk_prefetch_l2(p.sin, (uint32_t)(rows - n1 - 1) * rowb + tail);
+                }
+              }
+            }
             if (!(ok = mbar_wait(&empty[s], ((cnt / kPStages) & 1) ^ 1, abort_flag, p.status))) break;
             uint8_t* st = smem + s * SH::STAGE;
             mbar_arrive_expect_tx(&full[s], (uint32_t)SH::STAGE);
@@ -402,51 +424,58 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     bool ok = true;
     for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++bc) {
       const int sb = bc & 1;
+      // Stage this warp's 32 table rows once per row block (coalesced reads,
+      // fp16), before waiting for the block's row sums: the tables do not
+      // depend on them, so this overlaps the block's first tile in the MMA.
+      // Tables whose halves are not duplicated keep the direct path.
+      // 16-byte loads: lane = (row of a group, float4 of a half row), 4 or 8
+      // rows per warp instruction, 4 rows per lane in flight per batch; the
+      // pieces go to shared memory as 8-byte stores.
+      bool tab_ok = false;
+      if (p.rope_cols > 0) {
+        const int half = p.head_dim >> 1;   // 16 or 32
+        const int qb = half == 32 ? 3 : 2;  // log2(float4s per half row)
+        const int q = lane & ((1 << qb) - 1), rsub = lane >> qb, rstep = 32 >> qb;
+        const int pos0 = (rb * 128 + wq * 32) % p.seq_len;
+        bool dup = true;
+        for (int j0 = 0; j0 < 32 / rstep; j0 += 4) {
+          float4 cl[4], ch[4], sl[4], sh[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            int pi = pos0 + (j0 + u) * rstep + rsub;
+            while (pi >= p.seq_len) pi -= p.seq_len;
+            const float4* cr = reinterpret_cast<const float4*>(p.cos + (size_t)pi * p.cs_stride) + q;
+            const float4* sr = reinterpret_cast<const float4*>(p.sin + (size_t)pi * p.cs_stride) + q;
+            cl[u] = __ldg(cr);
+            ch[u] = __ldg(cr + (half >> 2));
+            sl[u] = __ldg(sr);
+            sh[u] = __ldg(sr + (half >> 2));
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = (j0 + u) * rstep + rsub;  // row of the warp slice
+            dup = dup && cl[u].x == ch[u].x && cl[u].y == ch[u].y && cl[u].z == ch[u].z && cl[u].w == ch[u].w &&
+                  sl[u].x == sh[u].x && sl[u].y == sh[u].y && sl[u].z == sh[u].z && sl[u].w == sh[u].w;
+            uint8_t* trow = tab_s + wq * SH::TAB_WARP + i * 128;
+            const int sw = i & 7, off = (q & 1) * 8;
+            const __half2 c01 = __floats2half2_rn(cl[u].x, cl[u].y), c23 = __floats2half2_rn(cl[u].z, cl[u].w);
+            const __half2 s01 = __floats2half2_rn(sl[u].x, sl[u].y), s23 = __floats2half2_rn(sl[u].z, sl[u].w);
+            // halves 4q..4q+3 of the cos table (pieces 0..3) and of the sin table (4..7)
+            *reinterpret_cast<uint2*>(trow + (((q >> 1) ^ sw) << 4) + off) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&c01), *reinterpret_cast<const uint32_t*>(&c23));
+            *reinterpret_cast<uint2*>(trow + (((4 + (q >> 1)) ^ sw) << 4) + off) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&s01), *reinterpret_cast<const uint32_t*>(&s23));
+          }
+        }
+        tab_ok = __all_sync(0xffffffffu, dup);
+        __syncwarp();
+      }
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&ss_full[sb], (bc >> 1) & 1, abort_flag, p.status)))) break;
       const float rs = rsqrtf(ss_s[sb * 128 + r] / (float)p.K + p.eps);
       const int row_g = rb * 128 + r;
       const int pos = p.rope_cols > 0 ? row_g % p.seq_len : 0;
       const float* crow = p.cos + (size_t)pos * p.cs_stride;
       const float* srow = p.sin + (size_t)pos * p.cs_stride;
-      // Stage this warp's 32 table rows once per row block (coalesced reads,
-      // fp16).  Tables whose halves are not duplicated keep the direct path.
-      // The 32 x half (row, column) entries are read in batches of 16 per
-      // lane, every load of a batch issued before its stores (one L2 round
-      // trip per batch instead of one per row).
-      bool tab_ok = false;
-      if (p.rope_cols > 0) {
-        const int half = p.head_dim >> 1;       // 16 or 32
-        const int hsh = half == 32 ? 5 : 4;     // log2(half)
-        bool dup = true;
-        for (int j0 = 0; j0 < half; j0 += 16) {  // half entries per lane in all
-          float c0[16], c1[16], s0[16], s1[16];
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int e = (j0 + u) * 32 + lane;  // entry of the warp slice
-            const int i = e >> hsh, dl = e & (half - 1);
-            const int pi = (rb * 128 + wq * 32 + i) % p.seq_len;
-            const float* cr = p.cos + (size_t)pi * p.cs_stride + dl;
-            const float* sr = p.sin + (size_t)pi * p.cs_stride + dl;
-            c0[u] = __ldg(cr);
-            c1[u] = __ldg(cr + half);
-            s0[u] = __ldg(sr);
-            s1[u] = __ldg(sr + half);
-          }
-#pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int e = (j0 + u) * 32 + lane;
-            const int i = e >> hsh, dl = e & (half - 1);
-            dup = dup && c0[u] == c1[u] && s0[u] == s1[u];
-            uint8_t* trow = tab_s + wq * SH::TAB_WARP + i * 128;
-            const int sw = i & 7;
-            // half dl of the cos table (pieces 0..3) and of the sin table (4..7)
-            *reinterpret_cast<__half*>(trow + (((dl >> 3) ^ sw) << 4) + (dl & 7) * 2) = __float2half_rn(c0[u]);
-            *reinterpret_cast<__half*>(trow + (((4 + (dl >> 3)) ^ sw) << 4) + (dl & 7) * 2) = __float2half_rn(s0[u]);
-          }
-        }
-        tab_ok = __all_sync(0xffffffffu, dup);
-        __syncwarp();
-      }
       const uint8_t* my_tab = tab_s + wq * SH::TAB_WARP + lane * 128;
       for (int ct = 0; ct < nt && ok; ++ct, ++tc) {
         const int buf = tc & 1;
