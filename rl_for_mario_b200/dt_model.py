@@ -209,19 +209,36 @@ class MarioStateEncoder(nn.Module):
             kb = k0 // f
             w0 = (w0.view(conv0.out_channels, C, kb, f, kb, f).permute(0, 1, 3, 5, 2, 4)
                   .reshape(conv0.out_channels, C * f * f, kb, kb))
-            x = F.relu(F.conv2d(x, w0.contiguous(memory_format=cl), conv0.bias), inplace=True)
+            x = self._conv_relu(x, w0.contiguous(memory_format=cl), conv0.bias, (1, 1))
         else:
             # One pass: frames -> compute dtype, channels-last (the layout the
             # convolution kernels run in, so no layout conversions per layer).
             x = torch.empty(s.shape, dtype=dt, device=s.device, memory_format=cl)
             x.copy_(s)
-            x = F.relu(F.conv2d(x, w0.contiguous(memory_format=cl), conv0.bias, stride=conv0.stride), inplace=True)
-        x = F.relu(F.conv2d(x, conv1.weight.contiguous(memory_format=cl), conv1.bias, stride=conv1.stride),
-                   inplace=True)
-        x = F.relu(F.conv2d(x, conv2.weight.contiguous(memory_format=cl), conv2.bias, stride=conv2.stride),
-                   inplace=True)
-        # Flatten in the reference's (C, H, W) order.
+            x = self._conv_relu(x, w0.contiguous(memory_format=cl), conv0.bias, conv0.stride)
+        x = self._conv_relu(x, conv1.weight.contiguous(memory_format=cl), conv1.bias, conv1.stride)
+        x = self._conv_relu(x, conv2.weight.contiguous(memory_format=cl), conv2.bias, conv2.stride)
+        if x.dim() == 4 and x.is_contiguous(memory_format=cl):
+            # The reference flattens in (C, H, W) order; channels-last
+            # activations are (H, W, C) in memory, so the Linear's input
+            # columns are permuted instead of the activations (no copy).
+            n, c3, h3, w3 = x.shape
+            lw = lin.weight.view(lin.out_features, c3, h3, w3).permute(0, 2, 3, 1).reshape(lin.out_features, -1)
+            return F.linear(x.permute(0, 2, 3, 1).reshape(n, -1), lw, lin.bias).reshape(B, T, -1)
         return lin(x.contiguous().flatten(1)).reshape(B, T, -1)
+
+    _fused_conv = True
+
+    def _conv_relu(self, x: Tensor, w: Tensor, b: Optional[Tensor], stride) -> Tensor:
+        """relu(conv2d(x, w) + b): cuDNN's fused convolution + bias + activation for
+        16-bit CUDA inputs (one pass over the output instead of three), else the
+        plain sequence."""
+        if self._fused_conv and x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype:
+            try:
+                return torch.cudnn_convolution_relu(x, w, b, tuple(stride), (0, 0), (1, 1), 1)
+            except RuntimeError:
+                type(self)._fused_conv = False  # no fused engine for this build / shape
+        return F.relu(F.conv2d(x, w, b, stride=stride), inplace=True)
 
 
 class DTBackbone(nn.Module):
