@@ -128,9 +128,11 @@ class FastDTAttention(nn.Module):
     # ------------------------------------------------------------------ forward
     def forward(self, x: Tensor, position_embeddings: Tuple[Tensor, Tensor],
                 past_key_value=None, use_cache: bool = False, attention_mask: Optional[Tensor] = None,
-                raw_input: bool = False, residual: Optional[Tensor] = None):
+                raw_input: bool = False, residual: Optional[Tensor] = None, residual_inplace: bool = False):
         """``residual`` (the block input, [B, S, H]) is added to the output: one
-        GEMM with the residual as its accumulator input when dropout is off."""
+        GEMM with the residual as its accumulator input when dropout is off;
+        with ``residual_inplace`` (a caller that owns the residual and no longer
+        needs it) the GEMM accumulates into it instead of a copy."""
         if not x.is_cuda:
             raise ValueError("FastDTAttention runs on CUDA only (no CPU path)")
         bsz, seq_len, _ = x.shape
@@ -193,6 +195,9 @@ class FastDTAttention(nn.Module):
         if ((not self.training or self.resid_dropout.p == 0) and self.o_proj.bias is None
                 and residual.dtype == out.dtype == w.dtype):
             r2 = residual.reshape(-1, residual.shape[-1])
+            if residual_inplace and r2.data_ptr() == residual.data_ptr() and r2.is_contiguous():
+                r2.addmm_(out.reshape(-1, out.shape[-1]), w.t())
+                return residual, past_kv
             return torch.addmm(r2, out.reshape(-1, out.shape[-1]), w.t()).view(residual.shape), past_kv
         return residual + self.resid_dropout(self.o_proj(out)), past_kv
 

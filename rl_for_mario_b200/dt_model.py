@@ -135,11 +135,15 @@ class DTBlock(nn.Module):
                 and h.shape[-1] % 8 == 0 and not (torch.is_grad_enabled() and h.requires_grad))
 
     def forward(self, hidden_states, position_embeddings, past_key_value=None, use_cache=False,
-                attention_mask=None):
+                attention_mask=None, _owns_input: bool = False):
+        """``_owns_input``: the caller (the backbone's layer loop) owns
+        ``hidden_states`` and drops it after this call, so the fused path may
+        accumulate the o_proj GEMM into it in place."""
         if self.self_attn._fused_norm is not None:
             h, present = self.self_attn(hidden_states, position_embeddings, past_key_value=past_key_value,
                                         use_cache=use_cache, attention_mask=attention_mask, raw_input=True,
-                                        residual=hidden_states)
+                                        residual=hidden_states,
+                                        residual_inplace=_owns_input and not torch.is_grad_enabled())
             if self._fused_mlp_ok(h):
                 a = kernels.rmsnorm_swiglu(h, self._swiglu_weight(h.dtype), self.post_attention_layernorm.eps)
                 # h is this block's own intermediate: the down projection
@@ -294,11 +298,13 @@ class DTBackbone(nn.Module):
             if attention_mask.shape != (B, T):
                 raise ValueError(f"attention_mask must be [B,T], got {tuple(attention_mask.shape)}")
             mask3 = torch.stack((attention_mask,) * 3, dim=2).reshape(B, 3 * T).to(h.dtype)
-        return self.run_layers(h, mask3, past_key_values, use_cache)
+        return self.run_layers(h, mask3, past_key_values, use_cache, _owns_h=True)
 
-    def run_layers(self, h, mask3=None, past_key_values=None, use_cache=False, flat: bool = False):
+    def run_layers(self, h, mask3=None, past_key_values=None, use_cache=False, flat: bool = False,
+                   _owns_h: bool = False):
         """Layers + final norm on [B, S, H] token states (:435-461); returns [B, S/3, 3, H]
-        (the reference's view) unless ``flat``."""
+        (the reference's view) unless ``flat``.  The caller's ``h`` is left as it
+        is unless ``_owns_h``; the layers' own intermediates are updated in place."""
         cfg = self.config
         B, S = h.shape[0], h.shape[1]
         if hasattr(past_key_values, "layers") and not isinstance(past_key_values, PagedKVCache):
@@ -312,8 +318,10 @@ class DTBackbone(nn.Module):
                              f"{self.freqs_cos.shape[0]}")
         pe = (self.freqs_cos[start:start + S], self.freqs_sin[start:start + S])
         presents = []
+        owns = _owns_h
         for layer, pkv in zip(self.layers, past):
-            h, pr = layer(h, pe, past_key_value=pkv, use_cache=use_cache, attention_mask=mask3)
+            h, pr = layer(h, pe, past_key_value=pkv, use_cache=use_cache, attention_mask=mask3, _owns_input=owns)
+            owns = True
             presents.append(pr)
         h = self.norm(h)
         if not flat:
