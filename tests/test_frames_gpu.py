@@ -20,6 +20,26 @@ def test_frames_to_blocks_exact(N, C, H, W, dtype):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("N,C,H,W,offset", [(7, 4, 84, 84, 4), (3, 4, 128, 128, 0), (5, 3, 8, 8, 4)])
+def test_frames_to_blocks_other_layouts(N, C, H, W, offset):
+    """Frames that are only 4-byte aligned, or larger than one CTA's shared memory,
+    take the per-position kernels; same result."""
+    from rl_for_mario_b200.kernels import device_status, frames_to_blocks
+
+    g = torch.Generator().manual_seed(N + C + H + offset)
+    fr = torch.randint(0, 256, (N, C, H, W), generator=g, dtype=torch.uint8)
+    buf = torch.zeros(fr.numel() + 16, dtype=torch.uint8, device="cuda")
+    view = buf[offset:offset + fr.numel()].view(N, C, H, W)
+    view.copy_(fr.cuda())
+    fm = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = frames_to_blocks(view, torch.bfloat16, fm)
+    assert device_status() == 0
+    ref = fr.view(N, C, H // 4, 4, W // 4, 4).permute(0, 1, 3, 5, 2, 4).reshape(N, C * 16, H // 4, W // 4)
+    assert torch.equal(out.cpu().to(torch.int32), ref.to(torch.int32))
+    assert int(fm.item()) == int(fr.max())
+
+
+@pytest.mark.gpu
 def test_frames_to_blocks_rejects_bad_shapes():
     from rl_for_mario_b200.kernels import frames_to_blocks
 
