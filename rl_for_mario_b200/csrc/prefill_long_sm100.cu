@@ -10,9 +10,10 @@
 // heads of one KV group, so every key block is loaded once for the whole
 // group and once for both slots.  Key blocks of 64 stream through a TMA
 // ring; per block and slot:
-//   S  = Q K^T          tcgen05.mma, fp32 in TMEM (64 columns, two buffers
-//                       per slot so the next block's S runs during this
-//                       block's softmax)
+//   S  = Q K^T          tcgen05.mma, fp32 in TMEM (64 columns, three
+//                       buffers per slot: the P V of a block is issued two
+//                       blocks after its S, so S stays two blocks ahead of
+//                       the softmax instead of waiting on the previous P)
 //   P  = exp2(S c2 - m) softmax warpgroup of the slot, one thread per row;
 //                       P is written back over its S columns as packed
 //                       16-bit pairs
@@ -20,9 +21,9 @@
 // The softmax never waits for a P V: the running maximum m only moves when a
 // block's maximum exceeds it by more than 2^8 (P <= 256 otherwise, exact in
 // 16 bits); then (rarely) it waits for the slot's previous P V and scales the
-// O row in TMEM and the row sum by the exact power of two.  O is
-// double-buffered per slot so a slot's epilogue (O / l -> HBM) runs after the
-// next item's first block.
+// O row in TMEM and the row sum by the exact power of two.  A slot's
+// epilogue (O / l -> HBM) runs after the next item's first softmax block; the
+// next item's first P V waits for it (one O buffer per slot).
 //
 // Warp roles (384 threads): warp 0 TMA producer, warp 1 TMEM owner and MMA
 // issuer of slot 0, warp 2 MMA issuer of slot 1, warp 3 RoPE (rotates each
@@ -62,15 +63,16 @@ struct LongShape {
   static constexpr int OFF_K = OFF_Q + 2 * NQB * Q_BYTES;
   static constexpr int OFF_V = OFF_K + NKV * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + NKV * KV_BYTES;
+  static constexpr int NSB = 3;  // S buffers per slot (P V lags its S by two blocks)
   // q_full[2][NQB], q_empty[2][NQB], q_ready[2][NQB], kv_full[NKV], kv_empty[NKV],
-  // kv_ready[NKV], s_full[2][2], p_full[2][2], pv_done[2], o_full[2][2],
-  // o_empty[2][2], drain[2]
-  static constexpr int NBAR = 6 * NQB + 3 * NKV + 4 + 4 + 2 + 4 + 4 + 2;
+  // kv_ready[NKV], s_full[2][NSB], p_full[2][NSB], pv_done[2][NSB], o_full[2],
+  // o_empty[2], drain[2]
+  static constexpr int NBAR = 6 * NQB + 3 * NKV + 3 * 2 * NSB + 2 + 2 + 2;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr uint32_t TMEM_S = 0;    // slot s, buffer b: TMEM_S + (2 s + b) kBK
-  static constexpr uint32_t TMEM_O = 256;  // slot s, buffer b: TMEM_O + (2 s + b) D
-  static_assert(TMEM_S + 4 * kBK <= TMEM_O && TMEM_O + 4 * D <= 512, "TMEM budget");
+  static constexpr uint32_t TMEM_S = 0;    // slot s, buffer b: TMEM_S + (NSB s + b) kBK
+  static constexpr uint32_t TMEM_O = 384;  // slot s: TMEM_O + s D (one O per slot)
+  static_assert(TMEM_S + 2 * NSB * kBK <= TMEM_O && TMEM_O + 2 * D <= 512, "TMEM budget");
 };
 
 // Geometry of one work item; every role derives it from the item index.
@@ -152,12 +154,12 @@ __global__ void __launch_bounds__(kLongThreads, 1)
   uint64_t* kv_full = q_ready + 2 * SH::NQB;
   uint64_t* kv_empty = kv_full + SH::NKV;
   uint64_t* kv_ready = kv_empty + SH::NKV;      // K block rotated (RoPE inputs only)
-  uint64_t* s_full = kv_ready + SH::NKV;        // [slot * 2 + buf]: S of a block is in TMEM
-  uint64_t* p_full = s_full + 4;                // [slot * 2 + buf]: P of a block is in TMEM
-  uint64_t* pv_done = p_full + 4;               // [slot]: a P V of the slot has completed
-  uint64_t* o_full = pv_done + 2;               // [slot * 2 + buf]
-  uint64_t* o_empty = o_full + 4;
-  uint64_t* drain = o_empty + 4;
+  uint64_t* s_full = kv_ready + SH::NKV;        // [slot * NSB + buf]: S of a block is in TMEM
+  uint64_t* p_full = s_full + 2 * SH::NSB;      // [slot * NSB + buf]: P of a block is in TMEM
+  uint64_t* pv_done = p_full + 2 * SH::NSB;     // [slot * NSB + buf]: the P V reading buf completed
+  uint64_t* o_full = pv_done + 2 * SH::NSB;     // [slot]
+  uint64_t* o_empty = o_full + 2;
+  uint64_t* drain = o_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -179,12 +181,12 @@ __global__ void __launch_bounds__(kLongThreads, 1)
       mbar_init(&kv_empty[j], 2);  // both MMA issuers release every block
       mbar_init(&kv_ready[j], 1);
     }
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 2 * SH::NSB; ++j) {
       mbar_init(&s_full[j], 1);
       mbar_init(&p_full[j], 4);  // one arrival per softmax warp
+      mbar_init(&pv_done[j], 1);
     }
-    for (int j = 0; j < 2; ++j) mbar_init(&pv_done[j], 1);
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 2; ++j) {
       mbar_init(&o_full[j], 1);
       mbar_init(&o_empty[j], 4);
     }
@@ -283,11 +285,45 @@ __global__ void __launch_bounds__(kLongThreads, 1)
       const uint64_t q_desc0 = umma_smem_desc(smem_u32(q_s + s * SH::NQB * SH::Q_BYTES), 16, SH::SBO, SH::LAYOUT);
       const uint64_t k_desc0 = umma_smem_desc(smem_u32(k_s), 16, SH::SBO, SH::LAYOUT);
       const uint64_t v_desc0 = umma_smem_desc(smem_u32(v_s), SH::KV_BYTES, SH::SBO, SH::LAYOUT);
-      const uint32_t t_s0 = tmem + SH::TMEM_S + (uint32_t)(2 * s * kBK);
-      const uint32_t t_o0 = tmem + SH::TMEM_O + (uint32_t)(2 * s * D);
+      const uint32_t t_s0 = tmem + SH::TMEM_S + (uint32_t)(SH::NSB * s * kBK);
+      const uint32_t t_o = tmem + SH::TMEM_O + (uint32_t)(s * D);
       int qc = 0, oc = 0, sc = 0, pc = 0;  // Q loads consumed, items, S issued, P consumed
       int kvc = 0;
       bool ok = true;
+      // Blocks ("events") in the producer's order; the P V of an event is
+      // issued two events after its S, so S runs two blocks ahead of the
+      // softmax (three S buffers per slot) and an item's first S goes out
+      // before the previous item's last two P V.
+      struct Ev {
+        int st, act, first, last;
+      };
+      Ev pq0{0, 0, 0, 0}, pq1{0, 0, 0, 0};
+      int npend = 0;
+      auto do_pv = [&](const Ev& e) -> bool {
+        if (e.act) {
+          // O += P V; the P sits in the S buffer its S used (PV k reads buffer k % NSB).
+          const int pb = pc % SH::NSB;
+          if (!wait1(&p_full[s * SH::NSB + pb], (pc / SH::NSB) & 1)) return false;
+          if (e.first && !wait1(&o_empty[s], (oc & 1) ^ 1)) return false;
+          const uint64_t vd = v_desc0 + (uint64_t)((e.st * SH::KV_BYTES) >> 4);
+          const uint32_t t_p = t_s0 + (uint32_t)(pb * kBK);
+          if (leader) {
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)  // 16 keys = 16 rows of 128 bytes per K step
+              umma_f16_ts(t_o, t_p + kk * 8, vd + (uint64_t)(kk * 16 * SH::ROWB >> 4), idesc_pv,
+                          (kk > 0 || !e.first) ? 1u : 0u);
+            umma_commit(&pv_done[s * SH::NSB + pb]);
+            if (e.last) umma_commit(&o_full[s]);
+            umma_commit(&kv_empty[e.st]);  // the block is released once this P V has read it
+          }
+          ++pc;
+          if (e.last) ++oc;
+        } else if (leader) {
+          mbar_arrive(&kv_empty[e.st]);  // a block this slot does not use
+        }
+        return true;
+      };
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
         const LongItem it = long_item(i, prm, n_units, npairs, ntiles);
         const bool act = (s ? it.tile[1] : it.tile[0]) >= 0;
@@ -295,57 +331,43 @@ __global__ void __launch_bounds__(kLongThreads, 1)
         const int qb = qc % SH::NQB;
         if (act && !(ok = wait1(&q_avail[s * SH::NQB + qb], (qc / SH::NQB) & 1))) break;
         const uint64_t qd = q_desc0 + (uint64_t)((qb * SH::Q_BYTES) >> 4);
-        for (int j = 0; j <= it.nblocks && ok; ++j) {
+        for (int j = 0; j < it.nblocks && ok; ++j) {
           const int st = (kvc + j) % SH::NKV;
-          const int stp = (kvc + j + SH::NKV - 1) % SH::NKV;  // stage of block j - 1
-          if (j < it.nblocks && !(ok = wait1(&kv_avail[st], ((kvc + j) / SH::NKV) & 1))) break;
-          if (act && j >= first && j <= last) {
-            // S = Q K^T of block j into the slot's next S buffer.  That buffer
-            // last held the P of two blocks back, whose P V is already issued.
-            const int sb = sc & 1;
+          if (!(ok = wait1(&kv_avail[st], ((kvc + j) / SH::NKV) & 1))) break;
+          const bool a = act && j >= first && j <= last;
+          if (a) {
+            // S = Q K^T of block j into the slot's next S buffer; the P V that
+            // last read it (three S back) was issued before the previous S.
+            const int sb = sc % SH::NSB;
             const uint64_t kd = k_desc0 + (uint64_t)((st * SH::KV_BYTES) >> 4);
             if (leader) {
               tc_fence_after();
 #pragma unroll
               for (int kk = 0; kk < D / 16; ++kk)
                 umma_f16_ss(t_s0 + (uint32_t)(sb * kBK), qd + 2 * kk, kd + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
-              umma_commit(&s_full[s * 2 + sb]);
+              umma_commit(&s_full[s * SH::NSB + sb]);
               if (j == last) umma_commit(&q_empty[s * SH::NQB + qb]);
             }
             ++sc;
             if (j == last) ++qc;
           }
-          if (act && j - 1 >= first && j - 1 <= last) {
-            // O += P V of block j - 1.
-            const int pb = pc & 1;
-            if (!(ok = wait1(&p_full[s * 2 + pb], (pc >> 1) & 1))) break;
-            ++pc;
-            const int ob = oc & 1;
-            if (j - 1 == first && !(ok = wait1(&o_empty[s * 2 + ob], ((oc >> 1) & 1) ^ 1))) break;
-            const uint64_t vd = v_desc0 + (uint64_t)((stp * SH::KV_BYTES) >> 4);
-            const uint32_t t_p = t_s0 + (uint32_t)(pb * kBK);
-            const uint32_t acc0 = (j - 1 > first) ? 1u : 0u;
-            if (leader) {
-              tc_fence_after();
-#pragma unroll
-              for (int kk = 0; kk < kBK / 16; ++kk)  // 16 keys = 16 rows of 128 bytes per K step
-                umma_f16_ts(t_o0 + (uint32_t)(ob * D), t_p + kk * 8, vd + (uint64_t)(kk * 16 * SH::ROWB >> 4),
-                            idesc_pv, kk > 0 ? 1u : acc0);
-              umma_commit(&pv_done[s]);
-              if (j - 1 == last) umma_commit(&o_full[s * 2 + ob]);
-            }
-            if (j - 1 == last) ++oc;
-          }
-          if (j >= 1 && leader) {
-            // Release block j - 1 (its kv_full was waited at step j - 1).
-            if (act && j - 1 >= first && j - 1 <= last)
-              umma_commit(&kv_empty[stp]);
-            else
-              mbar_arrive(&kv_empty[stp]);
+          const Ev e{st, a ? 1 : 0, j == first ? 1 : 0, j == last ? 1 : 0};
+          if (npend == 2) {
+            if (!(ok = do_pv(pq0))) break;
+            pq0 = pq1;
+            pq1 = e;
+          } else if (npend == 1) {
+            pq1 = e;
+            npend = 2;
+          } else {
+            pq0 = e;
+            npend = 1;
           }
         }
         kvc += it.nblocks;
       }
+      if (ok && npend >= 1) ok = do_pv(pq0);
+      if (ok && npend == 2) ok = do_pv(pq1);
       if (leader) {
         umma_commit(drain + s);
         mbar_wait(drain + s, 0, nullptr, nullptr);
@@ -414,14 +436,14 @@ __global__ void __launch_bounds__(kLongThreads, 1)
 
     // Deferred epilogue of a finished item: O / l -> HBM.
     struct Pending {
-      int valid, b, g, pos, ob, k;
+      int valid, b, g, pos, k;
       float l;
-    } pend{0, 0, 0, 0, 0, 0, 0.f};
+    } pend{0, 0, 0, 0, 0, 0.f};
     auto epilogue = [&](const Pending& pe) -> bool {
-      if (!__all_sync(0xffffffffu, mbar_wait(&o_full[s * 2 + pe.ob], (pe.k >> 1) & 1, abort_flag, prm.status)))
+      if (!__all_sync(0xffffffffu, mbar_wait(&o_full[s], pe.k & 1, abort_flag, prm.status)))
         return false;
       tc_fence_after();
-      const uint32_t t_o = t_lane + SH::TMEM_O + (uint32_t)((2 * s + pe.ob) * D);
+      const uint32_t t_o = t_lane + SH::TMEM_O + (uint32_t)(s * D);
       uint32_t o0[32], o1[32];
       tmem_ld32_async(t_o, o0);
       tmem_ld32_async(t_o + 32, o1);
@@ -429,7 +451,7 @@ __global__ void __launch_bounds__(kLongThreads, 1)
       tmem_wait_ld(o1);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[s * 2 + pe.ob]);
+      if (lane == 0) mbar_arrive(&o_empty[s]);
       if (r < q_rows && pe.pos < S) {
         const float inv = 1.f / pe.l;
         typename E::T* orow = reinterpret_cast<typename E::T*>(prm.o) + (size_t)pe.b * prm.o_sb +
@@ -465,14 +487,14 @@ __global__ void __launch_bounds__(kLongThreads, 1)
       const int hi = valid_row ? pos : (1 << 30);
       const bool warp_band = __any_sync(0xffffffffu, padded);
       const RowScore rs(padded, c2, sd64);
-      const int ob = oc & 1;
       float m = -INFINITY, l0 = 0.f, l1 = 0.f;
       for (int j = first; j <= last; ++j) {
-        const int sb = sc & 1;
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[s * 2 + sb], (sc >> 1) & 1, abort_flag, prm.status))))
+        const int sb = sc % SH::NSB;
+        if (!(ok = __all_sync(0xffffffffu,
+                              mbar_wait(&s_full[s * SH::NSB + sb], (sc / SH::NSB) & 1, abort_flag, prm.status))))
           break;
         tc_fence_after();
-        const uint32_t t_sb = t_lane + SH::TMEM_S + (uint32_t)((2 * s + sb) * kBK);
+        const uint32_t t_sb = t_lane + SH::TMEM_S + (uint32_t)((SH::NSB * s + sb) * kBK);
         const int kb = it.kstart + j * kBK;
         uint32_t u[2][32];
         tmem_ld32_async(t_sb, u[0]);
@@ -525,9 +547,12 @@ __global__ void __launch_bounds__(kLongThreads, 1)
           // f != 1 only after an earlier block of this item.  Wait for the
           // slot's latest P V (the completed S of this block implies every
           // earlier one is done), then scale the O rows.
-          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[s], (sc - 1) & 1, abort_flag, prm.status)))) break;
+          const int pvb = (sc - 1) % SH::NSB;  // P V of the previous block read S buffer pvb
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[s * SH::NSB + pvb], ((sc - 1) / SH::NSB) & 1,
+                                                       abort_flag, prm.status))))
+            break;
           tc_fence_after();
-          const uint32_t t_o = t_lane + SH::TMEM_O + (uint32_t)((2 * s + ob) * D);
+          const uint32_t t_o = t_lane + SH::TMEM_O + (uint32_t)(s * D);
 #pragma unroll 1
           for (int c = 0; c < D; c += 16) {
             uint32_t ov[16];
@@ -581,7 +606,7 @@ __global__ void __launch_bounds__(kLongThreads, 1)
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[s * 2 + sb]);
+        if (lane == 0) mbar_arrive(&p_full[s * SH::NSB + sb]);
         ++sc;
         if (j == first && pend.valid) {
           if (!(ok = epilogue(pend))) break;
@@ -589,7 +614,7 @@ __global__ void __launch_bounds__(kLongThreads, 1)
         }
       }
       if (!ok) break;
-      pend = Pending{1, it.b, it.g, pos, ob, oc, l0 + l1};
+      pend = Pending{1, it.b, it.g, pos, oc, l0 + l1};
       ++oc;
     }
     if (ok && pend.valid) epilogue(pend);
