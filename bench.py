@@ -319,6 +319,7 @@ def run_ours(args):
             line["prefill_long"] = bench_prefill_cfg4(dev, peaks)
             line["prefill_long"]["rmsnorm_qkv_kernel"] = bench_rmsnorm_qkv_cfg4(dev, peaks)
             line["prefill_long"]["rmsnorm_swiglu_kernel"] = bench_rmsnorm_swiglu_cfg4(dev, peaks)
+            line["prefill_long"]["frames_kernel"] = bench_frames_cfg4(dev, peaks)
         line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
@@ -618,6 +619,40 @@ def bench_rmsnorm_swiglu_cfg4(dev, peaks, batch=None):
                          "peak_source": peaks["source"]}}
 
 
+def bench_frames_cfg4(dev, peaks, batch=None):
+    """The state encoder's input kernel at cfg4's shape: batch x 256 frame stacks of
+    4 x 84 x 84 uint8 -> bf16 4x4 space-to-depth blocks (and the frames' maximum)."""
+    from rl_for_mario_b200.kernels import device_status, frames_to_blocks
+
+    C = PREFILL_LONG_CFG
+    n = (batch or C["batch"]) * C["timesteps"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    fr = torch.randint(0, 256, (n, 4, 84, 84), device=dev, generator=g, dtype=torch.uint8)
+    fm = torch.zeros(1, dtype=torch.int32, device=dev)
+    for _ in range(3):
+        out = frames_to_blocks(fr, torch.bfloat16, fm)
+    del out
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record()
+    for _ in range(reps):
+        out = frames_to_blocks(fr, torch.bfloat16, fm)
+    e1.record()
+    torch.cuda.synchronize()
+    if device_status() != 0:
+        raise SystemExit("device status error in the frame-block benchmark")
+    ms = e0.elapsed_time(e1) / reps
+    byts = fr.numel() * 3  # uint8 in, bf16 out
+    gbs = byts / (ms * 1e-3) / 1e9
+    del fr, out
+    torch.cuda.empty_cache()
+    return {"kernel": "frame_cta_to_blocks_kernel", "frames": n, "ms": ms,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": byts,
+                         "peak_source": peaks["source"]}}
+
+
 def bench_rollout_cfg5(dev, world, rank, pg):
     """8,192 environments per GPU, 64 cached steps, CNN on synthetic frames, all-gather of logits."""
     from rl_for_mario_b200.dt_model import DTConfig, MarioDT
@@ -692,7 +727,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / rollout sub-benchmarks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
-    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu"], default=None,
+    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "frames"],
+                    default=None,
                     help="run one sub-benchmark alone and print its JSON (profiling)")
     ap.add_argument("--long-batch", type=int, default=None,
                     help="with --only prefill_long: batch of the attention-kernel case, model forward skipped")
@@ -707,6 +743,8 @@ def main():
             emit({"only": "decode", **bench_decode_cfg3(dev, _peaks())})
         elif args.only == "rmsnorm_qkv":
             emit({"only": "rmsnorm_qkv", **bench_rmsnorm_qkv_cfg4(dev, _peaks(), batch=args.long_batch)})
+        elif args.only == "frames":
+            emit({"only": "frames", **bench_frames_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "rmsnorm_swiglu":
             emit({"only": "rmsnorm_swiglu", **bench_rmsnorm_swiglu_cfg4(dev, _peaks(), batch=args.long_batch)})
         else:
