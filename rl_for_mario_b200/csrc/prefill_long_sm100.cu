@@ -506,10 +506,20 @@ __global__ void __launch_bounds__(kLongThreads, 1)
         for (int c = 0; c < 2; ++c) mk[c] = masked ? key_mask32(kb + 32 * c, lo, hi) : 0xffffffffu;
         tmem_wait_ld(u[0]);
         tmem_wait_ld(u[1]);
+        if (masked && !warp_band) {
+          // Valid rows: a disallowed key's score becomes -inf, after which the
+          // unmasked path gives it P = 0 (one test and select per score
+          // instead of a separate, slower masked path).
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj)
+              if (!((mk[c] >> jj) & 1u)) u[c][jj] = 0xff800000u;
+        }
 
         // Block maximum over the allowed keys, in log2 units.
         float x0 = -INFINITY, x1 = -INFINITY, x2 = -INFINITY, x3 = -INFINITY;
-        if (masked) {
+        if (warp_band) {
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -567,7 +577,7 @@ __global__ void __launch_bounds__(kLongThreads, 1)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t pk[16];
-          if (!masked) {
+          if (!warp_band) {
             const float2 c2v = make_float2(c2, c2), nmv = make_float2(-mm, -mm);
             float2 lv = make_float2(0.f, 0.f);
 #pragma unroll
@@ -580,21 +590,12 @@ __global__ void __launch_bounds__(kLongThreads, 1)
             }
             l0 += lv.x;
             l1 += lv.y;
-          } else if (warp_band) {
+          } else {
+            // warps holding fully padded rows: the reference's -1e9 bands
 #pragma unroll
             for (int jj = 0; jj < 32; jj += 2) {
               const float t0 = ((mk[c] >> jj) & 1u) ? rs(__uint_as_float(u[c][jj])) - mm : -INFINITY;
               const float t1 = ((mk[c] >> (jj + 1)) & 1u) ? rs(__uint_as_float(u[c][jj + 1])) - mm : -INFINITY;
-              const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
-              l0 += p0;
-              l1 += p1;
-              pk[jj >> 1] = E::from_f2(p0, p1);
-            }
-          } else {
-#pragma unroll
-            for (int jj = 0; jj < 32; jj += 2) {
-              const float t0 = ((mk[c] >> jj) & 1u) ? fmaf(__uint_as_float(u[c][jj]), c2, -mm) : -INFINITY;
-              const float t1 = ((mk[c] >> (jj + 1)) & 1u) ? fmaf(__uint_as_float(u[c][jj + 1]), c2, -mm) : -INFINITY;
               const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
               l0 += p0;
               l1 += p1;
