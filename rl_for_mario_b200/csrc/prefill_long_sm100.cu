@@ -506,10 +506,10 @@ __global__ void __launch_bounds__(kLongThreads, 1)
         for (int c = 0; c < 2; ++c) mk[c] = masked ? key_mask32(kb + 32 * c, lo, hi) : 0xffffffffu;
         tmem_wait_ld(u[0]);
         tmem_wait_ld(u[1]);
-        if (masked && !warp_band) {
-          // Valid rows: a disallowed key's score becomes -inf, after which the
-          // unmasked path gives it P = 0 (one test and select per score
-          // instead of a separate, slower masked path).
+        if (masked) {
+          // A disallowed key's score becomes -inf, after which the row max and
+          // P need no mask (P = 0 for it): one test and select per score
+          // instead of separate, slower masked paths.
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -518,27 +518,16 @@ __global__ void __launch_bounds__(kLongThreads, 1)
         }
 
         // Block maximum over the allowed keys, in log2 units.
-        float x0 = -INFINITY, x1 = -INFINITY, x2 = -INFINITY, x3 = -INFINITY;
-        if (warp_band) {
+        // (the row score is monotonic in s, so the max of the raw scores gives it)
+        float x0 = -INFINITY, x1 = -INFINITY;
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int jj = 0; jj < 32; jj += 4) {
-              x0 = fmaxf(x0, ((mk[c] >> jj) & 1u) ? __uint_as_float(u[c][jj]) : -INFINITY);
-              x1 = fmaxf(x1, ((mk[c] >> (jj + 1)) & 1u) ? __uint_as_float(u[c][jj + 1]) : -INFINITY);
-              x2 = fmaxf(x2, ((mk[c] >> (jj + 2)) & 1u) ? __uint_as_float(u[c][jj + 2]) : -INFINITY);
-              x3 = fmaxf(x3, ((mk[c] >> (jj + 3)) & 1u) ? __uint_as_float(u[c][jj + 3]) : -INFINITY);
-            }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int jj = 0; jj < 32; jj += 4) {
-              x0 = fmax3(x0, __uint_as_float(u[c][jj]), __uint_as_float(u[c][jj + 1]));
-              x1 = fmax3(x1, __uint_as_float(u[c][jj + 2]), __uint_as_float(u[c][jj + 3]));
-            }
-        }
-        const float bmax = rs(fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)));
+          for (int jj = 0; jj < 32; jj += 4) {
+            x0 = fmax3(x0, __uint_as_float(u[c][jj]), __uint_as_float(u[c][jj + 1]));
+            x1 = fmax3(x1, __uint_as_float(u[c][jj + 2]), __uint_as_float(u[c][jj + 3]));
+          }
+        const float bmax = rs(fmaxf(x0, x1));
         // Move the reference only when P would exceed 2^8; then scale what
         // this row has accumulated (O in TMEM, the row sum) exactly.
         float f = 1.f;
@@ -591,16 +580,23 @@ __global__ void __launch_bounds__(kLongThreads, 1)
             l0 += lv.x;
             l1 += lv.y;
           } else {
-            // warps holding fully padded rows: the reference's -1e9 bands
+            // warps holding fully padded rows: the row score rs(s) - m as
+            // ((s mul + add) - add) out - m, two lanes per f32x2 instruction with
+            // the same roundings as the scalar form (disallowed keys are -inf)
+            const float2 mul2 = make_float2(rs.mul, rs.mul), add2 = make_float2(rs.add, rs.add);
+            const float2 nadd2 = make_float2(-rs.add, -rs.add), out2 = make_float2(rs.out, rs.out);
+            const float2 nmv = make_float2(-mm, -mm);
+            float2 lv = make_float2(0.f, 0.f);
 #pragma unroll
             for (int jj = 0; jj < 32; jj += 2) {
-              const float t0 = ((mk[c] >> jj) & 1u) ? rs(__uint_as_float(u[c][jj])) - mm : -INFINITY;
-              const float t1 = ((mk[c] >> (jj + 1)) & 1u) ? rs(__uint_as_float(u[c][jj + 1])) - mm : -INFINITY;
-              const float p0 = ex2_approx(t0), p1 = ex2_approx(t1);
-              l0 += p0;
-              l1 += p1;
-              pk[jj >> 1] = E::from_f2(p0, p1);
+              const float2 sv = make_float2(__uint_as_float(u[c][jj]), __uint_as_float(u[c][jj + 1]));
+              const float2 t = fadd2(fmul2(fadd2(ffma2(sv, mul2, add2), nadd2), out2), nmv);
+              const float2 pp = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+              lv = fadd2(lv, pp);
+              pk[jj >> 1] = E::from_f2(pp.x, pp.y);
             }
+            l0 += lv.x;
+            l1 += lv.y;
           }
           tmem_st16(t_sb + 16 * c, pk);
         }
