@@ -68,7 +68,9 @@ class RMSNorm(nn.Module):
     def forward(self, x: Tensor) -> Tensor:
         w = self.weight
         if (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype and x.numel()
-                and x.shape[-1] % 8 == 0 and not (torch.is_grad_enabled() and (x.requires_grad or w.requires_grad))):
+                and x.shape[-1] % 8 == 0 and x.stride(-1) == 1 and x.data_ptr() % 16 == 0
+                and all(st % 8 == 0 for st in x.stride()[:-1])
+                and not (torch.is_grad_enabled() and (x.requires_grad or w.requires_grad))):
             return kernels.rmsnorm(x, w.contiguous(), self.eps)  # one pass, same rounding
         xf = x.float()
         return w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).type_as(x)
@@ -240,6 +242,8 @@ class MarioStateEncoder(nn.Module):
         if self._fused_conv and x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype:
             try:
                 return torch.cudnn_convolution_relu(x, w, b, tuple(stride), (0, 0), (1, 1), 1)
+            except torch.cuda.OutOfMemoryError:
+                raise
             except RuntimeError:
                 type(self)._fused_conv = False  # no fused engine for this build / shape
         return F.relu(F.conv2d(x, w, b, stride=stride), inplace=True)

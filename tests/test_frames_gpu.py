@@ -96,3 +96,20 @@ def test_rmsnorm_kernel_matches_reference(M, K, dtype):
     # a different summation order may move the normalised value across a rounding boundary
     assert (err <= 2 * ulp * ref.float().abs() + 1e-6).all(), err.max().item()
     assert (err == 0).float().mean().item() > 0.95
+
+
+@pytest.mark.gpu
+def test_rmsnorm_module_unaligned_view_uses_reference_formula():
+    """A row view that is not 16-byte aligned takes the PyTorch formula instead of the kernel."""
+    from rl_for_mario_b200.dt_model import RMSNorm
+
+    g = torch.Generator().manual_seed(3)
+    big = (torch.randn(6, 10, 72, generator=g) * 2).to(torch.bfloat16).cuda()
+    x = big[..., 3:67]  # 64 columns starting 6 bytes into each row
+    norm = RMSNorm(64).cuda().to(torch.bfloat16)
+    with torch.no_grad():
+        norm.weight.copy_((1 + 0.1 * torch.randn(64, generator=g)).to(torch.bfloat16))
+        y = norm(x)
+    xf = x.float()
+    ref = norm.weight * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + norm.eps)).to(torch.bfloat16)
+    assert torch.equal(y, ref)
