@@ -212,7 +212,7 @@ def run_reference(args):
 
 def run_ours(args):
     from rl_for_mario_b200 import _lib
-    from rl_for_mario_b200.kernels import attn_prefill, device_status
+    from rl_for_mario_b200.kernels import attn_prefill, attn_prefill_host, device_status
     from oracle import precompute_freqs_cis
 
     rank, world, local, pg = _dist_setup(args.gpus)
@@ -267,12 +267,8 @@ def run_ours(args):
     e2e_steps = max(3, min(args.steps, 10))
 
     def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        dpad.copy_(hpad, non_blocking=True)
-        attn_prefill(dq, dk, dv, cos, sin, dpad, out=out)
-        ho.copy_(out, non_blocking=True)
+        # the host-buffer entry point: uploads, kernel and download pipelined over chunks of samples
+        attn_prefill_host(hq, hk, hv, cos, sin, hpad, ho, (dq, dk, dv, dpad, out), chunks=8)
 
     e2e_step()
     torch.cuda.synchronize()

@@ -93,6 +93,68 @@ def attn_prefill(q: Tensor, k: Tensor, v: Tensor, cos: Optional[Tensor], sin: Op
     return out
 
 
+_COPY_STREAMS: dict = {}
+
+
+def _copy_streams(device: torch.device):
+    """A host-to-device and a device-to-host stream per device (created once)."""
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    if key not in _COPY_STREAMS:
+        _COPY_STREAMS[key] = (torch.cuda.Stream(device=key), torch.cuda.Stream(device=key))
+    return _COPY_STREAMS[key]
+
+
+def attn_prefill_host(hq: Tensor, hk: Tensor, hv: Tensor, cos: Optional[Tensor], sin: Optional[Tensor],
+                      hpad: Optional[Tensor], hout: Tensor, device_buffers: Tuple[Tensor, ...],
+                      chunks: int = 8, apply_rope: bool = True, scale: Optional[float] = None) -> Tensor:
+    """attn_prefill on host tensors: q/k/v (and pad_len) in pinned host memory in,
+    out into the pinned host tensor ``hout``.
+
+    The batch is cut into ``chunks`` pieces of whole samples (samples are
+    independent) and pipelined over three streams: the copy of chunk i + 1 to
+    the device, the kernel on chunk i (current stream) and the copy of chunk
+    i - 1 back run at the same time, so the step costs about the larger of the
+    two PCIe transfers instead of their sum.  ``device_buffers`` = (q, k, v,
+    pad_len or None, out) device tensors of the full batch's shapes.  On return
+    the current stream is ordered after every copy (synchronise it, or record an
+    event on it, before reading ``hout`` on the host).
+    """
+    dq, dk, dv, dpad, dout = device_buffers
+    for name, h in (("hq", hq), ("hk", hk), ("hv", hv), ("hout", hout), ("hpad", hpad)):
+        if h is not None and (h.is_cuda or not h.is_pinned()):
+            raise ValueError(f"{name} must be a pinned host tensor")
+    _require_cuda(dq, dk, dv, dpad, dout)
+    if (hpad is None) != (dpad is None):
+        raise ValueError("hpad and the device pad_len buffer go together")
+    B = hq.shape[0]
+    chunks = max(1, min(int(chunks), B))
+    bounds = [B * i // chunks for i in range(chunks + 1)]
+    dev = dq.device
+    cur = torch.cuda.current_stream(dev)
+    s_in, s_out = _copy_streams(dev)
+    # Earlier work on the current stream (a previous call's kernels reading these
+    # buffers) comes before this call's uploads.
+    s_in.wait_stream(cur)
+    for i in range(chunks):
+        b0, b1 = bounds[i], bounds[i + 1]
+        if b1 == b0:
+            continue
+        with torch.cuda.stream(s_in):
+            dq[b0:b1].copy_(hq[b0:b1], non_blocking=True)
+            dk[b0:b1].copy_(hk[b0:b1], non_blocking=True)
+            dv[b0:b1].copy_(hv[b0:b1], non_blocking=True)
+            if hpad is not None:
+                dpad[b0:b1].copy_(hpad[b0:b1], non_blocking=True)
+        cur.wait_stream(s_in)
+        attn_prefill(dq[b0:b1], dk[b0:b1], dv[b0:b1], cos, sin, None if dpad is None else dpad[b0:b1],
+                     out=dout[b0:b1], apply_rope=apply_rope, scale=scale)
+        s_out.wait_stream(cur)
+        with torch.cuda.stream(s_out):
+            hout[b0:b1].copy_(dout[b0:b1], non_blocking=True)
+    cur.wait_stream(s_out)
+    return hout
+
+
 def device_status(device: Optional[torch.device] = None) -> int:
     """Synchronises the current stream; returns and clears the kernels' device status word."""
     dev = device or torch.device("cuda", torch.cuda.current_device())

@@ -172,3 +172,39 @@ LONG_CASES = [
 def test_prefill_prerotated_matches_oracle(case):
     out, ref = _run_case(*case, rope=False)
     _check(out, ref, case[6])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,chunks", [(37, 8), (5, 2), (3, 8), (1, 1)])
+def test_prefill_host_pipeline_matches_device_call(B, chunks):
+    """The host-buffer entry point (chunked, pipelined copies) gives the device call's result bit for bit,
+    twice in a row on the same buffers."""
+    from rl_for_mario_b200.kernels import attn_prefill, attn_prefill_host, device_status
+
+    S, Hq, Hkv, D = 192, 8, 2, 32
+    g = torch.Generator().manual_seed(B * 10 + chunks)
+    q = (torch.randn(B, S, Hq, D, generator=g) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, S, Hkv, D, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, S, Hkv, D, generator=g) * 0.5).to(torch.bfloat16)
+    pad = torch.randint(0, 97, (B,), generator=g, dtype=torch.int32)
+    cos, sin = (t.cuda() for t in precompute_freqs_cis(D, S))
+    ref = attn_prefill(q.cuda(), k.cuda(), v.cuda(), cos, sin, pad.cuda()).cpu()
+    hq, hk, hv, hpad = (t.pin_memory() for t in (q, k, v, pad))
+    ho = torch.empty(B, S, Hq, D, dtype=torch.bfloat16).pin_memory()
+    bufs = tuple(torch.empty(t.shape, dtype=t.dtype, device="cuda") for t in (q, k, v, pad, ho))
+    for _ in range(2):
+        ho.zero_()
+        attn_prefill_host(hq, hk, hv, cos, sin, hpad, ho, bufs, chunks=chunks)
+        torch.cuda.current_stream().synchronize()
+        assert device_status() == 0
+        assert torch.equal(ho, ref)
+
+
+@pytest.mark.gpu
+def test_prefill_host_rejects_pageable_buffers():
+    from rl_for_mario_b200.kernels import attn_prefill_host
+
+    t = torch.zeros(2, 8, 2, 32, dtype=torch.bfloat16)
+    bufs = tuple(torch.zeros(2, 8, 2, 32, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    with pytest.raises(ValueError):
+        attn_prefill_host(t, t, t, None, None, None, t.pin_memory(), bufs + (None, bufs[0]), apply_rope=False)
