@@ -36,7 +36,10 @@ namespace {
 constexpr int kDecThreads = kDecodeThreads;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kKMax = kDecodeKeyBlock;  // keys staged per block
-constexpr int kSnSmem = 16;  // new tokens staged from registers (more: re-read from the cache)
+// New tokens staged from registers (more: re-read from the cache).  8 covers
+// the rollout's 3 tokens per step and keeps a D = 32 CTA under 19 KB of shared
+// memory: 12 CTAs per SM, as many as the registers allow.
+constexpr int kSnSmem = 8;
 
 template <int D>
 struct DecShape {
@@ -49,7 +52,10 @@ struct DecShape {
   static constexpr int OFF_VN = OFF_KN + kSnSmem * ROWB;
   static constexpr int OFF_BT = OFF_VN + kSnSmem * ROWB;  // block-table row (vectorised front, <= one page per thread)
   static constexpr int OFF_BAR = OFF_BT + kDecThreads * 4;  // page-copy barrier
-  static constexpr int SMEM = OFF_BAR + 16 + 1024;        // + alignment of the K/V rows for TMA swizzle
+  // Base alignment of the K/V rows: one period of the TMA swizzle pattern
+  // (64-byte rows: 512 B; 128-byte rows: 1024 B).
+  static constexpr int ALIGN = ROWB == 64 ? 512 : 1024;
+  static constexpr int SMEM = OFF_BAR + 16 + ALIGN;
   // Split-K partials [warps][16][D + 2] floats, over the K / V rows once a row
   // group's blocks are consumed.
   static constexpr int OFF_RED = OFF_K;
@@ -117,7 +123,8 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const __grid_con
   using E = Elem<BF16>;
   using T = typename E::T;
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + SH::ALIGN - 1) &
+                                             ~uintptr_t(SH::ALIGN - 1));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int b = blockIdx.x / p.Hkv;
   const int g = blockIdx.x - b * p.Hkv;

@@ -18,6 +18,8 @@ CASES = [
     (3, 40, 1, 8, 2, 32, 16, [0, 1, 40], torch.bfloat16, True),
     (2, 30, 3, 12, 4, 64, 32, [0, 9], torch.float16, False),
     (2, 50, 8, 8, 2, 32, 64, [0, 20], torch.bfloat16, False),
+    (2, 60, 12, 8, 2, 32, 64, [0, 30], torch.bfloat16, True),   # new tokens re-read from the cache
+    (3, 70, 20, 8, 2, 32, 32, "random", torch.bfloat16, False),
     (5, 253, 3, 8, 2, 32, 64, "random", torch.bfloat16, True),
     (2, 100, 3, 4, 4, 64, 64, None, torch.bfloat16, True),
     (3, 24, 3, 8, 2, 32, 16, [0, 6, 15], torch.float32, True),
