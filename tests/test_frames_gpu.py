@@ -50,9 +50,11 @@ def test_frames_to_blocks_rejects_bad_shapes():
 
 
 @pytest.mark.gpu
-def test_state_encoder_matches_direct_convolution():
-    """bf16 encoder (frame blocks + 2 x 2 convolution) vs the reference's direct
-    8 x 8 stride-4 convolution of frames / 255, in fp32."""
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_state_encoder_matches_direct_convolution(dtype):
+    """16-bit encoder (frame blocks + 2 x 2 convolution, fused convolution + bias +
+    ReLU, permuted Linear) vs the reference's direct 8 x 8 stride-4 convolution of
+    frames / 255, in fp32."""
     from rl_for_mario_b200.dt_model import MarioStateEncoder
 
     torch.manual_seed(0)
@@ -60,7 +62,7 @@ def test_state_encoder_matches_direct_convolution():
     s = torch.randint(0, 256, (3, 5, 4, 84, 84), dtype=torch.uint8)
     with torch.no_grad():
         ref = enc.cnn(s.reshape(15, 4, 84, 84).float() / 255.0).reshape(3, 5, -1)
-        out = enc.cuda().to(torch.bfloat16)(s.cuda())
+        out = enc.cuda().to(dtype)(s.cuda())
     err = (out.float().cpu() - ref).abs().max().item()
     assert err < 3e-2 * max(1.0, ref.abs().max().item()), err
 

@@ -102,16 +102,18 @@ def test_rmsnorm_qkv_rope_matches_reference(B, S, K, Hq, Hkv, D, dtype, tables):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("hidden,heads,kv_heads,S", [(256, 8, 2, 96), (768, 12, 4, 300)])
-def test_fused_block_with_rope_epilogue_matches_unfused_block(hidden, heads, kv_heads, S):
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_block_with_rope_epilogue_matches_unfused_block(hidden, heads, kv_heads, S, dtype):
     """A block whose RMSNorm + QKV + RoPE run in one kernel and whose attention
-    takes pre-rotated q / k (short and long prefill kernels) equals the unfused block."""
+    takes pre-rotated q / k (short and long prefill kernels), with the fused
+    RMSNorm + SwiGLU MLP and residual GEMMs, equals the unfused block."""
     from rl_for_mario_b200.dt_model import DTConfig, DTBlock, rope_tables
 
     cfg = DTConfig(hidden_size=hidden, num_attention_heads=heads, num_key_value_heads=kv_heads,
                    context_len=(S + 2) // 3, dropout=0.0)
     torch.manual_seed(1)
-    blk = DTBlock(cfg).cuda().to(torch.bfloat16).eval()
-    x = torch.randn(3, S, hidden, device="cuda").to(torch.bfloat16)
+    blk = DTBlock(cfg).cuda().to(dtype).eval()
+    x = torch.randn(3, S, hidden, device="cuda").to(dtype)
     cos, sin = (t.cuda() for t in rope_tables(hidden // heads, S, 1e4))
     mask = (torch.arange(S, device="cuda")[None] >= torch.tensor([0, 5, S // 2], device="cuda")[:, None]).float()
     with torch.no_grad():
