@@ -658,7 +658,7 @@ def bench_rollout_cfg5(dev, world, rank, pg):
     torch.manual_seed(4)  # identical replicated weights on every rank
     cfg = DTConfig(hidden_size=C["hidden"], num_hidden_layers=C["layers"], num_attention_heads=C["q_heads"],
                    num_key_value_heads=C["kv_heads"], context_len=C["context_len"], dropout=0.0)
-    model = MarioDT(cfg).to(dev, torch.bfloat16).eval()
+    model = MarioDT(cfg).to(dev, torch.bfloat16).eval().fuse_norms()  # fused blocks
     b = C["envs_per_gpu"]
     B = b * world
     ro = DTRollout(model, num_envs=B, max_steps=C["steps"], page_size=64, device=dev)
@@ -691,8 +691,8 @@ def bench_rollout_cfg5(dev, world, rank, pg):
     res = {"metric": "sharded rollout env-steps/s (CNN + 4 layers + cached attention + all-gather)",
            "unit": "env-steps/s", "value": B * C["steps"] / (ms * 1e-3), "ms_total": ms, "n_gpus": world,
            "scaling": "weak",
-           "config": {"workload": f"{b} envs per GPU ({B} total), 64 steps, window 192, repo-default DT bf16, "
-                                  "synthetic uint8 frames, all_gather of [B/N, 7] logits per step"}}
+           "config": {"workload": f"{b} envs per GPU ({B} total), 64 steps, window 192, repo-default DT bf16 "
+                                  "(fused blocks), synthetic uint8 frames, all_gather of [B/N, 7] logits per step"}}
     del ro, model, frames
     torch.cuda.empty_cache()
     return res

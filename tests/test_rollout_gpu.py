@@ -8,8 +8,11 @@ from oracle.seeded import seeded_state_dict
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_cached_rollout_matches_reprefill(dtype):
+@pytest.mark.parametrize("dtype,fused", [(torch.float32, False), (torch.bfloat16, False), (torch.bfloat16, True)])
+def test_cached_rollout_matches_reprefill(dtype, fused):
+    """fused: every block on the fused kernels (RMSNorm + q|k|v + RoPE GEMM before the
+    decode kernel, RMSNorm + SwiGLU GEMM, residual GEMMs), in the rollout and in the
+    re-prefill alike."""
     from rl_for_mario_b200.dt_model import DTConfig, MarioDT
     from rl_for_mario_b200.rollout import DTRollout
 
@@ -21,6 +24,8 @@ def test_cached_rollout_matches_reprefill(dtype):
     model = MarioDT(cfg)
     model.load_state_dict(seeded_state_dict(dt_param_shapes(cfgd), 9), strict=True)
     model = model.cuda().to(dtype).eval()
+    if fused:
+        model.fuse_norms()
     B, T = 6, 8
     g = torch.Generator().manual_seed(0)
     states = torch.randint(0, 256, (B, T, 4, 84, 84), generator=g, dtype=torch.uint8).cuda()
