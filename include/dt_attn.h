@@ -163,6 +163,19 @@ int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, 
  */
 
 /*
+ * The state encoder's first layer from the uint8 frames: frames / 255 (when
+ * their maximum exceeds 1, model_decision_transformer.py:338), Conv2d(4, 32,
+ * 8, stride 4) and ReLU (:315-341), as one implicit GEMM on the tensor cores.
+ * frames [N, 4, H, W] uint8 (H, W = 8 + 4k; 16-byte aligned, N*4*H*W a
+ * multiple of 16); w [32, 256] 16-bit, the conv weight [32, 4, 8, 8] as is
+ * (unscaled); bias [32] fp32; y [N, OH, OW, 32] 16-bit (channels-last, OH =
+ * (H - 8) / 4 + 1); frame_max (device) ends > 1 exactly when some byte of the
+ * frames exceeds 1 (the reference's test; the scan stops at the first such byte).
+ */
+int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int W, const void* w, const float* bias,
+                    unsigned int* frame_max, void* y, int dtype, void* stream);
+
+/*
  * RMSNorm with the reference's rounding: y = w * cast(x * rsqrt(mean(x^2) +
  * eps)) with the mean and rsqrt in fp32, the normalised row cast to the
  * activation dtype before the weight product (model_decision_transformer.py:

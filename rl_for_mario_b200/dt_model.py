@@ -180,48 +180,59 @@ class MarioStateEncoder(nn.Module):
         conv0, conv1, conv2, lin = self.cnn[0], self.cnn[2], self.cnn[4], self.cnn[7]
         dt = conv0.weight.dtype
         s = states.reshape(B * T, C, H, W)
-        # The reference divides by 255 when the frames' max exceeds 1 (:338).
-        # The test stays on the device (no host synchronisation) and the 1/255
-        # goes into the first convolution's weight instead of a pass over the
-        # frames.
-        use_blocks = (conv0.kernel_size == (8, 8) and conv0.stride == (4, 4) and conv0.padding == (0, 0)
-                      and H % 4 == 0 and W % 4 == 0 and s.is_cuda and s.dtype == torch.uint8
-                      and dt in (torch.bfloat16, torch.float16) and s.is_contiguous())
-        if use_blocks:
-            # The frame-block kernel also reports the largest byte.
-            fmax = torch.zeros(1, dtype=torch.int32, device=s.device)
-            xb = kernels.frames_to_blocks(s, dt, fmax)
-            big = fmax > 1
-        else:
-            big = (s.amax() > 1) if s.dtype == torch.uint8 else (s.to(dt).amax() > 1.0)
-        w0 = torch.where(big, conv0.weight / 255.0, conv0.weight)
         cl = torch.channels_last
-        k0, st0 = conv0.kernel_size[0], conv0.stride[0]
-        if (conv0.kernel_size == (k0, k0) and conv0.stride == (st0, st0) and conv0.padding == (0, 0)
-                and k0 % st0 == 0 and H % st0 == 0 and W % st0 == 0):
-            # Space-to-depth: a k x k stride-st convolution over C channels is a
-            # (k/st) x (k/st) stride-1 convolution over C*st*st channels of the
-            # frames cut into st x st blocks (same products, same sums).  With
-            # 4 x 8 x 8 / 4 that turns a 4-channel input, which has no
-            # tensor-core convolution, into a 64-channel one.  One pass writes
-            # the blocked frames in the compute dtype, channels-last.
-            f = st0
-            if use_blocks:
-                x = xb
-            else:
-                x = torch.empty((B * T, C * f * f, H // f, W // f), dtype=dt, device=s.device, memory_format=cl)
-                x.permute(0, 2, 3, 1).view(B * T, H // f, W // f, C, f, f).copy_(
-                    s.view(B * T, C, H // f, f, W // f, f).permute(0, 2, 4, 1, 3, 5))
-            kb = k0 // f
-            w0 = (w0.view(conv0.out_channels, C, kb, f, kb, f).permute(0, 1, 3, 5, 2, 4)
-                  .reshape(conv0.out_channels, C * f * f, kb, kb))
-            x = self._conv_relu(x, w0.contiguous(memory_format=cl), conv0.bias, (1, 1))
+        if (conv0.in_channels == 4 and conv0.out_channels == 32 and conv0.kernel_size == (8, 8)
+                and conv0.stride == (4, 4) and conv0.padding == (0, 0) and conv0.bias is not None
+                and s.is_cuda and s.dtype == torch.uint8 and dt in (torch.bfloat16, torch.float16)
+                and s.is_contiguous() and (H - 8) % 4 == 0 and (W - 8) % 4 == 0
+                and s.data_ptr() % 16 == 0 and s.numel() % 16 == 0):
+            # One tensor-core kernel from the uint8 frames: the reference's
+            # /255 when the max exceeds 1 (:338), the 8 x 8 stride-4
+            # convolution, bias and ReLU (device-side decision, no host sync).
+            x, _ = kernels.frames_conv1(s, conv0.weight, conv0.bias)
         else:
-            # One pass: frames -> compute dtype, channels-last (the layout the
-            # convolution kernels run in, so no layout conversions per layer).
-            x = torch.empty(s.shape, dtype=dt, device=s.device, memory_format=cl)
-            x.copy_(s)
-            x = self._conv_relu(x, w0.contiguous(memory_format=cl), conv0.bias, conv0.stride)
+            # The reference divides by 255 when the frames' max exceeds 1 (:338).
+            # The test stays on the device (no host synchronisation) and the 1/255
+            # goes into the first convolution's weight instead of a pass over the
+            # frames.
+            use_blocks = (conv0.kernel_size == (8, 8) and conv0.stride == (4, 4) and conv0.padding == (0, 0)
+                          and H % 4 == 0 and W % 4 == 0 and s.is_cuda and s.dtype == torch.uint8
+                          and dt in (torch.bfloat16, torch.float16) and s.is_contiguous())
+            if use_blocks:
+                # The frame-block kernel also reports the largest byte.
+                fmax = torch.zeros(1, dtype=torch.int32, device=s.device)
+                xb = kernels.frames_to_blocks(s, dt, fmax)
+                big = fmax > 1
+            else:
+                big = (s.amax() > 1) if s.dtype == torch.uint8 else (s.to(dt).amax() > 1.0)
+            w0 = torch.where(big, conv0.weight / 255.0, conv0.weight)
+            cl = torch.channels_last
+            k0, st0 = conv0.kernel_size[0], conv0.stride[0]
+            if (conv0.kernel_size == (k0, k0) and conv0.stride == (st0, st0) and conv0.padding == (0, 0)
+                    and k0 % st0 == 0 and H % st0 == 0 and W % st0 == 0):
+                # Space-to-depth: a k x k stride-st convolution over C channels is a
+                # (k/st) x (k/st) stride-1 convolution over C*st*st channels of the
+                # frames cut into st x st blocks (same products, same sums).  With
+                # 4 x 8 x 8 / 4 that turns a 4-channel input, which has no
+                # tensor-core convolution, into a 64-channel one.  One pass writes
+                # the blocked frames in the compute dtype, channels-last.
+                f = st0
+                if use_blocks:
+                    x = xb
+                else:
+                    x = torch.empty((B * T, C * f * f, H // f, W // f), dtype=dt, device=s.device, memory_format=cl)
+                    x.permute(0, 2, 3, 1).view(B * T, H // f, W // f, C, f, f).copy_(
+                        s.view(B * T, C, H // f, f, W // f, f).permute(0, 2, 4, 1, 3, 5))
+                kb = k0 // f
+                w0 = (w0.view(conv0.out_channels, C, kb, f, kb, f).permute(0, 1, 3, 5, 2, 4)
+                      .reshape(conv0.out_channels, C * f * f, kb, kb))
+                x = self._conv_relu(x, w0.contiguous(memory_format=cl), conv0.bias, (1, 1))
+            else:
+                # One pass: frames -> compute dtype, channels-last (the layout the
+                # convolution kernels run in, so no layout conversions per layer).
+                x = torch.empty(s.shape, dtype=dt, device=s.device, memory_format=cl)
+                x.copy_(s)
+                x = self._conv_relu(x, w0.contiguous(memory_format=cl), conv0.bias, conv0.stride)
         x = self._conv_relu(x, conv1.weight.contiguous(memory_format=cl), conv1.bias, conv1.stride)
         x = self._conv_relu(x, conv2.weight.contiguous(memory_format=cl), conv2.bias, conv2.stride)
         if x.dim() == 4 and x.is_contiguous(memory_format=cl):

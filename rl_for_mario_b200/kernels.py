@@ -270,6 +270,28 @@ def frames_to_blocks(frames: Tensor, dtype: torch.dtype, frame_max: Optional[Ten
     return out
 
 
+def frames_conv1(frames: Tensor, weight: Tensor, bias: Tensor) -> Tuple[Tensor, Tensor]:
+    """relu(conv2d(frames / 255 if max > 1 else frames, weight, bias, stride 4)) from
+    uint8 frames [N, 4, H, W] with an 8 x 8 weight [32, 4, 8, 8] (16-bit): returns the
+    output as a channels-last [N, 32, OH, OW] tensor of the weight's dtype and an
+    int32 [1] device tensor that is > 1 exactly when the frames' max exceeds 1."""
+    _require_cuda(frames, weight, bias)
+    if frames.dtype != torch.uint8 or frames.dim() != 4 or not frames.is_contiguous():
+        raise ValueError("frames must be a contiguous uint8 [N, C, H, W] tensor")
+    N, C, H, W = frames.shape
+    if tuple(weight.shape) != (32, C, 8, 8):
+        raise ValueError(f"weight must be [32, {C}, 8, 8]")
+    OH, OW = (H - 8) // 4 + 1, (W - 8) // 4 + 1
+    w2 = weight.reshape(32, C * 64).contiguous()
+    b = bias.float().contiguous()
+    out = torch.empty((N, 32, OH, OW), dtype=weight.dtype, device=frames.device, memory_format=torch.channels_last)
+    fmax = torch.empty(1, dtype=torch.int32, device=frames.device)
+    rc = _lib.load().dt_frames_conv1(_ptr(frames), N, C, H, W, _ptr(w2), _ptr(b), _ptr(fmax), _ptr(out),
+                                     _dtype_code(out), _stream_ptr(frames.device))
+    _lib.check("dt_frames_conv1", rc)
+    return out, fmax
+
+
 def rmsnorm(x: Tensor, weight: Tensor, eps: float, out: Optional[Tensor] = None) -> Tensor:
     """weight * cast(x * rsqrt(mean(x^2) + eps)) over the last dim (bf16 / fp16)."""
     _require_cuda(x, weight, out)

@@ -115,3 +115,44 @@ def test_rmsnorm_module_unaligned_view_uses_reference_formula():
     xf = x.float()
     ref = norm.weight * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + norm.eps)).to(torch.bfloat16)
     assert torch.equal(y, ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N,H,W,hi", [(1, 84, 84, 255), (37, 84, 84, 255), (3, 12, 20, 255), (5, 84, 84, 1)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_frames_conv1_matches_reference(N, H, W, hi, dtype):
+    """relu(conv2d(frames / 255 when their max exceeds 1, w, b, stride 4)) from uint8 frames in one kernel."""
+    import torch.nn.functional as Fn
+    from rl_for_mario_b200.kernels import device_status, frames_conv1
+
+    g = torch.Generator().manual_seed(N * 3 + H + hi)
+    fr = torch.randint(0, hi + 1, (N, 4, H, W), generator=g, dtype=torch.uint8)
+    w = (torch.randn(32, 4, 8, 8, generator=g) * 0.05).to(dtype)
+    b = (torch.randn(32, generator=g) * 0.1).to(dtype)
+    out, fmax = frames_conv1(fr.cuda(), w.cuda(), b.cuda())
+    assert device_status() == 0
+    assert (int(fmax.item()) > 1) == (int(fr.max()) > 1)
+    x = fr.float() / 255.0 if int(fr.max()) > 1 else fr.float()
+    ref = Fn.relu(Fn.conv2d(x, w.float(), b.float(), stride=4))
+    assert out.shape == ref.shape and out.is_contiguous(memory_format=torch.channels_last)
+    err = (out.float().cpu() - ref).abs()
+    tol = 1e-2 if dtype == torch.bfloat16 else 2e-3
+    assert (err <= tol * (1 + ref.abs())).all(), err.max().item()
+
+
+@pytest.mark.gpu
+def test_frames_conv1_scale_from_a_single_byte():
+    """Frames of 0 / 1 with one byte of 2 in the last frame still take the 1/255 scale."""
+    import torch.nn.functional as Fn
+    from rl_for_mario_b200.kernels import frames_conv1
+
+    g = torch.Generator().manual_seed(11)
+    fr = torch.randint(0, 2, (50, 4, 84, 84), generator=g, dtype=torch.uint8)
+    fr[-1, 3, 83, 83] = 2
+    w = (torch.randn(32, 4, 8, 8, generator=g) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(32, generator=g) * 0.1).to(torch.bfloat16)
+    out, fmax = frames_conv1(fr.cuda(), w.cuda(), b.cuda())
+    assert int(fmax.item()) > 1
+    ref = Fn.relu(Fn.conv2d(fr.float() / 255.0, w.float(), b.float(), stride=4))
+    err = (out.float().cpu() - ref).abs()
+    assert (err <= 1e-2 * (1 + ref.abs())).all(), err.max().item()
