@@ -315,7 +315,7 @@ def run_ours(args):
             line["prefill_long"] = bench_prefill_cfg4(dev, peaks)
             line["prefill_long"]["rmsnorm_qkv_kernel"] = bench_rmsnorm_qkv_cfg4(dev, peaks)
             line["prefill_long"]["rmsnorm_swiglu_kernel"] = bench_rmsnorm_swiglu_cfg4(dev, peaks)
-            line["prefill_long"]["frames_kernel"] = bench_frames_cfg4(dev, peaks)
+            line["prefill_long"]["encoder_conv1_kernel"] = bench_conv1_cfg4(dev, peaks)
         line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
@@ -615,35 +615,38 @@ def bench_rmsnorm_swiglu_cfg4(dev, peaks, batch=None):
                          "peak_source": peaks["source"]}}
 
 
-def bench_frames_cfg4(dev, peaks, batch=None):
-    """The state encoder's input kernel at cfg4's shape: batch x 256 frame stacks of
-    4 x 84 x 84 uint8 -> bf16 4x4 space-to-depth blocks (and the frames' maximum)."""
-    from rl_for_mario_b200.kernels import device_status, frames_to_blocks
+def bench_conv1_cfg4(dev, peaks, batch=None):
+    """The state encoder's first layer at cfg4's shape: batch x 256 frame stacks of
+    4 x 84 x 84 uint8 -> relu(conv 8x8/4 + bias) with the /255 test, one kernel
+    (dt_frames_conv1) plus its early-exit frame-max pre-pass."""
+    from rl_for_mario_b200.kernels import device_status, frames_conv1
 
     C = PREFILL_LONG_CFG
     n = (batch or C["batch"]) * C["timesteps"]
     g = torch.Generator(device=dev).manual_seed(7)
     fr = torch.randint(0, 256, (n, 4, 84, 84), device=dev, generator=g, dtype=torch.uint8)
-    fm = torch.zeros(1, dtype=torch.int32, device=dev)
+    w = (torch.randn(32, 4, 8, 8, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(32, device=dev, generator=g) * 0.1).to(torch.bfloat16)
     for _ in range(3):
-        out = frames_to_blocks(fr, torch.bfloat16, fm)
+        out, _ = frames_conv1(fr, w, b)
     del out
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 5
     e0.record()
     for _ in range(reps):
-        out = frames_to_blocks(fr, torch.bfloat16, fm)
+        out, _ = frames_conv1(fr, w, b)
     e1.record()
     torch.cuda.synchronize()
     if device_status() != 0:
-        raise SystemExit("device status error in the frame-block benchmark")
+        raise SystemExit("device status error in the first-layer benchmark")
     ms = e0.elapsed_time(e1) / reps
-    byts = fr.numel() * 3  # uint8 in, bf16 out
+    byts = fr.numel() + out.numel() * 2  # uint8 frames in, bf16 activations out
+    flops = 2 * n * 400 * 32 * 256
     gbs = byts / (ms * 1e-3) / 1e9
     del fr, out
     torch.cuda.empty_cache()
-    return {"kernel": "frame_cta_to_blocks_kernel", "frames": n, "ms": ms,
+    return {"kernel": "frames_conv1_kernel", "frames": n, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": byts,
                          "peak_source": peaks["source"]}}
@@ -723,7 +726,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / rollout sub-benchmarks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
-    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "frames"],
+    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "conv1"],
                     default=None,
                     help="run one sub-benchmark alone and print its JSON (profiling)")
     ap.add_argument("--long-batch", type=int, default=None,
@@ -739,8 +742,8 @@ def main():
             emit({"only": "decode", **bench_decode_cfg3(dev, _peaks())})
         elif args.only == "rmsnorm_qkv":
             emit({"only": "rmsnorm_qkv", **bench_rmsnorm_qkv_cfg4(dev, _peaks(), batch=args.long_batch)})
-        elif args.only == "frames":
-            emit({"only": "frames", **bench_frames_cfg4(dev, _peaks(), batch=args.long_batch)})
+        elif args.only == "conv1":
+            emit({"only": "conv1", **bench_conv1_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "rmsnorm_swiglu":
             emit({"only": "rmsnorm_swiglu", **bench_rmsnorm_swiglu_cfg4(dev, _peaks(), batch=args.long_batch)})
         else:
