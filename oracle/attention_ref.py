@@ -157,3 +157,34 @@ def attention_module_ref(x: Tensor, wq: Tensor, wk: Tensor, wv: Tensor, wo: Tens
         past = (kc, vc) if use_cache else None
     out = out.reshape(B, S, n_heads * D) @ wo.float().t()
     return out, past
+
+
+class ReferenceAttention(torch.nn.Module):
+    """DecisionTransformerAttention (reference :137-249) as a module with the
+    reference's parameter names and forward contract, evaluated by
+    ``attention_module_ref`` in float32 on the inputs' device.  Lets a test
+    build a model whose attention is the reference's and then swap it for the
+    drop-in replacement."""
+
+    def __init__(self, config):
+        super().__init__()
+        nh = config.num_attention_heads
+        nkv = nh if config.num_key_value_heads is None else config.num_key_value_heads
+        if nh % nkv:
+            raise ValueError("num_attention_heads must be divisible by num_key_value_heads")
+        self.n_local_heads, self.n_local_kv_heads = nh, nkv
+        self.head_dim = config.hidden_size // nh
+        H = config.hidden_size
+        self.q_proj = torch.nn.Linear(H, nh * self.head_dim, bias=False)
+        self.k_proj = torch.nn.Linear(H, nkv * self.head_dim, bias=False)
+        self.v_proj = torch.nn.Linear(H, nkv * self.head_dim, bias=False)
+        self.o_proj = torch.nn.Linear(nh * self.head_dim, H, bias=False)
+
+    def forward(self, x, position_embeddings, past_key_value=None, use_cache=False, attention_mask=None):
+        cos, sin = position_embeddings
+        out, past = attention_module_ref(x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight,
+                                         self.o_proj.weight, self.n_local_heads, self.n_local_kv_heads,
+                                         cos.float(), sin.float(), past_key_value, use_cache, attention_mask)
+        if past is not None:
+            past = (past[0].to(x.dtype), past[1].to(x.dtype))
+        return out.to(x.dtype), past

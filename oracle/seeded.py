@@ -54,3 +54,22 @@ def checksum(t: torch.Tensor) -> float:
     a = t.detach().double().reshape(-1)
     w = torch.arange(1, a.numel() + 1, dtype=torch.float64)
     return float((a * (1.0 + (w % 97) / 97.0)).sum())
+
+
+def dt_synthetic_inputs(tag: str, seed: int, B: int, T: int, state_shape, act_dim: int,
+                        pad_max: int = -1):
+    """Seeded DT inputs with the shapes and distributions of the repo-default
+    workload: uint8 frames U[0, 255], actions U{0..act_dim-1}, returns-to-go
+    U[0, 3000], timesteps start + arange(T) with start U{0..3999}, and (when
+    pad_max >= 0) left padding U{0..pad_max} timesteps per sample with the
+    matching [B, T] attention mask (1 = valid).  Returns a dict of CPU tensors."""
+    states = seeded_uniform_int((B, T, *state_shape), 0, 256, seed, tag + ":states").to(torch.uint8)
+    actions = seeded_uniform_int((B, T), 0, act_dim, seed, tag + ":actions")
+    rtg = seeded_uniform((B, T), 0.0, 3000.0, seed, tag + ":rtg")
+    start = seeded_uniform_int((B, 1), 0, 4000, seed, tag + ":start")
+    out = {"states": states, "actions": actions, "rtg": rtg, "timesteps": start + torch.arange(T)[None]}
+    if pad_max >= 0:
+        pads = seeded_uniform_int((B,), 0, pad_max + 1, seed, tag + ":pads")
+        out["pad_steps"] = pads
+        out["mask"] = (torch.arange(T)[None] >= pads[:, None]).long()
+    return out

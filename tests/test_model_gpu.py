@@ -161,17 +161,31 @@ def test_dt_cached_step_matches_reference():
     assert cache.length == 3 * (T + 1)
 
 
+def _argmax_where_decided(out, ref, tol):
+    """Argmax agreement on the rows whose reference top-2 gap exceeds 2 * tol (a
+    logit error below tol cannot flip those); returns (agreeing, decided rows)."""
+    top2 = ref.topk(2, dim=-1).values
+    decided = (top2[..., 0] - top2[..., 1]) > 2 * tol
+    same = out.argmax(-1) == ref.argmax(-1)
+    return int((same & decided).sum()), int(decided.sum())
+
+
 @pytest.mark.gpu
 def test_dt_bf16_model_argmax_agreement():
-    """Whole model in bf16: logits within 5e-2 of the fp32 reference and identical argmax."""
+    """Whole model in bf16: logits within 5e-2 of the fp32 reference, and the same
+    argmax on every row the 5e-2 bound decides (13 of the 14 rows; the 14th has a
+    top-2 gap of 4e-3).  The 4,096-row agreement rates are in test_dt_parity_gpu."""
     g, model, states, actions, rtg, ts = _dt(torch.bfloat16)
     T = int(g["T"])
     mask = (torch.arange(T)[None] >= torch.from_numpy(g["pad_steps"]).long()[:, None]).long().cuda()
     with torch.no_grad():
         out = model(states[:, :T], actions[:, :T], rtg[:, :T], ts[:, :T], attention_mask=mask)
     ref = torch.from_numpy(g["logits"])
-    err = (out.action_logits.float().cpu() - ref).abs().max().item()
+    lo = out.action_logits.float().cpu()
+    err = (lo - ref).abs().max().item()
     assert err < 5e-2, f"bf16 model logits max abs err {err:.3e}"
+    same, decided = _argmax_where_decided(lo, ref, 5e-2)
+    assert decided >= 13 and same == decided, (same, decided)
 
 
 @pytest.mark.gpu

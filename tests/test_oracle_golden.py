@@ -159,3 +159,25 @@ def test_oracle_catches_a_planted_mask_error():
     w = [sd[k] for k in ("q_proj.weight", "k_proj.weight", "v_proj.weight", "o_proj.weight")]
     out, _ = attention_module_ref(x, *w, nh, nkv, cos, sin, attention_mask=None)  # planted: mask dropped
     assert np.abs(out.numpy() - g["out"]).max() > 1e-2
+
+
+@pytest.mark.parametrize("name,samples", [("dt_cfg1", [0, 17, 63]), ("dt_cfg4", [2]), ("dt_rollout", [0, 15])])
+def test_dt_workload_goldens_pin_the_oracle(name, samples):
+    """The oracle's DT forward equals the reference's fp32 logits at the workload
+    shapes (cfg1: 4/256/8x2, cfg4: 12/768/12x4 at 768 tokens, the 252-token
+    rollout trajectory) on a few samples of each fixture (the CPU suite stays fast;
+    samples are independent, so a slice of the batch is the same computation)."""
+    from oracle.seeded import dt_synthetic_inputs
+
+    g = load(name)
+    cfgd = {k[4:]: (tuple(v.tolist()) if v.ndim else v.item()) for k, v in g.items() if k.startswith("cfg_")}
+    sd = seeded_state_dict(dt_param_shapes(cfgd), int(g["seed"]))
+    assert sum(checksum(sd[k]) for k in sorted(sd)) == pytest.approx(float(g["w_checksum"]), rel=1e-12)
+    inp = dt_synthetic_inputs(name, int(g["seed"]), int(g["B"]), int(g["T"]), cfgd["state_shape"], cfgd["act_dim"],
+                              int(g["pad_max"]))
+    sel = torch.tensor(samples)
+    mask = inp["mask"][sel] if "mask" in inp else None
+    logits, values, _, _ = dt_forward_ref(sd, cfgd, inp["states"][sel], inp["actions"][sel], inp["rtg"][sel],
+                                          inp["timesteps"][sel], mask)
+    np.testing.assert_allclose(logits.numpy(), g["logits"][samples], atol=ATOL, rtol=1e-5)
+    np.testing.assert_allclose(values.numpy(), g["values"][samples], atol=ATOL, rtol=1e-5)
