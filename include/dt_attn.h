@@ -150,19 +150,6 @@ int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, 
                       int M, int K, int N, float eps, int dtype, void* stream);
 
 /*
- * State-encoder input: uint8 frame stacks [N, C, H, W] -> 16-bit 4 x 4
- * space-to-depth blocks, channels-last [N, H/4, W/4, C*16] with channel
- * c*16 + dy*4 + dx = frames[n, c, 4Y + dy, 4X + dx] (values 0..255, exact).
- * With the first convolution's weight regrouped the same way (and scaled by
- * 1/255), the reference's frames / 255 -> Conv2d(C, 32, 8, stride 4)
- * (model_decision_transformer.py:315-341, division at :338) becomes a 2 x 2
- * stride-1 convolution over C*16 channels.  frame_max (nullable, device):
- * raised by atomicMax to the largest byte read (the reference's x.max() > 1
- * test, :338, without a separate pass).  H, W multiples of 4; frames 4-byte
- * aligned, out 16-byte aligned; bf16 or fp16 output.
- */
-
-/*
  * The state encoder's first layer from the uint8 frames: frames / 255 (when
  * their maximum exceeds 1, model_decision_transformer.py:338), Conv2d(4, 32,
  * 8, stride 4) and ReLU (:315-341), as one implicit GEMM on the tensor cores.
@@ -171,6 +158,12 @@ int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, 
  * (unscaled); bias [32] fp32; y [N, OH, OW, 32] 16-bit (channels-last, OH =
  * (H - 8) / 4 + 1); frame_max (device) ends > 1 exactly when some byte of the
  * frames exceeds 1 (the reference's test; the scan stops at the first such byte).
+ * Rounding: the pixels enter the MMA as exact 16-bit integers, the 1/255 is
+ * applied to the fp32 accumulator and the output is rounded once.  The
+ * reference's 16-bit model rounds frames / 255 to its dtype before the
+ * convolution; this kernel does not (it is the fp32 convolution of frames / 255
+ * to within one output rounding), so its outputs differ from the reference's
+ * 16-bit ones by that input rounding.
  */
 int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int W, const void* w, const float* bias,
                     unsigned int* frame_max, void* y, int dtype, void* stream);
@@ -185,6 +178,19 @@ int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int W, const vo
  */
 int dt_rmsnorm(const void* x, int64_t x_row_stride, const void* w, void* y, int64_t y_row_stride, int M, int K,
                float eps, int dtype, void* stream);
+
+/*
+ * State-encoder input: uint8 frame stacks [N, C, H, W] -> 16-bit 4 x 4
+ * space-to-depth blocks, channels-last [N, H/4, W/4, C*16] with channel
+ * c*16 + dy*4 + dx = frames[n, c, 4Y + dy, 4X + dx] (values 0..255, exact).
+ * With the first convolution's weight regrouped the same way (and scaled by
+ * 1/255), the reference's frames / 255 -> Conv2d(C, 32, 8, stride 4)
+ * (model_decision_transformer.py:315-341, division at :338) becomes a 2 x 2
+ * stride-1 convolution over C*16 channels.  frame_max (nullable, device):
+ * raised by atomicMax to the largest byte read (the reference's x.max() > 1
+ * test, :338, without a separate pass).  H, W multiples of 4; frames 4-byte
+ * aligned, out 16-byte aligned; bf16 or fp16 output.
+ */
 int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int C, int H, int W, unsigned int* frame_max,
                         int dtype, void* stream);
 

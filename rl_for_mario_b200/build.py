@@ -11,6 +11,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
@@ -63,20 +64,25 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     obj_dir = OUT_DIR / "obj"
     obj_dir.mkdir(exist_ok=True)
     nvcc = _nvcc()
-    objs = []
-    for src in sources():
+
+    def compile_one(src: Path):
         obj = obj_dir / (src.stem + ".o")
         cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE_DIR}", "-c", str(src), "-o", str(obj)]
         if ptxas_info:
             cmd.insert(1, "-Xptxas=-v")
-        if verbose:
-            print(" ".join(cmd), flush=True)
-        res = subprocess.run(cmd, capture_output=True, text=True)
-        if res.returncode != 0:
-            raise RuntimeError(f"nvcc failed on {src.name}:\n{res.stdout}\n{res.stderr}")
-        if verbose or ptxas_info:
-            sys.stdout.write(res.stdout + res.stderr)
-        objs.append(str(obj))
+        return src, obj, cmd, subprocess.run(cmd, capture_output=True, text=True)
+
+    objs = []
+    # Translation units compile independently: one nvcc process per source.
+    with ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as pool:
+        for src, obj, cmd, res in pool.map(compile_one, sources()):
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            if res.returncode != 0:
+                raise RuntimeError(f"nvcc failed on {src.name}:\n{res.stdout}\n{res.stderr}")
+            if verbose or ptxas_info:
+                sys.stdout.write(res.stdout + res.stderr)
+            objs.append(str(obj))
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-Xcompiler", "-fPIC", *objs, "-o", str(tmp)]
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -266,7 +266,7 @@ cudaError_t launch_frames_conv1_sm100(const void* frames, long long N, int H, in
   const long long ntiles = (total + 127) / 128;
   const unsigned grid = (unsigned)(ntiles < num_sms ? ntiles : num_sms);
   auto kfn = bf16 ? frames_conv1_kernel<true> : frames_conv1_kernel<false>;
-  e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C1Shape::SMEM);
+  e = smem_limit_once(reinterpret_cast<const void*>(kfn), C1Shape::SMEM);
   if (e != cudaSuccess) return e;
   kfn<<<grid, kC1Threads, C1Shape::SMEM, st>>>(static_cast<const uint8_t*>(frames), static_cast<const uint16_t*>(w),
                                                 bias, frame_max, static_cast<uint16_t*>(y), total, H, W, OH, OW,

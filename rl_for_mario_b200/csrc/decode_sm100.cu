@@ -631,7 +631,7 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const __grid_con
 cudaError_t launch_decode_sm100(const DecodeParams& prm, const CUtensorMap& kmap, const CUtensorMap& vmap, int D,
                                 bool bf16, int grid, cudaStream_t stream) {
   auto go = [&](auto kfn, int smem) -> cudaError_t {
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = smem_limit_once(reinterpret_cast<const void*>(kfn), smem);
     if (e != cudaSuccess) return e;
     kfn<<<grid, kDecThreads, smem, stream>>>(kmap, vmap, prm);
     return cudaGetLastError();

@@ -5,7 +5,32 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 namespace dtk {
+
+// Raises a kernel's dynamic shared-memory limit on the current device once:
+// the attribute stays set in the device's context, and the launch paths are
+// host-bound (the rollout enqueues dozens of launches per step), so later
+// launches skip the driver call.  Thread-safe; one record per (kernel, device).
+inline cudaError_t smem_limit_once(const void* func, int bytes) {
+  struct Done {
+    const void* f;
+    int dev, bytes;
+  };
+  static std::mutex mu;
+  static Done done[256];
+  static int n = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < n; ++i)
+    if (done[i].f == func && done[i].dev == dev && done[i].bytes >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && n < 256) done[n++] = Done{func, dev, bytes};
+  return e;
+}
 
 // Kernel parameters of the fused prefill (everything except the TMA maps).
 struct PrefillParams {

@@ -629,7 +629,7 @@ static cudaError_t launch_long(const CUtensorMap& q, const CUtensorMap& k, const
                                const PrefillParams& prm, int n_units, int grid, cudaStream_t st) {
   using SH = LongShape<D>;
   auto kern = dt_prefill_long_kernel<D, BF16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SH::SMEM);
+  cudaError_t e = smem_limit_once(reinterpret_cast<const void*>(kern), SH::SMEM);
   if (e != cudaSuccess) return e;
   kern<<<grid, kLongThreads, SH::SMEM, st>>>(q, k, v, prm, n_units);
   return cudaGetLastError();

@@ -546,7 +546,7 @@ cudaError_t launch_prefill_short_sm100(const CUtensorMap& q, const CUtensorMap& 
                                        cudaStream_t stream) {
   if ((n_units + grid - 1) / grid > SS::MAX_UNITS) return cudaErrorInvalidValue;
   auto kfn = bf16 ? dt_prefill_short_kernel<true> : dt_prefill_short_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, SS::SMEM_BYTES);
+  cudaError_t e = smem_limit_once(reinterpret_cast<const void*>(kfn), SS::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   kfn<<<grid, SS::NTHREADS, SS::SMEM_BYTES, stream>>>(q, k, v, prm, n_units);
   return cudaGetLastError();

@@ -370,8 +370,7 @@ static cudaError_t launch_t(const CUtensorMap& q, const CUtensorMap& k, const CU
                             const PrefillParams& prm, int grid, cudaStream_t stream) {
   using SH = PrefillShape<D>;
   auto kfn = dt_prefill_kernel<D, BF16>;
-  // The attribute is per device; set it on every launch (cheap host call).
-  cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, SH::SMEM_BYTES);
+  cudaError_t e = smem_limit_once(reinterpret_cast<const void*>(kfn), SH::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   kfn<<<grid, 256, SH::SMEM_BYTES, stream>>>(q, k, v, prm);
   return cudaGetLastError();

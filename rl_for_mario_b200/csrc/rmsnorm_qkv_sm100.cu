@@ -654,7 +654,7 @@ template <int NCTA>
 static cudaError_t launch_rq(const CUtensorMap& x, const CUtensorMap& w, const RmsQkvParams& p, cudaStream_t st) {
   using SH = GemmShape<NCTA>;
   auto k = dt_rmsnorm_qkv_kernel<NCTA>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SH::SMEM);
+  cudaError_t e = smem_limit_once(reinterpret_cast<const void*>(k), SH::SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid((p.M + 127) / 128, (p.N + NCTA - 1) / NCTA);
   k<<<grid, kGemmThreads, SH::SMEM, st>>>(x, w, p);
@@ -675,7 +675,7 @@ cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w,
                                      const RmsQkvParams& p, int ncta, int num_sms, cudaStream_t st) {
   if (ncta == 0) {
     auto k = dt_rmsnorm_qkv_persist_kernel;
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PShape::SMEM);
+    cudaError_t e = smem_limit_once(reinterpret_cast<const void*>(k), PShape::SMEM);
     if (e != cudaSuccess) return e;
     const int nrb = (p.M + 127) / 128;
     const int grid = nrb < num_sms ? nrb : num_sms;

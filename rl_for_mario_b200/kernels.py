@@ -126,6 +126,12 @@ def attn_prefill_host(hq: Tensor, hk: Tensor, hv: Tensor, cos: Optional[Tensor],
     _require_cuda(dq, dk, dv, dpad, dout)
     if (hpad is None) != (dpad is None):
         raise ValueError("hpad and the device pad_len buffer go together")
+    # Tensor.copy_ would silently cast or broadcast: host and device buffers
+    # must match exactly.
+    for name, h, d in (("q", hq, dq), ("k", hk, dk), ("v", hv, dv), ("out", hout, dout), ("pad_len", hpad, dpad)):
+        if h is not None and (h.dtype != d.dtype or h.shape != d.shape):
+            raise ValueError(f"host {name} {tuple(h.shape)} {h.dtype} does not match its device buffer "
+                             f"{tuple(d.shape)} {d.dtype}")
     B = hq.shape[0]
     chunks = max(1, min(int(chunks), B))
     bounds = [B * i // chunks for i in range(chunks + 1)]

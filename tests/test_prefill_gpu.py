@@ -208,3 +208,22 @@ def test_prefill_host_rejects_pageable_buffers():
     bufs = tuple(torch.zeros(2, 8, 2, 32, dtype=torch.bfloat16, device="cuda") for _ in range(3))
     with pytest.raises(ValueError):
         attn_prefill_host(t, t, t, None, None, None, t.pin_memory(), bufs + (None, bufs[0]), apply_rope=False)
+
+
+@pytest.mark.gpu
+def test_prefill_host_rejects_mismatched_buffers():
+    """A host tensor whose dtype or batch differs from its device buffer is an error
+    (a copy would cast or fill only part of the buffer)."""
+    from rl_for_mario_b200.kernels import attn_prefill_host
+
+    dev = tuple(torch.zeros(2, 8, 2, 32, dtype=torch.bfloat16, device="cuda") for _ in range(4))
+    bufs = dev[:3] + (None, dev[3])
+    ok = torch.zeros(2, 8, 2, 32, dtype=torch.bfloat16).pin_memory()
+    f32 = torch.zeros(2, 8, 2, 32, dtype=torch.float32).pin_memory()
+    short = torch.zeros(1, 8, 2, 32, dtype=torch.bfloat16).pin_memory()
+    with pytest.raises(ValueError):
+        attn_prefill_host(f32, ok, ok, None, None, None, ok, bufs, apply_rope=False)
+    with pytest.raises(ValueError):
+        attn_prefill_host(ok, ok, short, None, None, None, ok, bufs, apply_rope=False)
+    attn_prefill_host(ok, ok, ok, None, None, None, ok, bufs, apply_rope=False)
+    torch.cuda.synchronize()
