@@ -169,6 +169,25 @@ int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int W, const vo
                     unsigned int* frame_max, void* y, int dtype, void* stream);
 
 /*
+ * dt_frames_conv1 for callers that cannot allocate device memory.  No
+ * counterpart in the reference: it exists for callers such as an environment
+ * host written in C or C++ that hands the library frames it already holds on
+ * the GPU and owns no allocator, or a process whose memory pool has reserved
+ * the device's memory, where a cudaMalloc would fail or stall the step loop.
+ * Same arguments and result as dt_frames_conv1 without frame_max: the
+ * frame-maximum word lives in a 256-byte static device array of the library
+ * (held on every GPU that loads it, until exit).  A call needs one word of it
+ * whatever the frame count, and is rejected with DT_ERR_INVALID if the array
+ * cannot hold that.  The call allocates nothing (no cudaMalloc, cudaFree or
+ * allocating library routine).  Its first call on a device looks up the
+ * array's device address there; make that first call before any stream
+ * capture.  Every call shares the array (each clears its word first), so
+ * calls whose work overlaps on the GPU, on different streams, race.
+ */
+int dt_frames_conv1_noalloc(const void* frames, int64_t N, int C, int H, int W, const void* w, const float* bias,
+                            void* y, int dtype, void* stream);
+
+/*
  * RMSNorm with the reference's rounding: y = w * cast(x * rsqrt(mean(x^2) +
  * eps)) with the mean and rsqrt in fp32, the normalised row cast to the
  * activation dtype before the weight product (model_decision_transformer.py:

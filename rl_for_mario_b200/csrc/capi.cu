@@ -501,6 +501,36 @@ extern "C" int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int 
   return DT_OK;
 }
 
+extern "C" int dt_frames_conv1_noalloc(const void* frames, int64_t N, int C, int H, int W, const void* w,
+                                       const float* bias, void* y, int dtype, void* stream) {
+  const char* fn = "dt_frames_conv1_noalloc";
+  if (!frames || !w || !bias || !y) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
+  if (C != 4) return fail(DT_ERR_UNSUPPORTED, "%s: %d input channels (the kernel takes 4)", fn, C);
+  if (N < 1 || H < 8 || W < 8 || (H - 8) % 4 || (W - 8) % 4)
+    return fail(DT_ERR_INVALID, "%s: N >= 1 and H, W = 8 + 4 k required", fn);
+  if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
+    return fail(DT_ERR_UNSUPPORTED, "%s: dtype %d not supported (bf16 / fp16)", fn, dtype);
+  if (!aligned16(frames) || (N * (int64_t)C * H * W) % 16 || !aligned16(w) || !aligned16(y) ||
+      (reinterpret_cast<uintptr_t>(bias) & 3))
+    return fail(DT_ERR_INVALID, "%s: frames, w and y 16-byte aligned, frame bytes a multiple of 16", fn);
+  // The static scratch must hold what this call needs (one word, whatever N).
+  if (dtk::kConv1NoallocWordsPerCall > dtk::kConv1NoallocScratchWords)
+    return fail(DT_ERR_INVALID, "%s: needs %d scratch words, the static array holds %d", fn,
+                dtk::kConv1NoallocWordsPerCall, dtk::kConv1NoallocScratchWords);
+  int dev = 0;
+  int* status = nullptr;
+  int rc = device_setup(&dev, &status);
+  if (rc) return rc;
+  if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
+  unsigned int* scratch = nullptr;
+  cudaError_t e = dtk::conv1_noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s: scratch address: %s", fn, cudaGetErrorString(e));
+  e = dtk::launch_frames_conv1_sm100(frames, N, H, W, w, bias, scratch, y, dtype == DT_DTYPE_BF16, g_num_sms[dev],
+                                     status, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
+  return DT_OK;
+}
+
 extern "C" int dt_rmsnorm(const void* x, int64_t x_row_stride, const void* w, void* y, int64_t y_row_stride, int M,
                           int K, float eps, int dtype, void* stream) {
   const char* fn = "dt_rmsnorm";

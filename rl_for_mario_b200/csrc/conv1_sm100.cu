@@ -23,6 +23,8 @@
 // The pixel values 0..255 are exact in bf16 / fp16; the 1/255 is applied to
 // the fp32 accumulator.  Whether it applies (some byte > 1) is decided by a
 // first kernel that stops reading as soon as any thread has seen such a byte.
+#include <mutex>
+
 #include "dt_common.cuh"
 #include "dt_internal.h"
 
@@ -272,6 +274,35 @@ cudaError_t launch_frames_conv1_sm100(const void* frames, long long N, int H, in
                                                 bias, frame_max, static_cast<uint16_t*>(y), total, H, W, OH, OW,
                                                 status);
   return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Scratch of the allocation-free entry point (dt_frames_conv1_noalloc): the
+// frame-maximum word lives in this file-scope array instead of a buffer the
+// caller allocates.  Host code must not pass the array's name to a kernel (on
+// the host it names a shadow, not device memory); it passes the device address
+// that conv1_noalloc_scratch() looked up for the current device.  Every call
+// shares the array and the launch clears the word first; calls whose work
+// overlaps on the GPU race on it.
+static __device__ __align__(256) unsigned int g_conv1_noalloc_scratch[kConv1NoallocScratchWords];
+
+cudaError_t conv1_noalloc_scratch(unsigned int** out) {
+  constexpr int kMaxDev = 64;
+  static std::mutex mu;
+  static unsigned int* ptr[kMaxDev] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDev) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_conv1_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    ptr[dev] = static_cast<unsigned int*>(p);
+  }
+  *out = ptr[dev];
+  return cudaSuccess;
 }
 
 }  // namespace dtk

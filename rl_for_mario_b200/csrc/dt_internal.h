@@ -140,6 +140,18 @@ struct RmsQkvParams {
 int rmsnorm_qkv_ncta(int N);
 constexpr int kPersistKChunk = 64;  // K elements per stage of the persistent RMSNorm GEMM (x / W box width)
 
+// Static scratch of dt_frames_conv1_noalloc: 64 32-bit words (256 bytes) of
+// device memory that every GPU loading the library holds until exit.  A call
+// uses kConv1NoallocWordsPerCall of them (the frame-maximum word), whatever
+// its frame count.
+constexpr int kConv1NoallocScratchWords = 64;
+constexpr int kConv1NoallocWordsPerCall = 1;
+
+// Device address of that array on the current device, looked up once per
+// device (cudaGetSymbolAddress with the device current) and cached.
+cudaError_t conv1_noalloc_scratch(unsigned int** out);
+
+
 cudaError_t launch_frames_to_blocks_sm100(const void* frames, void* out, long long N, int C, int H, int W, bool bf16,
                                           unsigned int* frame_max, cudaStream_t st);
 cudaError_t launch_frames_conv1_sm100(const void* frames, long long N, int H, int W, const void* w,
