@@ -653,7 +653,13 @@ def bench_conv1_cfg4(dev, peaks, batch=None):
 
 
 def bench_rollout_cfg5(dev, world, rank, pg):
-    """8,192 environments per GPU, 64 cached steps, CNN on synthetic frames, all-gather of logits."""
+    """8,192 environments per GPU, 64 cached steps, CNN on synthetic frames, all-gather of logits.
+
+    Each step draws the environments' uint8 frames on the device from the seed
+    (written straight into the rollout's frame buffer, as a GPU environment
+    would), runs the policy step (one CUDA graph per step index after the
+    first two episodes) and all-gathers the logits.  Reported: device time of
+    the 64-step episode (max over ranks) and the host time to enqueue it."""
     from rl_for_mario_b200.dt_model import DTConfig, MarioDT
     from rl_for_mario_b200.rollout import DTRollout
 
@@ -664,9 +670,9 @@ def bench_rollout_cfg5(dev, world, rank, pg):
     model = MarioDT(cfg).to(dev, torch.bfloat16).eval().fuse_norms()  # fused blocks
     b = C["envs_per_gpu"]
     B = b * world
-    ro = DTRollout(model, num_envs=B, max_steps=C["steps"], page_size=64, device=dev)
+    ro = DTRollout(model, num_envs=B, max_steps=C["steps"], page_size=64, device=dev, graphs=True)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
-    frames = torch.randint(0, 256, (4, b, 4, 84, 84), device=dev, generator=g, dtype=torch.uint8)
+    first = torch.empty((b, 4, 84, 84), dtype=torch.uint8, device=dev)
     rtg = torch.rand(C["steps"], b, device=dev, generator=g) * 3000
     ts0 = torch.randint(0, 4000 - C["steps"], (b,), device=dev, generator=g)
 
@@ -674,29 +680,39 @@ def bench_rollout_cfg5(dev, world, rank, pg):
         ro.reset()
         a = None
         for t in range(C["steps"]):
-            a, _ = ro.step(frames[t % 4], rtg[t], ts0 + t)
+            fb = ro.frame_buffer if ro.frame_buffer is not None else first
+            fb.random_(0, 256, generator=g)  # the environments' observation of step t
+            a, _ = ro.step(fb, rtg[t], ts0 + t)
         return a
 
-    run()  # warm-up
+    run()  # eager episode (initialises kernels and libraries)
+    run()  # captures one graph per step index
+    run()  # warm replay
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0 = time.perf_counter()
     e0.record()
     run()
     e1.record()
+    host_ms = (time.perf_counter() - h0) * 1e3
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     if pg:
-        t = torch.tensor([ms], device=dev)
+        t = torch.tensor([ms, host_ms], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, host_ms = float(t[0].item()), float(t[1].item())
     res = {"metric": "sharded rollout env-steps/s (CNN + 4 layers + cached attention + all-gather)",
-           "unit": "env-steps/s", "value": B * C["steps"] / (ms * 1e-3), "ms_total": ms, "n_gpus": world,
-           "scaling": "weak",
+           "unit": "env-steps/s", "value": B * C["steps"] / (ms * 1e-3), "ms_total": ms, "gpu_ms": ms,
+           "host_enqueue_ms": host_ms, "n_gpus": world, "scaling": "weak",
            "config": {"workload": f"{b} envs per GPU ({B} total), 64 steps, window 192, repo-default DT bf16 "
-                                  "(fused blocks), synthetic uint8 frames, all_gather of [B/N, 7] logits per step"}}
-    del ro, model, frames
+                                  "(fused blocks), all_gather of [B/N, 7] logits per step",
+                      "frames": "uint8 U[0,255] drawn on the device from the seed every step (inside the timed "
+                                "region), written into the rollout's frame buffer",
+                      "step": "one CUDA graph replay per step (embeddings, encoder, 4 layers with cache append "
+                              "and attention, action head) + all-gather + argmax"}}
+    del ro, model, first
     torch.cuda.empty_cache()
     return res
 

@@ -158,15 +158,16 @@ int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, 
  * (unscaled); bias [32] fp32; y [N, OH, OW, 32] 16-bit (channels-last, OH =
  * (H - 8) / 4 + 1); frame_max (device) ends > 1 exactly when some byte of the
  * frames exceeds 1 (the reference's test; the scan stops at the first such byte).
- * Rounding: the pixels enter the MMA as exact 16-bit integers, the 1/255 is
- * applied to the fp32 accumulator and the output is rounded once.  The
- * reference's 16-bit model rounds frames / 255 to its dtype before the
- * convolution; this kernel does not (it is the fp32 convolution of frames / 255
- * to within one output rounding), so its outputs differ from the reference's
- * 16-bit ones by that input rounding.
+ * Rounding (round_input = 0): the pixels enter the MMA as exact 16-bit
+ * integers, the 1/255 is applied to the fp32 accumulator and the output is
+ * rounded once: the fp32 convolution of frames / 255 to within one output
+ * rounding.  round_input = 1: frames / 255 is rounded to the output dtype
+ * first, as the reference's 16-bit model evaluates x / 255 before its
+ * convolution; the products then accumulate in fp32 and the output is
+ * rounded once.
  */
 int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int W, const void* w, const float* bias,
-                    unsigned int* frame_max, void* y, int dtype, void* stream);
+                    unsigned int* frame_max, void* y, int round_input, int dtype, void* stream);
 
 /*
  * dt_frames_conv1 for callers that cannot allocate device memory.  No
@@ -185,7 +186,7 @@ int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int W, const vo
  * calls whose work overlaps on the GPU, on different streams, race.
  */
 int dt_frames_conv1_noalloc(const void* frames, int64_t N, int C, int H, int W, const void* w, const float* bias,
-                            void* y, int dtype, void* stream);
+                            void* y, int round_input, int dtype, void* stream);
 
 /*
  * RMSNorm with the reference's rounding: y = w * cast(x * rsqrt(mean(x^2) +

@@ -57,6 +57,10 @@ class FastDTAttention(nn.Module):
         self.resid_dropout = nn.Dropout(self.dropout)
         self.compute_dtype = compute_dtype
         self.check_masks = check_masks
+        # "fp32": RoPE in fp32 inside the kernels, one rounding of the result.
+        # "reference": the reference's roundings (q * cos, rotate_half(q) * sin
+        # and their sum each rounded to the activation dtype, :113-116).
+        self.rope_rounding = "fp32"
         # RMSNorm of the owning block, fused into the projections when set
         # (held outside the module tree so the state_dict is unchanged).
         object.__setattr__(self, "_fused_norm", None)
@@ -139,7 +143,9 @@ class FastDTAttention(nn.Module):
         kd = self._kernel_dtype(x)
         cos, sin = position_embeddings
         xq, xk, xv, rotated = self._project(x, kd, raw_input, (cos, sin))
-        rope = not rotated
+        if self.rope_rounding not in ("fp32", "reference"):
+            raise ValueError(f"rope_rounding must be 'fp32' or 'reference', got {self.rope_rounding!r}")
+        rope = 0 if rotated else (2 if self.rope_rounding == "reference" else 1)
 
         if (isinstance(past_key_value, LayerKV) and past_key_value.length == 0 and seq_len > 1 and self.flash
                 and attention_mask is None):

@@ -47,6 +47,20 @@ __device__ __forceinline__ void rope_f32(float x0, float x1, const float* cr, co
   y1 = x1 * cr[d + half] + x0 * sr[d + half];
 }
 
+// The reference's fp32 evaluation of q * cos + rotate_half(q) * sin: two
+// rounded products and a rounded sum (no fused multiply-add).
+__device__ __forceinline__ void rope_f32_ref(float x0, float x1, const float* cr, const float* sr, int d, int half,
+                                             float& y0, float& y1) {
+  y0 = __fadd_rn(__fmul_rn(x0, cr[d]), -__fmul_rn(x1, sr[d]));
+  y1 = __fadd_rn(__fmul_rn(x1, cr[d + half]), __fmul_rn(x0, sr[d + half]));
+}
+
+__device__ __forceinline__ void rope_f32_mode(int mode, float x0, float x1, const float* cr, const float* sr, int d,
+                                              int half, float& y0, float& y1) {
+  if (mode == kRopeRefRound) rope_f32_ref(x0, x1, cr, sr, d, half, y0, y1);
+  else rope_f32(x0, x1, cr, sr, d, half, y0, y1);
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------- prefill
@@ -72,7 +86,7 @@ __global__ void __launch_bounds__(kF32Threads) dt_prefill_f32_kernel(const Prefi
       const float* cr = p.cos + (size_t)pos * p.cs_stride;
       const float* sr = p.sin + (size_t)pos * p.cs_stride;
 #pragma unroll
-      for (int d = 0; d < D / 2; ++d) rope_f32(qr[d], qr[d + D / 2], cr, sr, d, D / 2, q[d], q[d + D / 2]);
+      for (int d = 0; d < D / 2; ++d) rope_f32_mode(p.rope, qr[d], qr[d + D / 2], cr, sr, d, D / 2, q[d], q[d + D / 2]);
     } else {
 #pragma unroll
       for (int d = 0; d < D; ++d) q[d] = qr[d];
@@ -94,7 +108,7 @@ __global__ void __launch_bounds__(kF32Threads) dt_prefill_f32_kernel(const Prefi
       const float* kr = p.k + (size_t)b * p.k_sb + (size_t)key * p.k_ss + (size_t)g * p.k_sh;
       const float* vr = p.v + (size_t)b * p.v_sb + (size_t)key * p.v_ss + (size_t)g * p.v_sh;
       float y0 = kr[d], y1 = kr[d + D / 2];
-      if (p.rope) rope_f32(kr[d], kr[d + D / 2], p.cos + (size_t)key * p.cs_stride,
+      if (p.rope) rope_f32_mode(p.rope, kr[d], kr[d + D / 2], p.cos + (size_t)key * p.cs_stride,
                            p.sin + (size_t)key * p.cs_stride, d, D / 2, y0, y1);
       ks[j][d] = y0;
       ks[j][d + D / 2] = y1;
@@ -148,7 +162,7 @@ __global__ void __launch_bounds__(kF32Threads) dt_decode_f32_kernel(const Decode
       const float* kr = Kn + (size_t)b * p.kn_sb + (size_t)i * p.kn_ss + (size_t)g * p.kn_sh;
       const float* vr = Vn + (size_t)b * p.vn_sb + (size_t)i * p.vn_ss + (size_t)g * p.vn_sh;
       float y0 = kr[d], y1 = kr[d + D / 2];
-      if (p.rope) rope_f32(kr[d], kr[d + D / 2], p.cos + cs_row(i), p.sin + cs_row(i), d, D / 2, y0, y1);
+      if (p.rope) rope_f32_mode(p.rope, kr[d], kr[d + D / 2], p.cos + cs_row(i), p.sin + cs_row(i), d, D / 2, y0, y1);
       float* kc = static_cast<float*>(p.k_pages) + cache_off(L + i);
       float* vc = static_cast<float*>(p.v_pages) + cache_off(L + i);
       kc[d] = y0;
@@ -170,7 +184,7 @@ __global__ void __launch_bounds__(kF32Threads) dt_decode_f32_kernel(const Decode
     if (p.rope) {
 #pragma unroll
       for (int d = 0; d < D / 2; ++d)
-        rope_f32(qr[d], qr[d + D / 2], p.cos + cs_row(i), p.sin + cs_row(i), d, D / 2, q[d], q[d + D / 2]);
+        rope_f32_mode(p.rope, qr[d], qr[d + D / 2], p.cos + cs_row(i), p.sin + cs_row(i), d, D / 2, q[d], q[d + D / 2]);
     } else {
 #pragma unroll
       for (int d = 0; d < D; ++d) q[d] = qr[d];
@@ -195,7 +209,7 @@ __global__ void __launch_bounds__(kF32Threads) dt_decode_f32_kernel(const Decode
         const float* kr = Kn + (size_t)b * p.kn_sb + (size_t)ii * p.kn_ss + (size_t)g * p.kn_sh;
         const float* vr = Vn + (size_t)b * p.vn_sb + (size_t)ii * p.vn_ss + (size_t)g * p.vn_sh;
         k0 = kr[d], k1 = kr[d + D / 2], v0 = vr[d], v1 = vr[d + D / 2];
-        if (p.rope) rope_f32(kr[d], kr[d + D / 2], p.cos + cs_row(ii), p.sin + cs_row(ii), d, D / 2, k0, k1);
+        if (p.rope) rope_f32_mode(p.rope, kr[d], kr[d + D / 2], p.cos + cs_row(ii), p.sin + cs_row(ii), d, D / 2, k0, k1);
       }
       ks[j][d] = k0;
       ks[j][d + D / 2] = k1;

@@ -169,6 +169,8 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
     if (strides[i] <= 0 || (!f32 && strides[i] % 8 != 0))
       return fail(DT_ERR_INVALID, "dt_attn_prefill: stride #%d (%lld) must be a positive multiple of 8", i,
                   (long long)strides[i]);
+  if (apply_rope < 0 || apply_rope > 2)
+    return fail(DT_ERR_INVALID, "dt_attn_prefill: apply_rope must be 0, 1 or 2 (got %d)", apply_rope);
   if (apply_rope) {
     if (!cos_tab || !sin_tab) return fail(DT_ERR_INVALID, "dt_attn_prefill: null cos/sin with apply_rope");
     if (cos_rows < S) return fail(DT_ERR_INVALID, "dt_attn_prefill: cos/sin have %d rows < S=%d", cos_rows, S);
@@ -192,7 +194,7 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
     fp.o = static_cast<float*>(o); fp.cos = cos_tab; fp.sin = sin_tab; fp.pad_len = pad_len;
     fp.q_sb = q_sb; fp.q_ss = q_ss; fp.q_sh = q_sh; fp.k_sb = k_sb; fp.k_ss = k_ss; fp.k_sh = k_sh;
     fp.v_sb = v_sb; fp.v_ss = v_ss; fp.v_sh = v_sh; fp.o_sb = o_sb; fp.o_ss = o_ss; fp.o_sh = o_sh;
-    fp.cs_stride = (int)cos_stride; fp.rope = apply_rope ? 1 : 0; fp.S = S; fp.Hkv = Hkv; fp.R = R;
+    fp.cs_stride = (int)cos_stride; fp.rope = apply_rope; fp.S = S; fp.Hkv = Hkv; fp.R = R;
     fp.scale_log2 = sc0 * 1.4426950408889634f;
     fp.scale_div64 = sc0 / 64.f;
     cudaError_t e = dtk::launch_prefill_f32(fp, D, B, static_cast<cudaStream_t>(stream));
@@ -230,7 +232,7 @@ int dt_attn_prefill(const void* q, const void* k, const void* v, void* o, const 
   const float sc = scale > 0.f ? scale : 1.0f / sqrtf((float)D);
   prm.scale_log2 = sc * 1.4426950408889634f;
   prm.scale_div64 = sc / 64.f;
-  prm.rope = apply_rope ? 1 : 0;
+  prm.rope = apply_rope;
   const int units = B * Hkv;
   cudaError_t e;
   if (short_path) {
@@ -286,6 +288,7 @@ int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o,
   int rc = check_cache(fn, k_pages, v_pages, num_pages, page_size, block_table, max_pages, D, dtype);
   if (rc) return rc;
   if ((long long)max_pages * page_size > 0x7fffffffLL) return fail(DT_ERR_INVALID, "%s: cache capacity too large", fn);
+  if (apply_rope < 0 || apply_rope > 2) return fail(DT_ERR_INVALID, "%s: apply_rope must be 0, 1 or 2", fn);
   if (apply_rope) {
     if (!cos_tab || !sin_tab) return fail(DT_ERR_INVALID, "%s: null cos/sin with apply_rope", fn);
     if (!rope_abs && cos_rows < Sn) return fail(DT_ERR_INVALID, "%s: cos/sin have %d rows < Sn=%d", fn, cos_rows, Sn);
@@ -301,7 +304,7 @@ int dt_attn_decode(const void* q, const void* k_new, const void* v_new, void* o,
   p.status = status;
   p.q_sb = q_sb; p.q_ss = q_ss; p.q_sh = q_sh; p.kn_sb = kn_sb; p.kn_ss = kn_ss; p.kn_sh = kn_sh;
   p.vn_sb = vn_sb; p.vn_ss = vn_ss; p.vn_sh = vn_sh; p.o_sb = o_sb; p.o_ss = o_ss; p.o_sh = o_sh;
-  p.cs_stride = (int)cos_stride; p.rope = apply_rope ? 1 : 0; p.rope_abs = rope_abs ? 1 : 0; p.cos_rows = cos_rows;
+  p.cs_stride = (int)cos_stride; p.rope = apply_rope; p.rope_abs = rope_abs ? 1 : 0; p.cos_rows = cos_rows;
   p.Sn = Sn; p.Hkv = Hkv; p.R = Hq / Hkv; p.page_size = page_size; p.max_pages = max_pages; p.num_pages = num_pages;
   p.o_pairs = ((reinterpret_cast<uintptr_t>(o) & 3u) == 0 && o_sb % 2 == 0 && o_ss % 2 == 0 && o_sh % 2 == 0) ? 1 : 0;
   {
@@ -346,6 +349,7 @@ int dt_kv_write(const void* k, const void* v, void* k_pages, void* v_pages, int 
   if (B < 1 || S < 1 || Hkv < 1) return fail(DT_ERR_INVALID, "%s: sizes must be positive", fn);
   int rc = check_cache(fn, k_pages, v_pages, num_pages, page_size, block_table, max_pages, D, dtype);
   if (rc) return rc;
+  if (apply_rope < 0 || apply_rope > 2) return fail(DT_ERR_INVALID, "%s: apply_rope must be 0, 1 or 2", fn);
   if (apply_rope) {
     if (!cos_tab || !sin_tab) return fail(DT_ERR_INVALID, "%s: null cos/sin with apply_rope", fn);
     if (!rope_abs && cos_rows < S) return fail(DT_ERR_INVALID, "%s: cos/sin have %d rows < S=%d", fn, cos_rows, S);
@@ -357,7 +361,7 @@ int dt_kv_write(const void* k, const void* v, void* k_pages, void* v_pages, int 
   p.k = k; p.v = v; p.k_pages = k_pages; p.v_pages = v_pages; p.block_table = block_table; p.start_pos = start_pos;
   p.cos = cos_tab; p.sin = sin_tab; p.status = status;
   p.k_sb = k_sb; p.k_ss = k_ss; p.k_sh = k_sh; p.v_sb = v_sb; p.v_ss = v_ss; p.v_sh = v_sh;
-  p.cs_stride = (int)cos_stride; p.cos_rows = cos_rows; p.rope = apply_rope ? 1 : 0; p.rope_abs = rope_abs ? 1 : 0;
+  p.cs_stride = (int)cos_stride; p.cos_rows = cos_rows; p.rope = apply_rope; p.rope_abs = rope_abs ? 1 : 0;
   p.S = S; p.Hkv = Hkv; p.page_size = page_size; p.max_pages = max_pages; p.num_pages = num_pages;
   cudaError_t e = dtk::launch_kv_write_sm100(p, D, dtype, B, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "dt_kv_write launch");
@@ -479,7 +483,7 @@ extern "C" int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int
 }
 
 extern "C" int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int W, const void* w, const float* bias,
-                               unsigned int* frame_max, void* y, int dtype, void* stream) {
+                               unsigned int* frame_max, void* y, int round_input, int dtype, void* stream) {
   const char* fn = "dt_frames_conv1";
   if (!frames || !w || !bias || !frame_max || !y) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
   if (C != 4) return fail(DT_ERR_UNSUPPORTED, "%s: %d input channels (the kernel takes 4)", fn, C);
@@ -496,13 +500,14 @@ extern "C" int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int 
   if (rc) return rc;
   if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
   cudaError_t e = dtk::launch_frames_conv1_sm100(frames, N, H, W, w, bias, frame_max, y, dtype == DT_DTYPE_BF16,
-                                                 g_num_sms[dev], status, static_cast<cudaStream_t>(stream));
+                                                 round_input != 0, g_num_sms[dev], status,
+                                                 static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
   return DT_OK;
 }
 
 extern "C" int dt_frames_conv1_noalloc(const void* frames, int64_t N, int C, int H, int W, const void* w,
-                                       const float* bias, void* y, int dtype, void* stream) {
+                                       const float* bias, void* y, int round_input, int dtype, void* stream) {
   const char* fn = "dt_frames_conv1_noalloc";
   if (!frames || !w || !bias || !y) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
   if (C != 4) return fail(DT_ERR_UNSUPPORTED, "%s: %d input channels (the kernel takes 4)", fn, C);
@@ -525,8 +530,8 @@ extern "C" int dt_frames_conv1_noalloc(const void* frames, int64_t N, int C, int
   unsigned int* scratch = nullptr;
   cudaError_t e = dtk::conv1_noalloc_scratch(&scratch);
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s: scratch address: %s", fn, cudaGetErrorString(e));
-  e = dtk::launch_frames_conv1_sm100(frames, N, H, W, w, bias, scratch, y, dtype == DT_DTYPE_BF16, g_num_sms[dev],
-                                     status, static_cast<cudaStream_t>(stream));
+  e = dtk::launch_frames_conv1_sm100(frames, N, H, W, w, bias, scratch, y, dtype == DT_DTYPE_BF16, round_input != 0,
+                                     g_num_sms[dev], status, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
   return DT_OK;
 }

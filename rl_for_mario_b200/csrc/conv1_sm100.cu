@@ -88,7 +88,10 @@ __global__ void __launch_bounds__(256) frames_max_kernel(const uint4* __restrict
   }
 }
 
-template <bool BF16>
+// ROUND: the pixels enter the MMA as frames / 255 rounded to the 16-bit type
+// (the reference's 16-bit evaluation of x / 255 before its convolution, :338)
+// instead of exact integers with the 1/255 applied to the accumulator.
+template <bool BF16, bool ROUND>
 __global__ void __launch_bounds__(kC1Threads, 1)
     frames_conv1_kernel(const uint8_t* __restrict__ frames, const uint16_t* __restrict__ w,
                         const float* __restrict__ bias, const unsigned int* __restrict__ frame_max,
@@ -144,6 +147,9 @@ __global__ void __launch_bounds__(kC1Threads, 1)
   if (warp >= 8) {
     // ---------------------------------------------------------------- A builders
     const int tb = tid - 256;  // 0..511
+    // x / 255 in fp32, then rounded with the 16-bit conversion below: the same
+    // value as the reference's 16-bit division for every byte.
+    const float in_scale = (ROUND && *frame_max > 1u) ? (1.f / 255.f) : 1.f;
     int i = 0;
     bool ok = true;
     for (long long t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
@@ -174,10 +180,17 @@ __global__ void __launch_bounds__(kC1Threads, 1)
       for (int ky = 0; ky < 8; ++ky) {
         const uint32_t w0 = px[ky][0], w1 = px[ky][1];
         uint4 o;
-        o.x = E::from_f2(byte_f(w0, 0), byte_f(w0, 1));
-        o.y = E::from_f2(byte_f(w0, 2), byte_f(w0, 3));
-        o.z = E::from_f2(byte_f(w1, 0), byte_f(w1, 1));
-        o.w = E::from_f2(byte_f(w1, 2), byte_f(w1, 3));
+        if (ROUND) {
+          o.x = E::from_f2(byte_f(w0, 0) * in_scale, byte_f(w0, 1) * in_scale);
+          o.y = E::from_f2(byte_f(w0, 2) * in_scale, byte_f(w0, 3) * in_scale);
+          o.z = E::from_f2(byte_f(w1, 0) * in_scale, byte_f(w1, 1) * in_scale);
+          o.w = E::from_f2(byte_f(w1, 2) * in_scale, byte_f(w1, 3) * in_scale);
+        } else {
+          o.x = E::from_f2(byte_f(w0, 0), byte_f(w0, 1));
+          o.y = E::from_f2(byte_f(w0, 2), byte_f(w0, 3));
+          o.z = E::from_f2(byte_f(w1, 0), byte_f(w1, 1));
+          o.w = E::from_f2(byte_f(w1, 2), byte_f(w1, 3));
+        }
         *reinterpret_cast<uint4*>(ab + c * SH::A_ATOM + sw128_off(r, ky)) = o;
       }
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
@@ -214,7 +227,7 @@ __global__ void __launch_bounds__(kC1Threads, 1)
     // ---------------------------------------------------------------- epilogue
     const int wq = warp;
     const int r = wq * 32 + lane;
-    const float s = (*frame_max > 1u) ? (1.f / 255.f) : 1.f;
+    const float s = (!ROUND && *frame_max > 1u) ? (1.f / 255.f) : 1.f;
     const float* b = bias_s;
     int i = 0;
     bool ok = true;
@@ -253,8 +266,8 @@ __global__ void __launch_bounds__(kC1Threads, 1)
 }  // namespace
 
 cudaError_t launch_frames_conv1_sm100(const void* frames, long long N, int H, int W, const void* w,
-                                      const float* bias, unsigned int* frame_max, void* y, bool bf16, int num_sms,
-                                      int* status, cudaStream_t st) {
+                                      const float* bias, unsigned int* frame_max, void* y, bool bf16,
+                                      bool round_input, int num_sms, int* status, cudaStream_t st) {
   const long long bytes = N * 4LL * H * W;
   cudaError_t e = cudaMemsetAsync(frame_max, 0, sizeof(unsigned int), st);
   if (e != cudaSuccess) return e;
@@ -267,7 +280,8 @@ cudaError_t launch_frames_conv1_sm100(const void* frames, long long N, int H, in
   const long long total = N * OH * OW;
   const long long ntiles = (total + 127) / 128;
   const unsigned grid = (unsigned)(ntiles < num_sms ? ntiles : num_sms);
-  auto kfn = bf16 ? frames_conv1_kernel<true> : frames_conv1_kernel<false>;
+  auto kfn = bf16 ? (round_input ? frames_conv1_kernel<true, true> : frames_conv1_kernel<true, false>)
+                  : (round_input ? frames_conv1_kernel<false, true> : frames_conv1_kernel<false, false>);
   e = smem_limit_once(reinterpret_cast<const void*>(kfn), C1Shape::SMEM);
   if (e != cudaSuccess) return e;
   kfn<<<grid, kC1Threads, C1Shape::SMEM, st>>>(static_cast<const uint8_t*>(frames), static_cast<const uint16_t*>(w),

@@ -282,8 +282,13 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const __grid_con
       for (int u = 0; u < 4; ++u) {
         const float2 a2 = E::to_f2(wa[u]), b2 = E::to_f2(wb[u]);
         float y0, y1, z0, z1;
-        rope_pair(a2.x, b2.x, ca[2 * u], sa[2 * u], cb[2 * u], sb[2 * u], y0, z0);
-        rope_pair(a2.y, b2.y, ca[2 * u + 1], sa[2 * u + 1], cb[2 * u + 1], sb[2 * u + 1], y1, z1);
+        if (p.rope == kRopeRefRound) {
+          rope_pair_ref_round<BF16>(a2.x, b2.x, ca[2 * u], sa[2 * u], cb[2 * u], sb[2 * u], y0, z0);
+          rope_pair_ref_round<BF16>(a2.y, b2.y, ca[2 * u + 1], sa[2 * u + 1], cb[2 * u + 1], sb[2 * u + 1], y1, z1);
+        } else {
+          rope_pair(a2.x, b2.x, ca[2 * u], sa[2 * u], cb[2 * u], sb[2 * u], y0, z0);
+          rope_pair(a2.y, b2.y, ca[2 * u + 1], sa[2 * u + 1], cb[2 * u + 1], sb[2 * u + 1], y1, z1);
+        }
         ya[u] = E::from_f2(y0, y1);
         yb[u] = E::from_f2(z0, z1);
       }
@@ -316,7 +321,10 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const __grid_con
       const float* cr = cos_row(i);
       const float* sr = sin_row(i);
       float y0, y1;
-      rope_pair(k0, k1, cr[d], sr[d], cr[d + D / 2], sr[d + D / 2], y0, y1);
+      if (p.rope == kRopeRefRound)
+        rope_pair_ref_round<BF16>(k0, k1, cr[d], sr[d], cr[d + D / 2], sr[d + D / 2], y0, y1);
+      else
+        rope_pair(k0, k1, cr[d], sr[d], cr[d + D / 2], sr[d + D / 2], y0, y1);
       k0 = y0;
       k1 = y1;
     }
@@ -358,7 +366,10 @@ __global__ void __launch_bounds__(kDecThreads) dt_decode_kernel(const __grid_con
         if (p.rope) {
           const float* cr = cos_row(i);
           const float* sr = sin_row(i);
-          rope_pair(x0, x1, cr[d], sr[d], cr[d + D / 2], sr[d + D / 2], y0, y1);
+          if (p.rope == kRopeRefRound)
+            rope_pair_ref_round<BF16>(x0, x1, cr[d], sr[d], cr[d + D / 2], sr[d + D / 2], y0, y1);
+          else
+            rope_pair(x0, x1, cr[d], sr[d], cr[d + D / 2], sr[d + D / 2], y0, y1);
         } else {
           y0 = x0;
           y1 = x1;

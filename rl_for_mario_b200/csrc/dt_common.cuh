@@ -427,6 +427,8 @@ struct Elem<true> {
     __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
     return __bfloat1622float2(h);
   }
+  // x rounded to bf16 (nearest even), as a float.
+  static __device__ __forceinline__ float rnd(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
   static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -449,6 +451,8 @@ struct Elem<false> {
     __half2 h = *reinterpret_cast<__half2*>(&u);
     return __half22float2(h);
   }
+  // x rounded to fp16 (nearest even), as a float.
+  static __device__ __forceinline__ float rnd(float x) { return __half2float(__float2half_rn(x)); }
   static __device__ __forceinline__ uint32_t from_f2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -463,5 +467,24 @@ struct Elem<false> {
     return *reinterpret_cast<uint32_t*>(&r);
   }
 };
+
+// RoPE modes of the attention entry points (their apply_rope argument).
+constexpr int kRopeFp32 = 1;   // rotate in fp32, one rounding when the result is stored
+constexpr int kRopeRefRound = 2;  // the reference's roundings in the activation dtype (below)
+
+// One output pair of rotate-half RoPE with the reference's roundings: on
+// 16-bit tensors the reference evaluates q * cos + rotate_half(q) * sin
+// (model_decision_transformer.py:103-117) as three ops, each rounded to the
+// tensor dtype: y0 = rnd(rnd(x0 c0) + rnd(-x1 s0)), y1 = rnd(rnd(x1 c1) +
+// rnd(x0 s1)), with x1 the partner element D/2 away and c, s the (16-bit)
+// table entries.  Products of two 16-bit values are exact in fp32, so only
+// the three roundings matter.
+template <bool BF16>
+__device__ __forceinline__ void rope_pair_ref_round(float x0, float x1, float c0, float s0, float c1, float s1,
+                                                    float& y0, float& y1) {
+  using E = Elem<BF16>;
+  y0 = E::rnd(__fadd_rn(E::rnd(__fmul_rn(x0, c0)), -E::rnd(__fmul_rn(x1, s0))));
+  y1 = E::rnd(__fadd_rn(E::rnd(__fmul_rn(x1, c1)), E::rnd(__fmul_rn(x0, s1))));
+}
 
 }  // namespace dtk

@@ -154,9 +154,11 @@ cudaError_t conv1_noalloc_scratch(unsigned int** out);
 
 cudaError_t launch_frames_to_blocks_sm100(const void* frames, void* out, long long N, int C, int H, int W, bool bf16,
                                           unsigned int* frame_max, cudaStream_t st);
+// round_input: frames / 255 rounded to the output dtype before the
+// convolution (the reference's 16-bit rounding) instead of exact pixels.
 cudaError_t launch_frames_conv1_sm100(const void* frames, long long N, int H, int W, const void* w,
-                                      const float* bias, unsigned int* frame_max, void* y, bool bf16, int num_sms,
-                                      int* status, cudaStream_t st);
+                                      const float* bias, unsigned int* frame_max, void* y, bool bf16,
+                                      bool round_input, int num_sms, int* status, cudaStream_t st);
 cudaError_t launch_rmsnorm_sm100(const void* x, long long x_stride, const void* w, void* y, long long y_stride, int M,
                                  int K, float eps, bool bf16, int num_sms, cudaStream_t st);
 cudaError_t launch_rmsnorm_qkv_sm100(const CUtensorMap& x, const CUtensorMap& w, const CUtensorMap& y,

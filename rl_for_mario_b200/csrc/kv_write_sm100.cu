@@ -40,8 +40,16 @@ __global__ void __launch_bounds__(256) dt_kv_write_kernel(const KvWriteParams p)
       }
       const float* cr = p.cos + (size_t)row * p.cs_stride;
       const float* sr = p.sin + (size_t)row * p.cs_stride;
-      const float y0 = k0 * cr[d] - k1 * sr[d];
-      const float y1 = k1 * cr[d + D / 2] + k0 * sr[d + D / 2];
+      float y0, y1;
+      if (p.rope == kRopeRefRound) {
+        // The reference's roundings in T (rope_pair_ref_round; fp32: unfused products).
+        auto rnd = [](float x) { return (float)(T)x; };
+        y0 = rnd(__fadd_rn(rnd(__fmul_rn(k0, cr[d])), -rnd(__fmul_rn(k1, sr[d]))));
+        y1 = rnd(__fadd_rn(rnd(__fmul_rn(k1, cr[d + D / 2])), rnd(__fmul_rn(k0, sr[d + D / 2]))));
+      } else {
+        y0 = k0 * cr[d] - k1 * sr[d];
+        y1 = k1 * cr[d + D / 2] + k0 * sr[d + D / 2];
+      }
       k0 = y0;
       k1 = y1;
     }

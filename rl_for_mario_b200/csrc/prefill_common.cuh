@@ -19,10 +19,12 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 
 // Rotate one row of a swizzled tile in place:
 //   y[d] = x[d] cos[d] - x[d+D/2] sin[d],  y[d+D/2] = x[d+D/2] cos[d+D/2] + x[d] sin[d+D/2]
-// (rotate-half RoPE, reference :103-117).  Arithmetic in fp32.
+// (rotate-half RoPE, reference :103-117).  Arithmetic in fp32, or with the
+// reference's roundings in the activation dtype when ref_round
+// (rope_pair_ref_round).
 template <int D, bool BF16>
 __device__ __forceinline__ void rope_row_inplace(uint8_t* tile, int r, const float* __restrict__ cr,
-                                                 const float* __restrict__ sr) {
+                                                 const float* __restrict__ sr, bool ref_round = false) {
   constexpr int NCH = D / 8;  // 16-byte chunks per row
   constexpr int HALF = NCH / 2;
 #pragma unroll
@@ -48,10 +50,16 @@ __device__ __forceinline__ void rope_row_inplace(uint8_t* tile, int r, const flo
     for (int i = 0; i < 4; ++i) {
       const float2 xa = Elem<BF16>::to_f2(au[i]);
       const float2 xb = Elem<BF16>::to_f2(bu[i]);
-      const float y0 = xa.x * ca[2 * i] - xb.x * sa[2 * i];
-      const float y1 = xa.y * ca[2 * i + 1] - xb.y * sa[2 * i + 1];
-      const float z0 = xb.x * cb[2 * i] + xa.x * sb[2 * i];
-      const float z1 = xb.y * cb[2 * i + 1] + xa.y * sb[2 * i + 1];
+      float y0, y1, z0, z1;
+      if (ref_round) {
+        rope_pair_ref_round<BF16>(xa.x, xb.x, ca[2 * i], sa[2 * i], cb[2 * i], sb[2 * i], y0, z0);
+        rope_pair_ref_round<BF16>(xa.y, xb.y, ca[2 * i + 1], sa[2 * i + 1], cb[2 * i + 1], sb[2 * i + 1], y1, z1);
+      } else {
+        y0 = xa.x * ca[2 * i] - xb.x * sa[2 * i];
+        y1 = xa.y * ca[2 * i + 1] - xb.y * sa[2 * i + 1];
+        z0 = xb.x * cb[2 * i] + xa.x * sb[2 * i];
+        z1 = xb.y * cb[2 * i + 1] + xa.y * sb[2 * i + 1];
+      }
       ya[i] = Elem<BF16>::from_f2(y0, y1);
       yb[i] = Elem<BF16>::from_f2(z0, z1);
     }
@@ -98,9 +106,11 @@ __device__ __forceinline__ void rope_row_inplace_smem(uint8_t* tile, int r, cons
 
 // Same rotation from a shared-memory cos / sin row whose sin entries of the
 // first half are stored negated, in packed fp32 pairs (one multiply and one
-// fused multiply-add instruction per two outputs).
+// fused multiply-add instruction per two outputs).  ref_round: the
+// reference's roundings instead (rope_pair_ref_round).
 template <int D, bool BF16>
-__device__ __forceinline__ void rope_row_inplace_f2(uint8_t* tile, int r, const float* cr, const float* sr) {
+__device__ __forceinline__ void rope_row_inplace_f2(uint8_t* tile, int r, const float* cr, const float* sr,
+                                                    bool ref_round = false) {
   constexpr int NCH = D / 8;
   constexpr int HALF = NCH / 2;
   using E = Elem<BF16>;
@@ -118,6 +128,15 @@ __device__ __forceinline__ void rope_row_inplace_f2(uint8_t* tile, int r, const 
       const float2 cb = *reinterpret_cast<const float2*>(cr + (c + HALF) * 8 + 2 * i);
       const float2 sa = *reinterpret_cast<const float2*>(sr + c * 8 + 2 * i);  // negated
       const float2 sb = *reinterpret_cast<const float2*>(sr + (c + HALF) * 8 + 2 * i);
+      if (ref_round) {
+        // sa holds -sin: the products with it are rotate_half(x) * sin exactly.
+        float y0, y1, z0, z1;
+        rope_pair_ref_round<BF16>(xa.x, xb.x, ca.x, -sa.x, cb.x, sb.x, y0, z0);
+        rope_pair_ref_round<BF16>(xa.y, xb.y, ca.y, -sa.y, cb.y, sb.y, y1, z1);
+        ya[i] = E::from_f2(y0, y1);
+        yb[i] = E::from_f2(z0, z1);
+        continue;
+      }
       const float2 y = ffma2(xa, ca, fmul2(xb, sa));
       const float2 z = ffma2(xb, cb, fmul2(xa, sb));
       ya[i] = E::from_f2(y.x, y.y);

@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(kLongThreads, 1)
             const int pos = tile * PT + rr / R;
             if (pos < S)
               rope_row_inplace<D, BF16>(tq, rr, prm.cos + (size_t)pos * prm.cs_stride,
-                                        prm.sin + (size_t)pos * prm.cs_stride);
+                                        prm.sin + (size_t)pos * prm.cs_stride, prm.rope == kRopeRefRound);
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(kLongThreads, 1)
             const int key = it.kstart + j * kBK + rr;
             if (key < S)
               rope_row_inplace<D, BF16>(tk, rr, prm.cos + (size_t)key * prm.cs_stride,
-                                        prm.sin + (size_t)key * prm.cs_stride);
+                                        prm.sin + (size_t)key * prm.cs_stride, prm.rope == kRopeRefRound);
           }
           fence_proxy_async_smem();
           __syncwarp();

@@ -311,7 +311,8 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
       if (prm.rope) {
         uint8_t* kt = k_s + kvb * SS::KV_BYTES;
         for (int row = rt; row < S; row += SS::NROPE)
-          rope_row_inplace_f2<32, BF16>(kt, row, cos_s + row * SS::CS_STRIDE, sin_s + row * SS::CS_STRIDE);
+          rope_row_inplace_f2<32, BF16>(kt, row, cos_s + row * SS::CS_STRIDE, sin_s + row * SS::CS_STRIDE,
+                                        prm.rope == kRopeRefRound);
         fence_proxy_async_smem();
       }
       mbar_arrive(&kv_ready[kvb]);
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
             const int pos = t * PT + row / R;
             if (pos < S)
               rope_row_inplace_f2<32, BF16>(q_s + qs * SS::Q_BYTES, row, cos_s + pos * SS::CS_STRIDE,
-                                            sin_s + pos * SS::CS_STRIDE);
+                                            sin_s + pos * SS::CS_STRIDE, prm.rope == kRopeRefRound);
           }
           fence_proxy_async_smem();
         }

@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(256, PrefillShape<D>::MIN_BLOCKS)
           const int pos = tp.pos0 + row / R;
           if (pos < S)
             rope_row_inplace<D, BF16>(tile, row, prm.cos + (size_t)pos * prm.cs_stride,
-                                      prm.sin + (size_t)pos * prm.cs_stride);
+                                      prm.sin + (size_t)pos * prm.cs_stride, prm.rope == kRopeRefRound);
         }
         fence_proxy_async_smem();
       }
@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(256, PrefillShape<D>::MIN_BLOCKS)
             const int key = kb0 + row;
             if (key < S)
               rope_row_inplace<D, BF16>(tile, row, prm.cos + (size_t)key * prm.cs_stride,
-                                        prm.sin + (size_t)key * prm.cs_stride);
+                                        prm.sin + (size_t)key * prm.cs_stride, prm.rope == kRopeRefRound);
           }
           fence_proxy_async_smem();
         }

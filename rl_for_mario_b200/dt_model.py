@@ -189,7 +189,14 @@ class MarioStateEncoder(nn.Module):
             # One tensor-core kernel from the uint8 frames: the reference's
             # /255 when the max exceeds 1 (:338), the 8 x 8 stride-4
             # convolution, bias and ReLU (device-side decision, no host sync).
-            x, _ = kernels.frames_conv1(s, conv0.weight, conv0.bias)
+            x, _ = kernels.frames_conv1(s, conv0.weight, conv0.bias, round_input=self.round_input)
+        elif self.round_input:
+            # The reference's own 16-bit evaluation (:336-341) for shapes the
+            # first-layer kernel does not take.
+            x = s.to(dt)
+            x = torch.where(x.amax() > 1.0, x / 255.0, x)
+            x = F.relu(F.conv2d(x, conv0.weight, conv0.bias, stride=conv0.stride))
+            x = x.contiguous(memory_format=cl)
         else:
             # The reference divides by 255 when the frames' max exceeds 1 (:338).
             # The test stays on the device (no host synchronisation) and the 1/255
@@ -245,6 +252,10 @@ class MarioStateEncoder(nn.Module):
         return lin(x.contiguous().flatten(1)).reshape(B, T, -1)
 
     _fused_conv = True
+    # True: frames / 255 rounded to the model dtype before the first convolution,
+    # as the reference's 16-bit model does (:338); False: exact pixels, 1/255 on
+    # the fp32 accumulator.
+    round_input = False
 
     def _conv_relu(self, x: Tensor, w: Tensor, b: Optional[Tensor], stride) -> Tensor:
         """relu(conv2d(x, w) + b): cuDNN's fused convolution + bias + activation for
@@ -367,6 +378,22 @@ class MarioDT(nn.Module):
         """Fuses every block's input RMSNorm into its Q/K/V projection kernel."""
         for layer in self.model.layers:
             layer.fuse_norm(on)
+        return self
+
+    def reference_rounding(self, on: bool = True) -> "MarioDT":
+        """Evaluates a 16-bit model at the reference's own rounding points, so its
+        logits track the reference's 16-bit execution (model.to(torch.bfloat16))
+        rather than only its fp32 one: unfused blocks (RMSNorm, projections,
+        residual adds and the SwiGLU as separate roundings), RoPE with the
+        reference's three roundings inside the attention kernels, and frames /
+        255 rounded before the first convolution.  Slower than the fused
+        default; off restores RoPE in fp32 and exact encoder inputs (call
+        fuse_norms() again for the fused blocks)."""
+        if on:
+            self.fuse_norms(False)
+        for layer in self.model.layers:
+            layer.self_attn.rope_rounding = "reference" if on else "fp32"
+        self.model.state_encoder.round_input = bool(on)
         return self
 
     def heads(self, hidden: Tensor) -> Tuple[Tensor, Tensor]:

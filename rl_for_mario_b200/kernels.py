@@ -39,6 +39,16 @@ def _require_cuda(*ts: Optional[Tensor]) -> None:
             raise ValueError("dt attention kernels take CUDA tensors only (no CPU path)")
 
 
+def _rope_mode(apply_rope) -> int:
+    """apply_rope of the entry points: False / 0 none, True / 1 RoPE in fp32 with one
+    rounding of the result, 2 the reference's roundings in the activation dtype
+    (q * cos, rotate_half(q) * sin and their sum each rounded, as on 16-bit tensors)."""
+    mode = int(apply_rope)
+    if mode not in (0, 1, 2):
+        raise ValueError(f"apply_rope must be False/True or 0, 1, 2 (got {apply_rope!r})")
+    return mode
+
+
 def pad_len_from_mask(attention_mask: Tensor, S: int) -> Tensor:
     """Left-padding length per row of a [B, S] 0/1 mask (1 = valid), as int32 on its device.
 
@@ -57,7 +67,8 @@ def attn_prefill(q: Tensor, k: Tensor, v: Tensor, cos: Optional[Tensor], sin: Op
     """Causal GQA prefill: q [B,S,Hq,D], k/v [B,S,Hkv,D] -> out [B,S,Hq,D].
 
     RoPE (cos/sin [>=S, D] fp32) is applied to q and k inside the kernel when
-    apply_rope; pad_len [B] int32 gives per-row left padding (None = no mask).
+    apply_rope (2: with the reference's roundings, see _rope_mode); pad_len [B]
+    int32 gives per-row left padding (None = no mask).
     """
     _require_cuda(q, k, v, cos, sin, pad_len, out)
     B, S, Hq, D = q.shape
@@ -87,7 +98,7 @@ def attn_prefill(q: Tensor, k: Tensor, v: Tensor, cos: Optional[Tensor], sin: Op
         cos.stride(0) if apply_rope else 0, _ptr(pad_len), B, S, Hq, Hkv, D,
         q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
         v.stride(0), v.stride(1), v.stride(2), out.stride(0), out.stride(1), out.stride(2),
-        float(scale) if scale is not None else 0.0, 1 if apply_rope else 0, _dtype_code(q),
+        float(scale) if scale is not None else 0.0, _rope_mode(apply_rope), _dtype_code(q),
         _stream_ptr(q.device))
     _lib.check("dt_attn_prefill", rc)
     return out
@@ -220,7 +231,7 @@ def attn_decode(q: Tensor, k_new: Tensor, v_new: Tensor, layer, cos: Optional[Te
         cos.shape[0] if apply_rope else 0, cos.stride(0) if apply_rope else 0, 1 if rope_abs else 0,
         B, Sn, Hq, Hkv, D, q.stride(0), q.stride(1), q.stride(2), k_new.stride(0), k_new.stride(1),
         k_new.stride(2), v_new.stride(0), v_new.stride(1), v_new.stride(2), out.stride(0), out.stride(1),
-        out.stride(2), float(scale) if scale is not None else 0.0, 1 if apply_rope else 0, _dtype_code(q),
+        out.stride(2), float(scale) if scale is not None else 0.0, _rope_mode(apply_rope), _dtype_code(q),
         _stream_ptr(q.device))
     _lib.check("dt_attn_decode", rc)
     return out
@@ -247,7 +258,7 @@ def kv_write(k: Tensor, v: Tensor, layer, cos: Optional[Tensor], sin: Optional[T
         _ptr(layer.block_table), layer.block_table.shape[1], _ptr(start_pos), _ptr(cos) if apply_rope else None,
         _ptr(sin) if apply_rope else None, cos.shape[0] if apply_rope else 0, cos.stride(0) if apply_rope else 0,
         1 if rope_abs else 0, B, S, Hkv, D, k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
-        v.stride(2), 1 if apply_rope else 0, _dtype_code(k), _stream_ptr(k.device))
+        v.stride(2), _rope_mode(apply_rope), _dtype_code(k), _stream_ptr(k.device))
     _lib.check("dt_kv_write", rc)
 
 
@@ -276,11 +287,13 @@ def frames_to_blocks(frames: Tensor, dtype: torch.dtype, frame_max: Optional[Ten
     return out
 
 
-def frames_conv1(frames: Tensor, weight: Tensor, bias: Tensor) -> Tuple[Tensor, Tensor]:
+def frames_conv1(frames: Tensor, weight: Tensor, bias: Tensor, round_input: bool = False) -> Tuple[Tensor, Tensor]:
     """relu(conv2d(frames / 255 if max > 1 else frames, weight, bias, stride 4)) from
     uint8 frames [N, 4, H, W] with an 8 x 8 weight [32, 4, 8, 8] (16-bit): returns the
     output as a channels-last [N, 32, OH, OW] tensor of the weight's dtype and an
-    int32 [1] device tensor that is > 1 exactly when the frames' max exceeds 1."""
+    int32 [1] device tensor that is > 1 exactly when the frames' max exceeds 1.
+    round_input: frames / 255 rounded to the weight's dtype before the
+    convolution (the reference's 16-bit rounding) instead of exact pixels."""
     _require_cuda(frames, weight, bias)
     if frames.dtype != torch.uint8 or frames.dim() != 4 or not frames.is_contiguous():
         raise ValueError("frames must be a contiguous uint8 [N, C, H, W] tensor")
@@ -293,7 +306,7 @@ def frames_conv1(frames: Tensor, weight: Tensor, bias: Tensor) -> Tuple[Tensor, 
     out = torch.empty((N, 32, OH, OW), dtype=weight.dtype, device=frames.device, memory_format=torch.channels_last)
     fmax = torch.empty(1, dtype=torch.int32, device=frames.device)
     rc = _lib.load().dt_frames_conv1(_ptr(frames), N, C, H, W, _ptr(w2), _ptr(b), _ptr(fmax), _ptr(out),
-                                     _dtype_code(out), _stream_ptr(frames.device))
+                                     1 if round_input else 0, _dtype_code(out), _stream_ptr(frames.device))
     _lib.check("dt_frames_conv1", rc)
     return out, fmax
 

@@ -55,10 +55,24 @@ def gather_rows(local: Tensor, group=None) -> Tensor:
 
 
 class DTRollout:
-    """Cached rollout over a batch of environments on this rank's GPU."""
+    """Cached rollout over a batch of environments on this rank's GPU.
+
+    ``graphs=True`` replays each step's device work (embeddings, state
+    encoder, every layer with its cache append and attention, action head) as
+    one CUDA graph per step index, so a step costs the host one graph launch
+    instead of dozens of kernel launches and Python wrappers.  The first
+    episode after construction runs eagerly (it initialises every library and
+    kernel for each step's shapes); the next one captures step t's graph at step
+    t and replays it; later episodes only replay.  Cache lengths and the RoPE
+    rows a step uses depend on the step index, hence one graph per index; the
+    graphs share one memory pool and are always replayed in capture order.
+    The all-gather of the logits, the action choice and the host's cache
+    bookkeeping stay outside the graphs.  Inputs are copied into static
+    buffers (``frame_buffer`` can be written in place by the environment to
+    avoid the frame copy)."""
 
     def __init__(self, model: MarioDT, num_envs: int, max_steps: int, page_size: int = 64,
-                 group=None, device: Optional[torch.device] = None):
+                 group=None, device: Optional[torch.device] = None, graphs: bool = False):
         cfg = model.config
         self.model = model
         self.group = group
@@ -80,12 +94,81 @@ class DTRollout:
         self.prev_action: Optional[Tensor] = None
         self.prev_timestep: Optional[Tensor] = None
         self.steps = 0
+        self.max_steps = max_steps
+        self.use_graphs = graphs
+        self.episodes = 0
+        self._graphs = {}   # step index -> (CUDAGraph, host cache lengths after the step)
+        self._pool = None
+        self._static = None
 
     def reset(self) -> None:
         self.cache.reset()
         self.prev_action = None
         self.prev_timestep = None
+        if self.steps:
+            self.episodes += 1
         self.steps = 0
+
+    # ------------------------------------------------------------ graph mode
+    def _static_buffers(self, states: Tensor):
+        if self._static is None:
+            cfg = self.model.config
+            b, dev = self.local_envs, self.device
+            self._static = {
+                "states": torch.empty((b,) + tuple(states.shape[1:]), dtype=states.dtype, device=dev),
+                "rtg": torch.empty(b, dtype=torch.float32, device=dev),
+                "ts": torch.empty(b, dtype=torch.long, device=dev),
+                "prev_action": torch.zeros(b, dtype=torch.long, device=dev),
+                "prev_ts": torch.zeros(b, dtype=torch.long, device=dev),
+                "logits": torch.empty(b, cfg.act_dim, dtype=torch.float32, device=dev),
+            }
+        return self._static
+
+    @property
+    def frame_buffer(self) -> Optional[Tensor]:
+        """The static [b, C, H, W] frame input of graph mode (after the first step):
+        an environment that writes its observations here saves the per-step copy."""
+        return None if self._static is None else self._static["states"]
+
+    def _body(self, st: dict, first: bool) -> None:
+        """One step's device work on the static buffers; writes st["logits"]."""
+        bb = self.model.model
+        cfg = self.model.config
+        ts = st["ts"].clamp(0, cfg.max_ep_len - 1)
+        te = bb.embed_timestep(ts)
+        se = bb.state_encoder(st["states"].unsqueeze(1))[:, 0] + te
+        re = bb.embed_return(st["rtg"].view(-1, 1).to(bb.embed_return.weight.dtype)) + te
+        toks = [re, se]
+        if not first:
+            ae = bb.embed_action(st["prev_action"].clamp(0, cfg.act_dim - 1)) + bb.embed_timestep(st["prev_ts"])
+            toks.insert(0, ae)
+        h = bb.embed_norm(torch.stack(toks, dim=1))
+        st["logits"].copy_(self.step_tokens(h))
+
+    def _step_graphed(self, states: Tensor, returns_to_go: Tensor, timesteps: Tensor) -> Tensor:
+        st = self._static_buffers(states)
+        if states.data_ptr() != st["states"].data_ptr():
+            st["states"].copy_(states)
+        st["rtg"].copy_(returns_to_go)
+        st["ts"].copy_(timesteps)
+        t = self.steps
+        if self.episodes == 0:
+            # First episode: eager, which also initialises every kernel and library.
+            self._body(st, t == 0)
+        elif t not in self._graphs:
+            if self._pool is None:
+                self._pool = torch.cuda.graph_pool_handle()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self._pool):
+                self._body(st, t == 0)  # the Python side advances the host cache lengths here
+            self._graphs[t] = (g, [layer.length for layer in self.cache.layers])
+            g.replay()
+        else:
+            g, lengths = self._graphs[t]
+            g.replay()
+            for layer, n in zip(self.cache.layers, lengths):
+                layer.length = n
+        return st["logits"]
 
     @torch.no_grad()
     def step_tokens(self, tokens: Tensor) -> Tensor:
@@ -104,16 +187,26 @@ class DTRollout:
         """
         bb = self.model.model
         cfg = self.model.config
+        if self.steps >= self.max_steps:
+            raise ValueError(f"episode already has {self.max_steps} steps (reset() starts a new one)")
         ts = timesteps.clamp(0, cfg.max_ep_len - 1).long()
-        te = bb.embed_timestep(ts)
-        se = bb.state_encoder(states.unsqueeze(1))[:, 0] + te
-        re = bb.embed_return(returns_to_go.view(-1, 1).to(bb.embed_return.weight.dtype)) + te
-        toks = [re, se]
-        if self.prev_action is not None:
-            tp = bb.embed_timestep(self.prev_timestep)
-            toks.insert(0, bb.embed_action(self.prev_action.clamp(0, cfg.act_dim - 1)) + tp)
-        h = bb.embed_norm(torch.stack(toks, dim=1))
-        logits_local = self.step_tokens(h)
+        if self.use_graphs:
+            if self.steps > 0:
+                # The previous step's action (possibly set by the caller) and timestep.
+                st = self._static
+                st["prev_action"].copy_(self.prev_action)
+                st["prev_ts"].copy_(self.prev_timestep)
+            logits_local = self._step_graphed(states, returns_to_go, ts)
+        else:
+            te = bb.embed_timestep(ts)
+            se = bb.state_encoder(states.unsqueeze(1))[:, 0] + te
+            re = bb.embed_return(returns_to_go.view(-1, 1).to(bb.embed_return.weight.dtype)) + te
+            toks = [re, se]
+            if self.prev_action is not None:
+                tp = bb.embed_timestep(self.prev_timestep)
+                toks.insert(0, bb.embed_action(self.prev_action.clamp(0, cfg.act_dim - 1)) + tp)
+            h = bb.embed_norm(torch.stack(toks, dim=1))
+            logits_local = self.step_tokens(h)
         logits = gather_rows(logits_local.float(), self.group)
         if deterministic:
             actions = logits.argmax(-1)

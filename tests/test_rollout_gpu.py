@@ -45,3 +45,41 @@ def test_cached_rollout_matches_reprefill(dtype, fused):
     assert worst < tol, f"cached vs re-prefill logits differ by {worst:.3e}"
     assert agree >= B * T - 1
     assert ro.cache.length == 3 * T - 1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fused", [False, True])
+def test_graph_replayed_rollout_equals_eager(fused):
+    """graphs=True: episode 1 eager, episode 2 captures one graph per step index and
+    replays it, episode 3 only replays; every step's logits and actions equal the
+    eager rollout's, and the host cache lengths follow."""
+    from rl_for_mario_b200.dt_model import DTConfig, MarioDT
+    from rl_for_mario_b200.rollout import DTRollout
+
+    cfg = DTConfig(hidden_size=256, num_hidden_layers=4, num_attention_heads=8, num_key_value_heads=2,
+                   context_len=16, dropout=0.0)
+    cfgd = {k: getattr(cfg, k) for k in ("state_shape", "act_dim", "max_ep_len", "context_len", "hidden_size",
+                                         "num_hidden_layers", "num_attention_heads", "num_key_value_heads",
+                                         "intermediate_size")}
+    model = MarioDT(cfg)
+    model.load_state_dict(seeded_state_dict(dt_param_shapes(cfgd), 9), strict=True)
+    model = model.cuda().to(torch.bfloat16).eval()
+    if fused:
+        model.fuse_norms()
+    B, T = 6, 8
+    g = torch.Generator().manual_seed(1)
+    states = torch.randint(0, 256, (B, T, 4, 84, 84), generator=g, dtype=torch.uint8).cuda()
+    rtg = (torch.rand(B, T, generator=g) * 3000).cuda()
+    ts = (torch.randint(0, 4000, (B, 1), generator=g) + torch.arange(T)).cuda()
+    eager = DTRollout(model, num_envs=B, max_steps=T, page_size=16)
+    graph = DTRollout(model, num_envs=B, max_steps=T, page_size=16, graphs=True)
+    for episode in range(3):
+        eager.reset()
+        graph.reset()
+        for t in range(T):
+            a_e, l_e = eager.step(states[:, t], rtg[:, t], ts[:, t])
+            a_g, l_g = graph.step(states[:, t], rtg[:, t], ts[:, t])
+            assert torch.equal(l_e, l_g), (episode, t, (l_e - l_g).abs().max().item())
+            assert torch.equal(a_e, a_g)
+            assert graph.cache.length == eager.cache.length
+    assert len(graph._graphs) == T

@@ -31,11 +31,11 @@ def _conv1(lib, frames, w2, bias, noalloc):
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     if noalloc:
         rc = lib.dt_frames_conv1_noalloc(frames.data_ptr(), N, C, H, W, w2.data_ptr(), bias.data_ptr(),
-                                         y.data_ptr(), _lib.DT_DTYPE_BF16, stream)
+                                         y.data_ptr(), 0, _lib.DT_DTYPE_BF16, stream)
     else:
         fmax = torch.empty(1, dtype=torch.int32, device="cuda")
         rc = lib.dt_frames_conv1(frames.data_ptr(), N, C, H, W, w2.data_ptr(), bias.data_ptr(), fmax.data_ptr(),
-                                 y.data_ptr(), _lib.DT_DTYPE_BF16, stream)
+                                 y.data_ptr(), 0, _lib.DT_DTYPE_BF16, stream)
     _lib.check("dt_frames_conv1_noalloc" if noalloc else "dt_frames_conv1", rc)
     return y
 
@@ -68,8 +68,8 @@ def test_noalloc_conv1_rejects_bad_arguments():
     y = torch.empty((2, 20, 20, 32), dtype=torch.bfloat16, device="cuda")
     s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     assert lib.dt_frames_conv1_noalloc(frames.data_ptr(), 2, 3, 84, 84, w2.data_ptr(), bias.data_ptr(), y.data_ptr(),
-                                       _lib.DT_DTYPE_BF16, s) == _lib.DT_ERR_UNSUPPORTED
+                                       0, _lib.DT_DTYPE_BF16, s) == _lib.DT_ERR_UNSUPPORTED
     assert lib.dt_frames_conv1_noalloc(None, 2, 4, 84, 84, w2.data_ptr(), bias.data_ptr(), y.data_ptr(),
-                                       _lib.DT_DTYPE_BF16, s) == _lib.DT_ERR_INVALID
+                                       0, _lib.DT_DTYPE_BF16, s) == _lib.DT_ERR_INVALID
     assert lib.dt_frames_conv1_noalloc(frames.data_ptr(), 2, 4, 83, 84, w2.data_ptr(), bias.data_ptr(),
-                                       y.data_ptr(), _lib.DT_DTYPE_BF16, s) == _lib.DT_ERR_INVALID
+                                       y.data_ptr(), 0, _lib.DT_DTYPE_BF16, s) == _lib.DT_ERR_INVALID
