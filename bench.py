@@ -74,7 +74,7 @@ class ClockSampler:
                0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
 
-    def __init__(self, device_index: int, period_s: float = 0.01):
+    def __init__(self, device_index: int, period_s: float = 0.001):
         self.idx, self.period = device_index, period_s
         self.samples, self.reasons, self.max_mhz = [], set(), None
         self._stop = threading.Event()
@@ -212,8 +212,8 @@ def run_reference(args):
 
 def run_ours(args):
     from rl_for_mario_b200 import _lib
+    from rl_for_mario_b200.dt_model import rope_tables
     from rl_for_mario_b200.kernels import attn_prefill, attn_prefill_host, device_status
-    from oracle import precompute_freqs_cis
 
     rank, world, local, pg = _dist_setup(args.gpus)
     if not torch.cuda.is_available():
@@ -223,7 +223,7 @@ def run_ours(args):
     W = WORKLOAD
     B, S, Hq, Hkv, D = W["batch"], W["seq_len"], W["q_heads"], W["kv_heads"], W["head_dim"]
     q, k, v, pad = _make_inputs(B, S, Hq, Hkv, D, seed=1234 + rank, device=dev)
-    cos, sin = (t.to(dev) for t in precompute_freqs_cis(D, S))
+    cos, sin = (t.to(dev) for t in rope_tables(D, S, 1e4))
     out = torch.empty_like(q)
     stream = torch.cuda.current_stream(dev)
 
@@ -310,13 +310,15 @@ def run_ours(args):
                      "algorithmic_bytes_per_launch": byts, "peak_source": peaks["source"]},
     }
     if not args.no_decode:
+        cpu = world == 1 and not args.no_cpu_baseline
         if world == 1:
-            line["decode"] = bench_decode_cfg3(dev, peaks)
-            line["prefill_long"] = bench_prefill_cfg4(dev, peaks)
+            line["dt_forward_cfg1"] = bench_dt_cfg1(dev, cpu=cpu)
+            line["decode"] = bench_decode_cfg3(dev, peaks, cpu=cpu)
+            line["prefill_long"] = bench_prefill_cfg4(dev, peaks, cpu=cpu)
             line["prefill_long"]["rmsnorm_qkv_kernel"] = bench_rmsnorm_qkv_cfg4(dev, peaks)
             line["prefill_long"]["rmsnorm_swiglu_kernel"] = bench_rmsnorm_swiglu_cfg4(dev, peaks)
             line["prefill_long"]["encoder_conv1_kernel"] = bench_conv1_cfg4(dev, peaks)
-        line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg)
+        line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg, cpu=cpu)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
@@ -325,6 +327,120 @@ def run_ours(args):
         emit(line)
     if pg:
         pg.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- CPU baselines (oracle port)
+# The reference's CPU path restated by the oracle (float32 PyTorch, pinned to
+# the reference's own outputs by the golden tests), timed on the host cores on a
+# bounded slice of each workload.  Reported next to the GPU numbers, not targets.
+
+def _cpu_threads() -> int:
+    n = len(os.sched_getaffinity(0))
+    torch.set_num_threads(n)
+    return n
+
+
+def _oracle_cfg(cfg) -> dict:
+    return {k: getattr(cfg, k) for k in ("state_shape", "act_dim", "max_ep_len", "context_len", "hidden_size",
+                                         "num_hidden_layers", "num_attention_heads", "num_key_value_heads",
+                                         "intermediate_size", "rms_norm_eps", "rope_theta")}
+
+
+def _cpu_sd(model) -> dict:
+    return {k: v.detach().float().cpu() for k, v in model.state_dict().items()}
+
+
+def cpu_dt_forward(model, B: int, T: int, pad_max: int, budget_s: float = 6.0, seed: int = 0):
+    """Tokens/s of the oracle's full DT forward (fp32, CPU) on B samples of T timesteps."""
+    from oracle.dt_ref import dt_forward_ref
+    from oracle.seeded import dt_synthetic_inputs
+
+    threads = _cpu_threads()
+    cfgd = _oracle_cfg(model.config)
+    sd = _cpu_sd(model)
+    inp = dt_synthetic_inputs("bench_cpu", seed, B, T, cfgd["state_shape"], cfgd["act_dim"], pad_max)
+    reps, t0 = 0, time.perf_counter()
+    with torch.no_grad():
+        while True:
+            dt_forward_ref(sd, cfgd, inp["states"], inp["actions"], inp["rtg"], inp["timesteps"], inp.get("mask"))
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s:
+                break
+    return {"value": reps * B * 3 * T / el, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} forward(s) of B={B} x {3 * T} tokens, fp32 oracle, {el:.1f} s"}
+
+
+def cpu_cached_steps(model, B: int, prefix: int, steps: int, tokens_per_step: int = 3, seed: int = 0):
+    """Env-steps/s of the oracle's cached decode (the reference's cat-based cache,
+    fp32, CPU): a prefix of hidden states prefilled (not timed), then `steps`
+    cached steps of `tokens_per_step` hidden tokens through every layer, final
+    norm and action head."""
+    from oracle.attention_ref import precompute_freqs_cis, rmsnorm_ref
+    from oracle.dt_ref import block_ref
+
+    threads = _cpu_threads()
+    cfgd = _oracle_cfg(model.config)
+    sd = _cpu_sd(model)
+    H, L = cfgd["hidden_size"], cfgd["num_hidden_layers"]
+    cos, sin = precompute_freqs_cis(H // cfgd["num_attention_heads"], prefix + tokens_per_step * steps + 1,
+                                    cfgd["rope_theta"])
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        h = torch.randn(B, prefix, H, generator=g)
+        past = [None] * L
+        for i in range(L):
+            h, past[i] = block_ref(sd, cfgd, i, h, cos[:prefix], sin[:prefix], None, True, None)
+        pos = prefix
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            h = torch.randn(B, tokens_per_step, H, generator=g)
+            c, s_ = cos[pos:pos + tokens_per_step], sin[pos:pos + tokens_per_step]
+            for i in range(L):
+                h, past[i] = block_ref(sd, cfgd, i, h, c, s_, past[i], True, None)
+            st = rmsnorm_ref(h[:, -1], sd["model.norm.weight"], cfgd["rms_norm_eps"])
+            (st @ sd["action_head.weight"].t()).argmax(-1)
+            pos += tokens_per_step
+        el = time.perf_counter() - t0
+    return {"value": B * steps / el, "unit": "env-steps/s", "cores": threads, "kind": "port",
+            "sample": f"B={B} envs x {steps} cached steps of {tokens_per_step} tokens after a {prefix}-token prefix, "
+                      f"fp32 oracle (cat-based cache), {el:.1f} s"}
+
+
+def cpu_rollout(model, B: int, steps: int, seed: int = 0):
+    """Env-steps/s of a cached rollout on the oracle (fp32, CPU): per step the CNN
+    on the uint8 frames, the (a, R, s) embeddings, every layer with the cat-based
+    cache, final norm and action head, from an empty cache."""
+    from oracle.attention_ref import precompute_freqs_cis, rmsnorm_ref
+    from oracle.dt_ref import block_ref, embed_tokens_ref
+
+    threads = _cpu_threads()
+    cfgd = _oracle_cfg(model.config)
+    sd = _cpu_sd(model)
+    L = cfgd["num_hidden_layers"]
+    cos, sin = precompute_freqs_cis(cfgd["hidden_size"] // cfgd["num_attention_heads"], 3 * steps + 3,
+                                    cfgd["rope_theta"])
+    g = torch.Generator().manual_seed(seed)
+    past = [None] * L
+    pos = 0
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        for t in range(steps):
+            fr = torch.randint(0, 256, (B, 1) + tuple(cfgd["state_shape"]), generator=g, dtype=torch.uint8)
+            act = torch.randint(0, cfgd["act_dim"], (B, 1), generator=g)
+            rtg = torch.rand(B, 1, generator=g) * 3000
+            ts = torch.full((B, 1), t, dtype=torch.long)
+            h = embed_tokens_ref(sd, cfgd, fr, act, rtg, ts)  # 3 tokens per env, as a cached step appends
+            c, s_ = cos[pos:pos + 3], sin[pos:pos + 3]
+            for i in range(L):
+                h, past[i] = block_ref(sd, cfgd, i, h, c, s_, past[i], True, None)
+            st = rmsnorm_ref(h[:, -1], sd["model.norm.weight"], cfgd["rms_norm_eps"])
+            (st @ sd["action_head.weight"].t()).argmax(-1)
+            pos += 3
+        el = time.perf_counter() - t0
+    return {"value": B * steps / el, "unit": "env-steps/s", "cores": threads, "kind": "port",
+            "sample": f"B={B} envs x {steps} steps from an empty cache (CNN + embeddings + {L} layers), "
+                      f"fp32 oracle, {el:.1f} s"}
 
 
 # ----------------------------------------------------------------------------- decode workloads
@@ -338,7 +454,7 @@ def _decode_kernel_bytes(B, L, Sn, Hq, Hkv, D):
     return 2 * (2 * B * Hkv * L * D + B * Sn * (2 * Hq + 4 * Hkv) * D)
 
 
-def bench_decode_cfg3(dev, peaks):
+def bench_decode_cfg3(dev, peaks, cpu: bool = False):
     """16,384 environments, cache prefilled with 189 tokens, 21 cached steps of 3 tokens."""
     from rl_for_mario_b200 import kernels
     from rl_for_mario_b200.cache import PagedKVCache
@@ -419,8 +535,69 @@ def bench_decode_cfg3(dev, peaks):
                             "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
                             "algorithmic_bytes_per_launch": kb},
     }
-    del cache, model, steps_h
+    del cache, steps_h
     torch.cuda.empty_cache()
+    if cpu:
+        res["cpu_baseline"] = cpu_cached_steps(model, B=512, prefix=C["prefix"], steps=C["steps"])
+    del model
+    return res
+
+
+CFG1 = dict(batch=4, timesteps=64, hidden=256, layers=4, q_heads=8, kv_heads=2, pad_max_timesteps=32)
+
+
+def bench_dt_cfg1(dev, cpu: bool = False):
+    """The repo-default DT forward at its own batch (4 x 64 timesteps = 768 tokens,
+    hidden 256, 4 layers, 8/2 heads, left padding U{0..32} timesteps): the fp32
+    model on the fp32 kernels, the bf16 model with fused blocks, and the oracle's
+    fp32 forward on the host cores.  A latency-bound workload (one small batch)."""
+    from rl_for_mario_b200.dt_model import DTConfig, MarioDT
+    from oracle.seeded import dt_synthetic_inputs
+
+    C = CFG1
+    B, T = C["batch"], C["timesteps"]
+    torch.manual_seed(0)
+    cfg = DTConfig(hidden_size=C["hidden"], num_hidden_layers=C["layers"], num_attention_heads=C["q_heads"],
+                   num_key_value_heads=C["kv_heads"], context_len=T, dropout=0.0)
+    base = MarioDT(cfg).eval()
+    inp = {k: v.to(dev) for k, v in dt_synthetic_inputs("bench_cfg1", 0, B, T, cfg.state_shape, cfg.act_dim,
+                                                           C["pad_max_timesteps"]).items()}
+    res = {"metric": "DT forward tokens/s (4 x 64 timesteps = 768 tokens, hidden 256, 4 layers, 8/2 heads)",
+           "unit": "tokens/s", "config": {"workload": "repo-default DT, batch 4 x 64 timesteps, left pad "
+                                                      "U{0..32} timesteps, synthetic inputs, random-init weights"}}
+    allow = torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = torch.backends.cudnn.allow_tf32 = False
+    try:
+        for name, dtype, fused in (("fp32", torch.float32, False), ("bf16_fused", torch.bfloat16, True)):
+            m = MarioDT(cfg).eval()
+            m.load_state_dict(base.state_dict())
+            m = m.to(dev, dtype)
+            if fused:
+                m.fuse_norms()
+
+            def fwd():
+                with torch.no_grad():
+                    return m(inp["states"], inp["actions"], inp["rtg"], inp["timesteps"],
+                             attention_mask=inp["mask"]).action_logits
+
+            for _ in range(3):
+                fwd()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = 10
+            e0.record()
+            for _ in range(n):
+                fwd()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / n
+            res[name] = {"value": B * 3 * T / (ms * 1e-3), "ms": ms}
+            del m
+    finally:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = allow
+    res["value"] = res["bf16_fused"]["value"]
+    if cpu:
+        res["cpu_baseline"] = cpu_dt_forward(base, B=B, T=T, pad_max=C["pad_max_timesteps"], budget_s=6.0)
     return res
 
 
@@ -438,7 +615,7 @@ def _attended_pairs(S: int, pads) -> int:
     return tot
 
 
-def bench_prefill_cfg4(dev, peaks, batch=None, model=True):
+def bench_prefill_cfg4(dev, peaks, batch=None, model=True, cpu: bool = False):
     """Larger DT prefill: B=1024, 256 timesteps (768 tokens), hidden 768, 12 layers, 12/4 heads, head_dim 64.
 
     (a) the attention op alone at that shape, with Q / K rotated upstream as in
@@ -447,8 +624,7 @@ def bench_prefill_cfg4(dev, peaks, batch=None, model=True):
     encoder, embeddings, 12 blocks with fused RMSNorm + QKV + RoPE, final norm,
     action head) in tokens/s."""
     from rl_for_mario_b200.kernels import attn_prefill, device_status
-    from rl_for_mario_b200.dt_model import DTConfig, MarioDT
-    from oracle import precompute_freqs_cis
+    from rl_for_mario_b200.dt_model import DTConfig, MarioDT, rope_tables
 
     C = PREFILL_LONG_CFG
     B, T = batch or C["batch"], C["timesteps"]
@@ -460,7 +636,7 @@ def bench_prefill_cfg4(dev, peaks, batch=None, model=True):
     v = (torch.randn(B, S, Hkv, D, device=dev, generator=g) * 0.5).to(torch.bfloat16)
     pad_t = torch.randint(0, C["pad_max_timesteps"] + 1, (B,), device=dev, generator=g, dtype=torch.int32)
     pad = (3 * pad_t).to(torch.int32)
-    cos, sin = (t.to(dev) for t in precompute_freqs_cis(D, S))
+    cos, sin = (t.to(dev) for t in rope_tables(D, S, 1e4))
     out = torch.empty_like(q)
     for _ in range(3):
         attn_prefill(q, k, v, cos, sin, pad, out=out, apply_rope=False)
@@ -537,16 +713,19 @@ def bench_prefill_cfg4(dev, peaks, batch=None, model=True):
                      "peak_source": peaks["source"] + " (sustained)"},
         "attention_kernel": kernel_res,
     }
-    del model, states
+    del states
     torch.cuda.empty_cache()
+    if cpu:
+        res["cpu_baseline"] = cpu_dt_forward(model, B=8, T=T, pad_max=C["pad_max_timesteps"], budget_s=1.0)
+    del model
     return res
 
 
 def bench_rmsnorm_qkv_cfg4(dev, peaks, batch=None):
     """The fused RMSNorm + Q/K/V projection + RoPE kernel at a cfg4 layer's shape:
     M = batch x 768 tokens, K = hidden 768, N = (12 + 2 x 4) x 64 = 1280."""
+    from rl_for_mario_b200.dt_model import rope_tables
     from rl_for_mario_b200.kernels import device_status, fold_norm_weight, rmsnorm_qkv
-    from oracle import precompute_freqs_cis
 
     C = PREFILL_LONG_CFG
     B, S, H = batch or C["batch"], 3 * C["timesteps"], C["hidden"]
@@ -555,7 +734,7 @@ def bench_rmsnorm_qkv_cfg4(dev, peaks, batch=None):
     x = torch.randn(B, S, H, device=dev, generator=g).to(torch.bfloat16)
     wq, wk, wv = (torch.randn(h * D, H, device=dev, generator=g) / H ** 0.5 for h in (Hq, Hkv, Hkv))
     wf = fold_norm_weight(wq, wk, wv, torch.ones(H, device=dev), torch.bfloat16)
-    cos, sin = (t.to(dev) for t in precompute_freqs_cis(D, S))
+    cos, sin = (t.to(dev) for t in rope_tables(D, S, 1e4))
     rope = (cos, sin, (Hq + Hkv) * D, D)
     out = torch.empty(B, S, (Hq + 2 * Hkv) * D, device=dev, dtype=torch.bfloat16)
     for _ in range(3):
@@ -652,7 +831,7 @@ def bench_conv1_cfg4(dev, peaks, batch=None):
                          "peak_source": peaks["source"]}}
 
 
-def bench_rollout_cfg5(dev, world, rank, pg):
+def bench_rollout_cfg5(dev, world, rank, pg, cpu: bool = False):
     """8,192 environments per GPU, 64 cached steps, CNN on synthetic frames, all-gather of logits.
 
     Each step draws the environments' uint8 frames on the device from the seed
@@ -681,7 +860,8 @@ def bench_rollout_cfg5(dev, world, rank, pg):
         a = None
         for t in range(C["steps"]):
             fb = ro.frame_buffer if ro.frame_buffer is not None else first
-            fb.random_(0, 256, generator=g)  # the environments' observation of step t
+            # the environments' observation of step t: uniform bytes, drawn as 32-bit words
+            fb.view(torch.int32).random_(-2 ** 31, 2 ** 31 - 1, generator=g)
             a, _ = ro.step(fb, rtg[t], ts0 + t)
         return a
 
@@ -712,8 +892,11 @@ def bench_rollout_cfg5(dev, world, rank, pg):
                                 "region), written into the rollout's frame buffer",
                       "step": "one CUDA graph replay per step (embeddings, encoder, 4 layers with cache append "
                               "and attention, action head) + all-gather + argmax"}}
-    del ro, model, first
+    del ro, first
     torch.cuda.empty_cache()
+    if cpu:
+        res["cpu_baseline"] = cpu_rollout(model, B=64, steps=C["steps"])
+    del model
     return res
 
 
@@ -742,7 +925,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / rollout sub-benchmarks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
-    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "conv1"],
+    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "conv1", "rollout"],
                     default=None,
                     help="run one sub-benchmark alone and print its JSON (profiling)")
     ap.add_argument("--long-batch", type=int, default=None,
@@ -760,6 +943,8 @@ def main():
             emit({"only": "rmsnorm_qkv", **bench_rmsnorm_qkv_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "conv1":
             emit({"only": "conv1", **bench_conv1_cfg4(dev, _peaks(), batch=args.long_batch)})
+        elif args.only == "rollout":
+            emit({"only": "rollout", **bench_rollout_cfg5(dev, 1, 0, None)})
         elif args.only == "rmsnorm_swiglu":
             emit({"only": "rmsnorm_swiglu", **bench_rmsnorm_swiglu_cfg4(dev, _peaks(), batch=args.long_batch)})
         else:

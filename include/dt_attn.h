@@ -150,6 +150,18 @@ int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, 
                       int M, int K, int N, float eps, int dtype, void* stream);
 
 /*
+ * Residual GEMM of the DT block: y[m, :] += x[m, :] @ w^T in place, in fp32
+ * with one rounding of the sum (the residual is the GEMM's accumulator input).
+ * Replaces o_proj and its residual add (model_decision_transformer.py:247-248,
+ * :300) and down_proj and its residual add (:271, :303).  x [M, K], w [N, K]
+ * (K contiguous), y [M, N], row strides in elements; bf16 or fp16; K, N and
+ * the strides multiples of 8, N a multiple of 64, 16-byte aligned pointers.
+ * Runs on the persistent tcgen05 GEMM of dt_rmsnorm_qkv (256-column tiles).
+ */
+int dt_gemm_residual(const void* x, int64_t x_row_stride, const void* w, void* y, int64_t y_row_stride, int M, int K,
+                     int N, int dtype, void* stream);
+
+/*
  * The state encoder's first layer from the uint8 frames: frames / 255 (when
  * their maximum exceeds 1, model_decision_transformer.py:338), Conv2d(4, 32,
  * 8, stride 4) and ReLU (:315-341), as one implicit GEMM on the tensor cores.

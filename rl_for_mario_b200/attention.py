@@ -201,10 +201,14 @@ class FastDTAttention(nn.Module):
         if ((not self.training or self.resid_dropout.p == 0) and self.o_proj.bias is None
                 and residual.dtype == out.dtype == w.dtype):
             r2 = residual.reshape(-1, residual.shape[-1])
-            if residual_inplace and r2.data_ptr() == residual.data_ptr() and r2.is_contiguous():
-                r2.addmm_(out.reshape(-1, out.shape[-1]), w.t())
-                return residual, past_kv
-            return torch.addmm(r2, out.reshape(-1, out.shape[-1]), w.t()).view(residual.shape), past_kv
+            o2 = out.reshape(-1, out.shape[-1])
+            if not (residual_inplace and r2.data_ptr() == residual.data_ptr() and r2.is_contiguous()):
+                r2 = r2.clone()  # the caller keeps its residual: accumulate into a copy
+            if kernels.gemm_residual_ok(o2, w, r2):
+                kernels.gemm_residual(o2, w, r2)  # o_proj + residual in one tcgen05 GEMM
+            else:
+                r2.addmm_(o2, w.t())
+            return r2.view(residual.shape), past_kv
         return residual + self.resid_dropout(self.o_proj(out)), past_kv
 
 

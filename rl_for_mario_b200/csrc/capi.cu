@@ -392,7 +392,7 @@ namespace {
 int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const void* w_fused, void* y,
                      int64_t y_row_stride, int M, int K, int N, float eps, const float* cos_tab, const float* sin_tab,
                      int64_t cos_stride, int cos_rows, int seq_len, int rope_cols, int head_dim, int dtype,
-                     void* stream, int swiglu = 0) {
+                     void* stream, int swiglu = 0, int resid = 0) {
   // N counts rows of w_fused; with swiglu, y has N / 2 columns.
   if (!x || !w_fused || !y) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
   if (M < 1 || K < 1 || N < 1) return fail(DT_ERR_INVALID, "%s: sizes must be positive", fn);
@@ -410,7 +410,7 @@ int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const 
   if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
   const bool bf16 = dtype == DT_DTYPE_BF16;
   // 0: persistent kernel, 256-column tiles (the only one with the SwiGLU epilogue)
-  const int ncta = swiglu ? 0 : dtk::rmsnorm_qkv_ncta(N);
+  const int ncta = (swiglu || resid) ? 0 : dtk::rmsnorm_qkv_ncta(N);
   const int nsub = ncta == 0 ? 256 : (ncta <= 256 ? ncta : ncta / 2);
   CUtensorMap mx, mw, my;
   // The persistent kernel stages kPersistKChunk-wide K slices (32: 64-byte rows, 64-byte swizzle).
@@ -429,6 +429,7 @@ int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const 
   p.cos = cos_tab; p.sin = sin_tab; p.rope_cols = rope_cols; p.head_dim = head_dim; p.seq_len = seq_len;
   p.cs_stride = (int)cos_stride;
   p.swiglu = swiglu;
+  p.resid = resid;
   cudaError_t e = dtk::launch_rmsnorm_qkv_sm100(mx, mw, my, p, ncta, g_num_sms[dev],
                                                 static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
@@ -458,6 +459,14 @@ extern "C" int dt_rmsnorm_qkv_rope(const void* x, int64_t x_row_stride, const vo
     return fail(DT_ERR_INVALID, "%s: cos / sin must be 16-byte aligned with row stride >= head_dim, %% 4", fn);
   return rmsnorm_qkv_impl(fn, x, x_row_stride, w_fused, y, y_row_stride, M, K, N, eps, cos_tab, sin_tab, cos_stride,
                           cos_rows, seq_len, rope_cols, head_dim, dtype, stream);
+}
+
+extern "C" int dt_gemm_residual(const void* x, int64_t x_row_stride, const void* w, void* y, int64_t y_row_stride,
+                                int M, int K, int N, int dtype, void* stream) {
+  const char* fn = "dt_gemm_residual";
+  if (N % 64) return fail(DT_ERR_INVALID, "%s: N must be a multiple of 64 (got %d)", fn, N);
+  return rmsnorm_qkv_impl(fn, x, x_row_stride, w, y, y_row_stride, M, K, N, 1.f, nullptr, nullptr, 0, 0, 1, 0, 0,
+                          dtype, stream, 0, 1);
 }
 
 extern "C" int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int C, int H, int W,

@@ -376,6 +376,19 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 
 // ---------------------------------------------------------------- numerics
 // Hardware base-2 exponential (PTX ex2.approx.ftz.f32); ex2(-inf) = +0.
+// 1/x for a positive normal x on the FMA pipe only (no MUFU): the seed negates
+// the exponent field (0x7F000000 - bits(x) is 2^-e (1 - f) for x = 2^e (1 + f),
+// within 25 % of 1/x), then four Newton-Raphson steps y <- y + y (1 - x y), each
+// squaring the relative error (0.25 -> 6e-2 -> 4e-3 -> 1.5e-5 -> 2e-10).  Used
+// where the MUFU pipe is saturated by exponentials and a reciprocal there would
+// wait behind them.
+__device__ __forceinline__ float rcp_newton(float x) {
+  float y = __int_as_float(0x7F000000 - __float_as_int(x));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) y = fmaf(y, fmaf(-x, y, 1.f), y);
+  return y;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -410,6 +423,7 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
+
 // max(a, b, c) in one instruction.
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;

@@ -265,9 +265,9 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
                                            SS::KV_BYTES, 8 * SS::ROWB, kSw64);
         const int ksteps = T.n / 16;
         umma_f16_ts(td, pa, bd, idesc_pv, 0u);
-#pragma unroll
-        for (int kk = 1; kk < 12; ++kk)
-          if (kk < ksteps) umma_f16_ts(td, pa + kk * 8, bd + (uint64_t)(kk * 64), idesc_pv, 1u);
+        // Exactly ksteps MMAs: a predicated-off tcgen05.mma still costs its issue slot time.
+#pragma unroll 1
+        for (int kk = 1; kk < ksteps; ++kk) umma_f16_ts(td, pa + kk * 8, bd + (uint64_t)(kk * 64), idesc_pv, 1u);
         umma_commit(&o_full[w * 2 + slot]);
         slot ^= 1u;
         return true;
@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(SS::NTHREADS, 1)
         const int unit = blockIdx.x + c.lu * gridDim.x;
         const int b = unit / prm.Hkv;
         const int g = unit - b * prm.Hkv;
-        const float inv = 1.f / l;
+        const float inv = rcp_newton(l);
         typename E::T* orow = reinterpret_cast<typename E::T*>(prm.o) + (size_t)b * prm.o_sb +
                               (size_t)pos * prm.o_ss + (size_t)(g * R + h) * prm.o_sh;
 #pragma unroll

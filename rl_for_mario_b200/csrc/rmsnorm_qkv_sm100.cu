@@ -18,7 +18,10 @@
 // is the [B, S, Hq + 2 Hkv, D] view the attention kernels take directly.
 // With rope_cols > 0 the epilogue also applies the rotate-half RoPE to the q
 // and k heads (apply_rotary_pos_emb, :103-117), so the attention kernels can
-// take them pre-rotated.
+// take them pre-rotated.  The persistent kernel also runs the block's two
+// residual GEMMs without a norm (resid mode): y += x @ W^T in place, the
+// residual read in the epilogue and the sum rounded once (o_proj + residual,
+// :247-248 and :300; down_proj + residual, :271 and :303).
 #include "dt_common.cuh"
 #include "dt_internal.h"
 
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         __syncwarp();
       }
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&ss_full[sb], (bc >> 1) & 1, abort_flag, p.status)))) break;
-      const float rs = rsqrtf(ss_s[sb * 128 + r] / (float)p.K + p.eps);
+      const float rs = p.resid ? 1.f : rsqrtf(ss_s[sb * 128 + r] / (float)p.K + p.eps);
       const int row_g = rb * 128 + r;
       const int pos = p.rope_cols > 0 ? row_g % p.seq_len : 0;
       const float* crow = p.cos + (size_t)pos * p.cs_stride;
@@ -529,6 +532,53 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
             __syncwarp();
             if (lane == 0) {
               tma_store_2d(&tmY, stb, (n0 + c) >> 1, rb * 128 + wq * 32);
+              bulk_commit();
+            }
+            ++sc;
+          }
+        } else
+        if (p.resid) {
+          // y = residual + x W^T in fp32, rounded once (a GEMM with the residual
+          // as its accumulator input), in place: per 64-column slice, two
+          // 32-column halves of this row's residual values and accumulators.
+          for (int c = 0; c < kPN && n0 + c < p.N; c += 64) {
+            uint8_t* stb = st_s + wq * SH::ST_WARP;
+            if (lane == 0 && sc >= 1) bulk_wait_read<0>();  // the previous copy has read the slice
+            __syncwarp();
+            const uint4* yr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.y) +
+                                                             (size_t)row_g * p.y_stride + n0 + c);
+#pragma unroll
+            for (int hh = 0; hh < 64; hh += 32) {
+              uint4 res[4] = {};
+              if (row_g < p.M) {
+#pragma unroll
+                for (int q8 = 0; q8 < 4; ++q8) res[q8] = yr[(hh >> 3) + q8];
+              }
+              float v[32];
+              tmem_ld32(t_row + buf * kPN + c + hh, v);
+#pragma unroll
+              for (int q8 = 0; q8 < 4; ++q8) {
+                const uint32_t w4[4] = {res[q8].x, res[q8].y, res[q8].z, res[q8].w};
+                uint32_t o4[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int i = q8 * 8 + 2 * e;
+                  if (p.bf16) {
+                    const float2 f = Elem<true>::to_f2(w4[e]);
+                    o4[e] = Elem<true>::from_f2(v[i] + f.x, v[i + 1] + f.y);
+                  } else {
+                    const float2 f = Elem<false>::to_f2(w4[e]);
+                    o4[e] = Elem<false>::from_f2(v[i] + f.x, v[i + 1] + f.y);
+                  }
+                }
+                *reinterpret_cast<uint4*>(stb + lane * 128 + (((((hh >> 3) + q8)) ^ (lane & 7)) << 4)) =
+                    make_uint4(o4[0], o4[1], o4[2], o4[3]);
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmY, stb, n0 + c, rb * 128 + wq * 32);
               bulk_commit();
             }
             ++sc;

@@ -365,6 +365,36 @@ def rmsnorm_swiglu(x: Tensor, w_fused: Tensor, eps: float, out: Optional[Tensor]
     return out
 
 
+def gemm_residual_ok(x: Tensor, w: Tensor, y: Tensor) -> bool:
+    """Whether gemm_residual takes these operands (16-bit CUDA tensors, row-major
+    views with 16-byte aligned rows, N a multiple of 64)."""
+    if not (x.is_cuda and y.is_cuda and w.is_cuda):
+        return False
+    if x.dtype not in (torch.bfloat16, torch.float16) or w.dtype != x.dtype or y.dtype != x.dtype:
+        return False
+    K, N = x.shape[-1], y.shape[-1]
+    if w.shape != (N, K) or N % 64 or K % 8 or not w.is_contiguous():
+        return False
+    for t in (x, y):
+        if t.dim() != 2 or t.stride(1) != 1 or t.stride(0) % 8 or t.data_ptr() % 16:
+            return False
+    return x.shape[0] == y.shape[0]
+
+
+def gemm_residual(x: Tensor, w: Tensor, y: Tensor) -> Tensor:
+    """y += x @ w^T in place (fp32 accumulation, one rounding of the sum): the
+    block's o_proj / down_proj with its residual add.  x [M, K], w [N, K],
+    y [M, N] (2-D row-major views), bf16 / fp16."""
+    _require_cuda(x, w, y)
+    if not gemm_residual_ok(x, w, y):
+        raise ValueError("gemm_residual: x [M, K], w [N, K] contiguous, y [M, N] 16-bit row-major views with "
+                         "16-byte aligned rows and N a multiple of 64")
+    rc = _lib.load().dt_gemm_residual(_ptr(x), x.stride(0), _ptr(w), _ptr(y), y.stride(0), x.shape[0], x.shape[1],
+                                      y.shape[1], _dtype_code(x), _stream_ptr(x.device))
+    _lib.check("dt_gemm_residual", rc)
+    return y
+
+
 def rmsnorm_qkv(x: Tensor, w_fused: Tensor, eps: float, out: Optional[Tensor] = None,
                 rope: Optional[Tuple[Tensor, Tensor, int, int]] = None) -> Tensor:
     """y = RMSNorm(x) @ [Wq; Wk; Wv]^T with the norm weight folded into ``w_fused`` [N, K].

@@ -156,3 +156,36 @@ def test_rmsnorm_swiglu_rejects_bad_widths():
         rmsnorm_swiglu(x, torch.zeros(2 * 96, 64, dtype=torch.bfloat16, device="cuda"), 1e-5)
     with pytest.raises(RuntimeError):
         rmsnorm_swiglu(x, torch.zeros(2 * 64, 64, dtype=torch.bfloat16, device="cuda"), 1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,N", [(300, 256, 256), (1000, 768, 768), (777, 2048, 768), (130, 704, 256),
+                                   (5000, 256, 256)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemm_residual_matches_fp32(M, K, N, dtype):
+    """y += x @ w^T in place (the block's o_proj / down_proj with the residual add):
+    within one output rounding of the fp32 result."""
+    from rl_for_mario_b200.kernels import device_status, gemm_residual
+
+    g = torch.Generator(device="cuda").manual_seed(M + K + N)
+    x = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(dtype)
+    y0 = torch.randn(M, N, device="cuda", generator=g).to(dtype)
+    ref = y0.float() + x.float() @ w.float().t()
+    y = y0.clone()
+    out = gemm_residual(x, w, y)
+    assert out.data_ptr() == y.data_ptr()
+    assert device_status() == 0
+    rel = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
+    err = (y.float() - ref).abs()
+    assert (err <= rel * ref.abs() + 1e-3).all(), (err - rel * ref.abs()).max().item()
+
+
+@pytest.mark.gpu
+def test_gemm_residual_rejects_bad_shapes():
+    from rl_for_mario_b200.kernels import gemm_residual
+
+    x = torch.zeros(8, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        gemm_residual(x, torch.zeros(100, 64, dtype=torch.bfloat16, device="cuda"),
+                      torch.zeros(8, 100, dtype=torch.bfloat16, device="cuda"))  # N not a multiple of 64
