@@ -318,6 +318,7 @@ def run_ours(args):
             line["prefill_long"]["rmsnorm_qkv_kernel"] = bench_rmsnorm_qkv_cfg4(dev, peaks)
             line["prefill_long"]["rmsnorm_swiglu_kernel"] = bench_rmsnorm_swiglu_cfg4(dev, peaks)
             line["prefill_long"]["encoder_conv1_kernel"] = bench_conv1_cfg4(dev, peaks)
+            line["prefill_long"]["residual_gemms"] = bench_gemm_residual_cfg4(dev, peaks)
         line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg, cpu=cpu)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
@@ -794,6 +795,52 @@ def bench_rmsnorm_swiglu_cfg4(dev, peaks, batch=None):
                          "peak_source": peaks["source"]}}
 
 
+def bench_gemm_residual_cfg4(dev, peaks, batch=None):
+    """The block's residual GEMMs at a cfg4 layer's shape (M = batch x 768 tokens):
+    o_proj (K = 768, N = 768) and down_proj (K = FFN 2048, N = 768), each y += x W^T
+    in place on dt_gemm_residual, with cuBLAS's addmm_ on the same operands timed
+    beside it."""
+    from rl_for_mario_b200.kernels import device_status, gemm_residual
+
+    C = PREFILL_LONG_CFG
+    B, S, H = batch or C["batch"], 3 * C["timesteps"], C["hidden"]
+    M = B * S
+    g = torch.Generator(device=dev).manual_seed(6)
+    res = {}
+    R = ROLLOUT_CFG
+    shapes = (("o_proj", M, C["q_heads"] * C["head_dim"], H), ("down_proj", M, C["ffn"], H),
+              # one rollout step of 8,192 environments x 3 tokens, hidden 256, FFN 704
+              ("rollout_o_proj", R["envs_per_gpu"] * 3, R["hidden"], R["hidden"]),
+              ("rollout_down_proj", R["envs_per_gpu"] * 3, 704, R["hidden"]))
+    for name, M, K, H in shapes:
+        x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        w = (torch.randn(H, K, device=dev, generator=g) / K ** 0.5).to(torch.bfloat16)
+        y = torch.randn(M, H, device=dev, generator=g).to(torch.bfloat16)
+        out = {}
+        for impl, fn in (("ours", lambda: gemm_residual(x, w, y)), ("cublas_addmm", lambda: y.addmm_(x, w.t()))):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = 10
+            e0.record()
+            for _ in range(n):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / n
+            tf = 2 * M * K * H / (ms * 1e-3) / 1e12
+            out[impl] = {"ms": ms, "tflops": tf, "frac": tf / peaks["bf16_tflops"]}
+        if device_status() != 0:
+            raise SystemExit("device status error in the residual-GEMM benchmark")
+        res[name] = {"kernel": "dt_rmsnorm_qkv_persist_kernel (resid mode)", "M": M, "K": K, "N": H, **out,
+                     "roofline": {"bound": "tensor", "achieved": out["ours"]["tflops"], "peak": peaks["bf16_tflops"],
+                                  "unit": "TFLOP/s", "frac": out["ours"]["frac"], "peak_source": peaks["source"]}}
+        del x, w, y
+    torch.cuda.empty_cache()
+    return res
+
+
 def bench_conv1_cfg4(dev, peaks, batch=None):
     """The state encoder's first layer at cfg4's shape: batch x 256 frame stacks of
     4 x 84 x 84 uint8 -> relu(conv 8x8/4 + bias) with the /255 test, one kernel
@@ -883,9 +930,18 @@ def bench_rollout_cfg5(dev, world, rank, pg, cpu: bool = False):
         t = torch.tensor([ms, host_ms], device=dev)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         ms, host_ms = float(t[0].item()), float(t[1].item())
+    # The environments' share: the 64 frame draws alone.
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    fb = ro.frame_buffer
+    f0.record()
+    for _ in range(C["steps"]):
+        fb.view(torch.int32).random_(-2 ** 31, 2 ** 31 - 1, generator=g)
+    f1.record()
+    torch.cuda.synchronize()
+    frames_ms = f0.elapsed_time(f1)
     res = {"metric": "sharded rollout env-steps/s (CNN + 4 layers + cached attention + all-gather)",
            "unit": "env-steps/s", "value": B * C["steps"] / (ms * 1e-3), "ms_total": ms, "gpu_ms": ms,
-           "host_enqueue_ms": host_ms, "n_gpus": world, "scaling": "weak",
+           "host_enqueue_ms": host_ms, "frame_draw_ms": frames_ms, "n_gpus": world, "scaling": "weak",
            "config": {"workload": f"{b} envs per GPU ({B} total), 64 steps, window 192, repo-default DT bf16 "
                                   "(fused blocks), all_gather of [B/N, 7] logits per step",
                       "frames": "uint8 U[0,255] drawn on the device from the seed every step (inside the timed "
@@ -925,7 +981,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / rollout sub-benchmarks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
-    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "conv1", "rollout"],
+    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "conv1", "rollout",
+                                       "gemm_residual"],
                     default=None,
                     help="run one sub-benchmark alone and print its JSON (profiling)")
     ap.add_argument("--long-batch", type=int, default=None,
@@ -943,6 +1000,8 @@ def main():
             emit({"only": "rmsnorm_qkv", **bench_rmsnorm_qkv_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "conv1":
             emit({"only": "conv1", **bench_conv1_cfg4(dev, _peaks(), batch=args.long_batch)})
+        elif args.only == "gemm_residual":
+            emit({"only": "gemm_residual", **bench_gemm_residual_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "rollout":
             emit({"only": "rollout", **bench_rollout_cfg5(dev, 1, 0, None)})
         elif args.only == "rmsnorm_swiglu":

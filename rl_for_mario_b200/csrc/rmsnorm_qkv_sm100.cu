@@ -294,8 +294,8 @@ struct PShape {
   static constexpr int TAB_WARP = 32 * 128;
   static constexpr int OFF_SS = OFF_TAB + 4 * TAB_WARP;      // [2][128] floats
   static constexpr int OFF_BAR = OFF_SS + 2 * 128 * 4;
-  // full[S], empty[S], acc_full[2], acc_empty[2], ss_full[2], ss_empty[2], drain
-  static constexpr int NBAR = 2 * kPStages + 9;
+  // full[S], empty[S], acc_full[2], acc_empty[2], ss_full[2], ss_empty[2], drain, res_full[4]
+  static constexpr int NBAR = 2 * kPStages + 9 + 4;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -317,7 +317,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
   uint64_t* ss_full = acc_empty + 2;
   uint64_t* ss_empty = ss_full + 2;
   uint64_t* drain = ss_empty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* res_full = drain + 1;  // [epilogue warp]: residual slice landed (resid mode)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(res_full + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -337,6 +338,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       mbar_init(&ss_empty[j], 4);   // one per epilogue warp
     }
     mbar_init(drain, 1);
+    for (int j = 0; j < 4; ++j) mbar_init(&res_full[j], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -353,12 +355,17 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     if (lane == 0) {
       prefetch_tmap(&tmX);
       prefetch_tmap(&tmW);
+      if (p.resid) prefetch_tmap(&tmY);
       int cnt = 0;
       bool ok = true;
       for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x)
         for (int ct = 0; ct < nt && ok; ++ct)
           for (int kc = 0; kc < nk; ++kc, ++cnt) {
             const int s = cnt % kPStages;
+            // Residual mode: this tile's residual into L2 while its K chunks
+            // stream, ahead of the epilogue's TMA loads of it.
+            if (p.resid && kc == 0)
+              for (int q = 0; q < 16; ++q) tma_prefetch_l2_2d(&tmY, ct * kPN + (q & 3) * 64, rb * 128 + (q >> 2) * 32);
             // While the second column tile of a row block streams, pull this
             // CTA's next row block of x from HBM into L2, so that its first
             // tile (which reads x) runs at the L2 rate of the others.
@@ -424,6 +431,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     const int r = wq * 32 + lane;  // tile row = TMEM lane
     const uint32_t t_row = tmem + ((uint32_t)(wq * 32) << 16);
     int tc = 0, bc = 0, sc = 0;  // tiles, row blocks, staged output chunks
+    uint32_t rph = 0;            // residual slices loaded (resid mode)
     bool ok = true;
     for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++bc) {
       const int sb = bc & 1;
@@ -482,8 +490,12 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       const uint8_t* my_tab = tab_s + wq * SH::TAB_WARP + lane * 128;
       for (int ct = 0; ct < nt && ok; ++ct, ++tc) {
         const int buf = tc & 1;
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (tc >> 1) & 1, abort_flag, p.status)))) break;
-        tc_fence_after();
+        // (resid mode waits for the accumulator after requesting its first residual slice)
+        if (!p.resid) {
+          if (!(ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (tc >> 1) & 1, abort_flag, p.status))))
+            break;
+          tc_fence_after();
+        }
         const int n0 = ct * kPN;
         if (p.swiglu) {
           // Column pairs (gate block, up block) of 64: one 64-column output
@@ -539,26 +551,44 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         } else
         if (p.resid) {
           // y = residual + x W^T in fp32, rounded once (a GEMM with the residual
-          // as its accumulator input), in place: per 64-column slice, two
-          // 32-column halves of this row's residual values and accumulators.
-          for (int c = 0; c < kPN && n0 + c < p.N; c += 64) {
+          // as its accumulator input), in place.  Each 32 x 64 residual slice is
+          // brought into this warp's 4 KB buffer (the RoPE-table region, unused
+          // here) by TMA one slice ahead: the first before the accumulator wait,
+          // the next as soon as the current one is in registers.
+          uint8_t* resb = tab_s + wq * SH::TAB_WARP;
+          const int ncs = (p.N - n0) < kPN ? (p.N - n0) / 64 : kPN / 64;  // 64-column slices of this tile
+          for (int c = 0; c < ncs && ok; ++c) {
+            if (c == 0 && lane == 0) {
+              mbar_arrive_expect_tx(&res_full[wq], 32 * 128);
+              tma_load_2d(resb, &tmY, &res_full[wq], n0, rb * 128 + wq * 32);
+            }
+            if (c == 0 && !(ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (tc >> 1) & 1, abort_flag,
+                                                                   p.status))))
+              break;
+            if (c == 0) tc_fence_after();
+            if (!(ok = __all_sync(0xffffffffu, mbar_wait(&res_full[wq], rph & 1u, abort_flag, p.status)))) break;
+            ++rph;
+            uint4 res[8];
+#pragma unroll
+            for (int q8 = 0; q8 < 8; ++q8)
+              res[q8] = *reinterpret_cast<const uint4*>(resb + lane * 128 + ((q8 ^ (lane & 7)) << 4));
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (c + 1 < ncs && lane == 0) {
+              mbar_arrive_expect_tx(&res_full[wq], 32 * 128);
+              tma_load_2d(resb, &tmY, &res_full[wq], n0 + (c + 1) * 64, rb * 128 + wq * 32);
+            }
             uint8_t* stb = st_s + wq * SH::ST_WARP;
             if (lane == 0 && sc >= 1) bulk_wait_read<0>();  // the previous copy has read the slice
             __syncwarp();
-            const uint4* yr = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.y) +
-                                                             (size_t)row_g * p.y_stride + n0 + c);
 #pragma unroll
             for (int hh = 0; hh < 64; hh += 32) {
-              uint4 res[4] = {};
-              if (row_g < p.M) {
-#pragma unroll
-                for (int q8 = 0; q8 < 4; ++q8) res[q8] = yr[(hh >> 3) + q8];
-              }
               float v[32];
-              tmem_ld32(t_row + buf * kPN + c + hh, v);
+              tmem_ld32(t_row + buf * kPN + c * 64 + hh, v);
 #pragma unroll
               for (int q8 = 0; q8 < 4; ++q8) {
-                const uint32_t w4[4] = {res[q8].x, res[q8].y, res[q8].z, res[q8].w};
+                const uint4 rq = res[(hh >> 3) + q8];
+                const uint32_t w4[4] = {rq.x, rq.y, rq.z, rq.w};
                 uint32_t o4[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -571,14 +601,14 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                     o4[e] = Elem<false>::from_f2(v[i] + f.x, v[i + 1] + f.y);
                   }
                 }
-                *reinterpret_cast<uint4*>(stb + lane * 128 + (((((hh >> 3) + q8)) ^ (lane & 7)) << 4)) =
+                *reinterpret_cast<uint4*>(stb + lane * 128 + ((((hh >> 3) + q8) ^ (lane & 7)) << 4)) =
                     make_uint4(o4[0], o4[1], o4[2], o4[3]);
               }
             }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&tmY, stb, n0 + c, rb * 128 + wq * 32);
+              tma_store_2d(&tmY, stb, n0 + c * 64, rb * 128 + wq * 32);
               bulk_commit();
             }
             ++sc;
@@ -644,6 +674,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
       if (lane == 0) mbar_arrive(&ss_empty[sb]);
     }
     if (lane == 0) bulk_wait<0>();  // output copies complete before the CTA exits
+    // A residual load issued before an abort lands before the CTA exits.
+    if (p.resid && !ok && lane == 0) mbar_wait(&res_full[wq], rph & 1u, nullptr, nullptr);
   } else {
     // Row sums of squares of a 128-row block, read from the x chunks that the
     // ring stages for the block's first column tile (no extra pass over x).
@@ -660,7 +692,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
           const int s = cnt % kPStages;
           if (!(ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (cnt / kPStages) & 1, abort_flag, p.status))))
             break;
-          if (ct == 0) {
+          if (ct == 0 && !p.resid) {  // (resid mode applies no norm: only the stage releases)
             // Row rr of the chunk is the RB bytes at rr * RB (the swizzle
             // permutes 16-byte pieces inside the row); start each lane at a
             // different piece to spread a quarter warp over the banks.

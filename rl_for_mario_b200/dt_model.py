@@ -6,9 +6,11 @@ block :278-304, state encoder :315-341, backbone :348-461, wrapper :468-548)
 whose attention is ``FastDTAttention``.  Parameter names match the reference,
 so a reference state_dict loads unchanged (checkpoint compatibility).  With
 ``fuse_norms()`` a block runs as: RMSNorm + Q/K/V + RoPE kernel, attention
-kernel, o_proj + residual GEMM, RMSNorm + gate/up + SwiGLU kernel, down_proj +
-residual GEMM (all tcgen05 kernels of the library); the rest (CNN encoder past
-its first layer, embeddings, final norm, heads) runs as PyTorch on the GPU.
+kernel, o_proj GEMM with the residual as accumulator input, RMSNorm + gate/up
++ SwiGLU kernel, down_proj GEMM with the residual (the two residual GEMMs on
+cuBLAS, which measures faster than the library's dt_gemm_residual at these
+shapes); the rest (CNN encoder past its first layer, embeddings, final norm,
+heads) runs as PyTorch on the GPU.
 """
 from __future__ import annotations
 
@@ -150,11 +152,8 @@ class DTBlock(nn.Module):
                 a = kernels.rmsnorm_swiglu(h, self._swiglu_weight(h.dtype), self.post_attention_layernorm.eps)
                 # h is this block's own intermediate: the down projection
                 # accumulates into it in place (no copy of the residual).
-                a2, h2, wd = a.reshape(-1, a.shape[-1]), h.view(-1, h.shape[-1]), self.mlp.down_proj.weight
-                if kernels.gemm_residual_ok(a2, wd, h2):
-                    kernels.gemm_residual(a2, wd, h2)
-                else:
-                    h2.addmm_(a2, wd.t())
+                # (cuBLAS's addmm_: measured faster than dt_gemm_residual here)
+                h.view(-1, h.shape[-1]).addmm_(a.reshape(-1, a.shape[-1]), self.mlp.down_proj.weight.t())
             else:
                 h = h + self.mlp(self.post_attention_layernorm(h))
             return h, present
