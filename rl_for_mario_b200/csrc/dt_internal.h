@@ -51,6 +51,9 @@ cudaError_t launch_prefill_sm100(const CUtensorMap& q, const CUtensorMap& k, con
                                  const PrefillParams& prm, int D, bool bf16, int grid, cudaStream_t stream);
 
 // Persistent variant for head_dim 32 and S <= 192 (K/V resident per unit).
+// A CTA stages the padding of at most kShortMaxUnitsPerCta units; the grid
+// grows past the SM count when there are more.
+constexpr int kShortMaxUnitsPerCta = 2048;
 cudaError_t launch_prefill_short_sm100(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                                        const PrefillParams& prm, bool bf16, int n_units, int grid,
                                        cudaStream_t stream);

@@ -48,7 +48,7 @@ struct SS {
   static constexpr int OFF_COS = OFF_V + NKV * KV_BYTES;
   static constexpr int OFF_SIN = OFF_COS + SMAX * CS_STRIDE * 4;
   static constexpr int OFF_PAD = OFF_SIN + SMAX * CS_STRIDE * 4;
-  static constexpr int MAX_UNITS = 2048;       // units per CTA (per-unit pads staged in smem)
+  static constexpr int MAX_UNITS = kShortMaxUnitsPerCta;  // units per CTA (per-unit pads staged in smem)
   static constexpr int OFF_BAR = OFF_PAD + MAX_UNITS * 4;
   // q_full, q_ready, q_empty [NQ]; kv_full, kv_ready, kv_empty [NKV]; s_full, p_full [2 warpgroups];
   // o_full [2 warpgroups x 2 slots]; drain [2 issuers]
