@@ -133,7 +133,8 @@ def _dist_setup(n_gpus: int):
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if backend == "nccl":
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local) if backend == "nccl" else None)
         pg = dist
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
@@ -455,8 +456,9 @@ def _decode_kernel_bytes(B, L, Sn, Hq, Hkv, D):
     return 2 * (2 * B * Hkv * L * D + B * Sn * (2 * Hq + 4 * Hkv) * D)
 
 
-def bench_decode_cfg3(dev, peaks, cpu: bool = False):
-    """16,384 environments, cache prefilled with 189 tokens, 21 cached steps of 3 tokens."""
+def bench_decode_cfg3(dev, peaks, cpu: bool = False, envs=None):
+    """16,384 environments, cache prefilled with 189 tokens, 21 cached steps of 3 tokens
+    (``envs``: another environment count, for profiling a smaller case)."""
     from rl_for_mario_b200 import kernels
     from rl_for_mario_b200.cache import PagedKVCache
     from rl_for_mario_b200.dt_model import DTConfig, MarioDT
@@ -466,7 +468,7 @@ def bench_decode_cfg3(dev, peaks, cpu: bool = False):
     cfg = DTConfig(hidden_size=C["hidden"], num_hidden_layers=C["layers"], num_attention_heads=C["q_heads"],
                    num_key_value_heads=C["kv_heads"], context_len=(C["prefix"] + 3 * C["steps"]) // 3, dropout=0.0)
     model = MarioDT(cfg).to(dev, torch.bfloat16).eval()
-    B, H = C["envs"], C["hidden"]
+    B, H = envs or C["envs"], C["hidden"]
     max_len = C["prefix"] + 3 * C["steps"]
     cache = PagedKVCache(C["layers"], B, C["kv_heads"], C["head_dim"], max_len, page_size=64, dtype=torch.bfloat16,
                          device=dev)
@@ -995,7 +997,7 @@ def main():
         _lib.load()
         dev = torch.device("cuda", 0)
         if args.only == "decode":
-            emit({"only": "decode", **bench_decode_cfg3(dev, _peaks())})
+            emit({"only": "decode", **bench_decode_cfg3(dev, _peaks(), envs=args.batch)})
         elif args.only == "rmsnorm_qkv":
             emit({"only": "rmsnorm_qkv", **bench_rmsnorm_qkv_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "conv1":
