@@ -84,10 +84,13 @@ struct LongItem {
 __device__ __forceinline__ LongItem long_item(int i, const PrefillParams& prm, int n_units, int npairs,
                                               int ntiles) {
   LongItem it;
-  // Heaviest pairs (latest positions) first, units innermost.  With an odd
-  // tile count the lone tile is tile 0, the lightest.
-  const int p = npairs - 1 - i / n_units;
-  const int unit = i - (i / n_units) * n_units;
+  // Unit-major: the pairs of one (sample, KV head) unit are consecutive items,
+  // heaviest (latest positions) first, so the CTAs that take them at the same
+  // time read the unit's K/V blocks from HBM once and from L2 after that; the
+  // round-robin over CTAs still gives each CTA a mix of pair weights.  With an
+  // odd tile count the lone tile is tile 0, the lightest.
+  const int unit = i / npairs;
+  const int p = npairs - 1 - (i - unit * npairs);
   it.b = unit / prm.Hkv;
   it.g = unit - it.b * prm.Hkv;
   const int S = prm.S, PT = prm.PT;
