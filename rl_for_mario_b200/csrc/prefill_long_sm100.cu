@@ -76,6 +76,8 @@ struct LongShape {
 };
 
 // Geometry of one work item; every role derives it from the item index.
+constexpr int kLongGroupUnits = 128;  // units whose pairs are scheduled together (L2 reuse of K/V)
+
 struct LongItem {
   int b, g, pad, kstart, nblocks;
   int tile[2], first[2], last[2];
@@ -84,13 +86,18 @@ struct LongItem {
 __device__ __forceinline__ LongItem long_item(int i, const PrefillParams& prm, int n_units, int npairs,
                                               int ntiles) {
   LongItem it;
-  // Unit-major: the pairs of one (sample, KV head) unit are consecutive items,
-  // heaviest (latest positions) first, so the CTAs that take them at the same
-  // time read the unit's K/V blocks from HBM once and from L2 after that; the
-  // round-robin over CTAs still gives each CTA a mix of pair weights.  With an
-  // odd tile count the lone tile is tile 0, the lightest.
-  const int unit = i / npairs;
-  const int p = npairs - 1 - (i - unit * npairs);
+  // Units in groups of kLongGroupUnits: within a group the heaviest pairs
+  // (latest positions) go first, units innermost, so the end of the grid runs
+  // the lightest items; a group's K/V (128 units x 196 KB at cfg4, 25 MB) stays
+  // in L2 while its pairs are worked through, so each K/V block crosses HBM
+  // about once instead of once per pair.  With an odd tile count the lone tile
+  // is tile 0, the lightest.
+  const int per = kLongGroupUnits * npairs;
+  const int grp = i / per;
+  const int j = i - grp * per;
+  const int gu = min(kLongGroupUnits, n_units - grp * kLongGroupUnits);  // units in this group
+  const int p = npairs - 1 - j / gu;
+  const int unit = grp * kLongGroupUnits + (j - (j / gu) * gu);
   it.b = unit / prm.Hkv;
   it.g = unit - it.b * prm.Hkv;
   const int S = prm.S, PT = prm.PT;
