@@ -659,13 +659,56 @@ def bench_prefill_cfg4(dev, peaks, batch=None, model=True, cpu: bool = False):
     byts = _algorithmic_bytes(B, S, Hq, Hkv, D)
     del q, k, v, out
     torch.cuda.empty_cache()
+    # The binding resource: the larger of the FLOP time at the GEMM peak and the
+    # byte time at the HBM peak (per launch); frac = that lower bound / the time.
+    t_flop = flops / (peaks["bf16_tflops"] * 1e12)
+    t_byte = byts / (peaks["hbm_gbs"] * 1e9)
+    bound = "tensor" if t_flop >= t_byte else "hbm"
     kernel_res = {"kernel": "dt_prefill_long_kernel", "inputs": "q / k rotated upstream", "batch": B, "ms": kms,
                   "tokens_per_s": B * S / (kms * 1e-3),
-                  "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
-                               "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"], "flops_per_launch": flops,
-                               "hbm_achieved_gbs": byts / (kms * 1e-3) / 1e9, "peak_source": peaks["source"]}}
+                  "roofline": {"bound": bound, "lower_bound_ms": max(t_flop, t_byte) * 1e3,
+                               "frac": max(t_flop, t_byte) / (kms * 1e-3),
+                               "achieved_tflops": tflops, "peak_tflops": peaks["bf16_tflops"],
+                               "tensor_frac": tflops / peaks["bf16_tflops"], "flops_per_launch": flops,
+                               "achieved_gbs": byts / (kms * 1e-3) / 1e9, "peak_gbs": peaks["hbm_gbs"],
+                               "hbm_frac": byts / (kms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                               "algorithmic_bytes_per_launch": byts, "peak_source": peaks["source"]}}
     if not model:
         return {"attention_kernel": kernel_res}
+
+    # (a') the drop-in module on the normalised layer input, as inside the
+    # reference's block: q | k | v + RoPE in one GEMM, the attention kernel on
+    # pre-rotated q / k, o_proj; against the same module with the projections
+    # on cuBLAS and the RoPE inside the attention kernel.
+    from rl_for_mario_b200.attention import FastDTAttention
+
+    class _Cfg:
+        hidden_size, num_attention_heads, num_key_value_heads = C["hidden"], Hq, Hkv
+        dropout, flash_attn = 0.0, True
+
+    att = FastDTAttention(_Cfg()).to(dev, torch.bfloat16).eval()
+    xin = torch.randn(B, S, C["hidden"], device=dev, generator=g).to(torch.bfloat16)
+    mask_tok = (torch.arange(S, device=dev)[None, :] >= pad[:, None].long()).to(torch.bfloat16)
+    dropin = {}
+    for name, rounding in (("one_gemm_qkv_rope", "fp32"), ("cublas_projections_rope_in_kernel", "reference")):
+        # "reference" RoPE rounding keeps the separate projections + in-kernel RoPE path
+        att.rope_rounding = rounding
+        with torch.no_grad():
+            for _ in range(2):
+                att(xin, (cos, sin), attention_mask=mask_tok)
+            torch.cuda.synchronize()
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            d0.record()
+            for _ in range(3):
+                att(xin, (cos, sin), attention_mask=mask_tok)
+            d1.record()
+            torch.cuda.synchronize()
+        dropin[name] = {"ms": d0.elapsed_time(d1) / 3}
+    dropin["note"] = ("FastDTAttention.forward on [1024, 768, 768] bf16 input with the padding mask "
+                      "(projections, RoPE, attention, o_proj)")
+    kernel_res["dropin_module_layer"] = dropin
+    del att, xin
+    torch.cuda.empty_cache()
 
     # (b) full model forward
     torch.manual_seed(4)

@@ -150,6 +150,20 @@ int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void* w_fused, 
                       int M, int K, int N, float eps, int dtype, void* stream);
 
 /*
+ * Q/K/V projection + RoPE without a norm: y = x @ w^T with the rotate-half RoPE
+ * of the q and k heads (columns [0, rope_cols)) applied in the epilogue, as
+ * dt_rmsnorm_qkv_rope does after its norm.  Replaces q_proj / k_proj / v_proj
+ * (model_decision_transformer.py:175-177) and apply_rotary_pos_emb (:103-117,
+ * applied at :179-183) when the caller has already normalised x (the drop-in
+ * module inside the reference's block, whose input_layernorm runs first,
+ * :296); the attention entry points then take q / k with apply_rope = 0.
+ * w = [Wq; Wk; Wv] ([N, K]); other arguments as dt_rmsnorm_qkv_rope.
+ */
+int dt_qkv_rope(const void* x, int64_t x_row_stride, const void* w, void* y, int64_t y_row_stride, int M, int K,
+                int N, const float* cos_tab, const float* sin_tab, int64_t cos_stride, int cos_rows, int seq_len,
+                int rope_cols, int head_dim, int dtype, void* stream);
+
+/*
  * Residual GEMM of the DT block: y[m, :] += x[m, :] @ w^T in place, in fp32
  * with one rounding of the sum (the residual is the GEMM's accumulator input).
  * Replaces o_proj and its residual add (model_decision_transformer.py:247-248,

@@ -43,6 +43,7 @@ SIGNATURES = {
     "dt_rmsnorm_qkv_rope": (_I, [_P, _L, _P, _P, _L, _I, _I, _I, _F, _P, _P, _L, _I, _I, _I, _I, _I, _P]),
     "dt_rmsnorm_swiglu": (_I, [_P, _L, _P, _P, _L, _I, _I, _I, _F, _I, _P]),
     "dt_gemm_residual": (_I, [_P, _L, _P, _P, _L, _I, _I, _I, _I, _P]),
+    "dt_qkv_rope": (_I, [_P, _L, _P, _P, _L, _I, _I, _I, _P, _P, _L, _I, _I, _I, _I, _I, _P]),
     "dt_frames_to_blocks": (_I, [_P, _P, _L, _I, _I, _I, _P, _I, _P]),
     "dt_rmsnorm": (_I, [_P, _L, _P, _P, _L, _I, _I, _F, _I, _P]),
     "dt_frames_conv1": (_I, [_P, _L, _I, _I, _I, _P, _P, _P, _P, _I, _I, _P]),

@@ -109,6 +109,24 @@ class FastDTAttention(nn.Module):
             object.__setattr__(self, "_fused_key", key)
         return self._fused_w
 
+    def _qkv_rope_ok(self, x: Tensor) -> bool:
+        """The one-GEMM q | k | v + RoPE path: 16-bit x [B, S, H] with a contiguous last
+        dimension, no projection biases, head_dim 32 / 64, sizes multiples of 8."""
+        H = x.shape[-1]
+        return (x.dim() == 3 and x.stride(-1) == 1 and H % 8 == 0 and self.head_dim in (32, 64)
+                and self.q_proj.bias is None and self.k_proj.bias is None and self.v_proj.bias is None
+                and self.q_proj.weight.dtype == x.dtype and x.data_ptr() % 16 == 0
+                and not (torch.is_grad_enabled() and (x.requires_grad or self.q_proj.weight.requires_grad)))
+
+    def _cat_weight(self, dtype: torch.dtype) -> Tensor:
+        """[Wq; Wk; Wv] as one contiguous [N, H] weight (cached while the parameters are unchanged)."""
+        ps = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+        key = tuple((p.data_ptr(), p._version) for p in ps) + (dtype,)
+        if getattr(self, "_cat_key", None) != key:
+            object.__setattr__(self, "_cat_w", torch.cat([p.to(dtype) for p in ps], dim=0).contiguous())
+            object.__setattr__(self, "_cat_key", key)
+        return self._cat_w
+
     def _project(self, x: Tensor, kd: torch.dtype, raw_input: bool, pe: Tuple[Tensor, Tensor]):
         """q, k, v [B, S, H*, D] and whether q / k are already rotated.  With the
         fused norm on 16-bit inputs one kernel does RMSNorm, the three
@@ -124,6 +142,14 @@ class FastDTAttention(nn.Module):
                 qkv = qkv.view(bsz, seq_len, Hq + 2 * Hkv, D)
                 return qkv[:, :, :Hq], qkv[:, :, Hq:Hq + Hkv], qkv[:, :, Hq + Hkv:], True
             x = self._fused_norm(x)  # fp32 models: exact RMSNorm, then the projections
+        if (x.dtype in (torch.bfloat16, torch.float16) and kd == x.dtype and self.rope_rounding == "fp32"
+                and self._qkv_rope_ok(x)):
+            # Drop-in path (x already normalised by the caller's block): one GEMM for
+            # q | k | v with the RoPE of q and k in its epilogue, so the attention
+            # kernels take pre-rotated q / k (their in-kernel RoPE is slower at D = 64).
+            qkv = kernels.qkv_rope(x, self._cat_weight(x.dtype), pe[0], pe[1], (Hq + Hkv) * D, D)
+            qkv = qkv.view(bsz, seq_len, Hq + 2 * Hkv, D)
+            return qkv[:, :, :Hq], qkv[:, :, Hq:Hq + Hkv], qkv[:, :, Hq + Hkv:], True
         xq = self.q_proj(x).view(bsz, seq_len, Hq, D).to(kd)
         xk = self.k_proj(x).view(bsz, seq_len, Hkv, D).to(kd)
         xv = self.v_proj(x).view(bsz, seq_len, Hkv, D).to(kd)

@@ -408,7 +408,7 @@ namespace {
 int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const void* w_fused, void* y,
                      int64_t y_row_stride, int M, int K, int N, float eps, const float* cos_tab, const float* sin_tab,
                      int64_t cos_stride, int cos_rows, int seq_len, int rope_cols, int head_dim, int dtype,
-                     void* stream, int swiglu = 0, int resid = 0) {
+                     void* stream, int swiglu = 0, int resid = 0, int nonorm = 0) {
   // N counts rows of w_fused; with swiglu, y has N / 2 columns.
   if (!x || !w_fused || !y) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
   if (M < 1 || K < 1 || N < 1) return fail(DT_ERR_INVALID, "%s: sizes must be positive", fn);
@@ -446,6 +446,7 @@ int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const 
   p.cs_stride = (int)cos_stride;
   p.swiglu = swiglu;
   p.resid = resid;
+  p.nonorm = nonorm;
   cudaError_t e = dtk::launch_rmsnorm_qkv_sm100(mx, mw, my, p, ncta, g_num_sms[dev],
                                                 static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
@@ -475,6 +476,23 @@ extern "C" int dt_rmsnorm_qkv_rope(const void* x, int64_t x_row_stride, const vo
     return fail(DT_ERR_INVALID, "%s: cos / sin must be 16-byte aligned with row stride >= head_dim, %% 4", fn);
   return rmsnorm_qkv_impl(fn, x, x_row_stride, w_fused, y, y_row_stride, M, K, N, eps, cos_tab, sin_tab, cos_stride,
                           cos_rows, seq_len, rope_cols, head_dim, dtype, stream);
+}
+
+extern "C" int dt_qkv_rope(const void* x, int64_t x_row_stride, const void* w, void* y, int64_t y_row_stride, int M,
+                           int K, int N, const float* cos_tab, const float* sin_tab, int64_t cos_stride, int cos_rows,
+                           int seq_len, int rope_cols, int head_dim, int dtype, void* stream) {
+  const char* fn = "dt_qkv_rope";
+  if (head_dim != 32 && head_dim != 64) return fail(DT_ERR_UNSUPPORTED, "%s: head_dim %d not in {32, 64}", fn, head_dim);
+  if (rope_cols < 0 || rope_cols > N || rope_cols % head_dim)
+    return fail(DT_ERR_INVALID, "%s: rope_cols must be a multiple of head_dim within [0, N]", fn);
+  if (!cos_tab || !sin_tab) return fail(DT_ERR_INVALID, "%s: null cos / sin", fn);
+  if (seq_len < 1 || M % seq_len) return fail(DT_ERR_INVALID, "%s: M must be a multiple of seq_len", fn);
+  if (cos_rows < seq_len) return fail(DT_ERR_INVALID, "%s: cos / sin have %d rows < seq_len %d", fn, cos_rows, seq_len);
+  if (cos_stride < head_dim || cos_stride % 4 || cos_stride > 0x7fffffffLL || !aligned16(cos_tab) ||
+      !aligned16(sin_tab))
+    return fail(DT_ERR_INVALID, "%s: cos / sin must be 16-byte aligned with row stride >= head_dim, %% 4", fn);
+  return rmsnorm_qkv_impl(fn, x, x_row_stride, w, y, y_row_stride, M, K, N, 1.f, cos_tab, sin_tab, cos_stride,
+                          cos_rows, seq_len, rope_cols, head_dim, dtype, stream, 0, 0, 1);
 }
 
 extern "C" int dt_gemm_residual(const void* x, int64_t x_row_stride, const void* w, void* y, int64_t y_row_stride,

@@ -138,6 +138,7 @@ struct RmsQkvParams {
   int rope_cols, head_dim, seq_len, cs_stride;  // rope_cols = 0: no rotation
   int swiglu;  // 1: W rows are 64-row gate / up blocks, y[:, j] = silu(gate_j) * up_j (N / 2 columns)
   int resid;   // 1: y += x @ W^T in place (no RMSNorm scale; y is read as the residual)
+  int nonorm;  // 1: no RMSNorm scale (y = x @ W^T, with the RoPE epilogue when rope_cols > 0)
   float eps;
 };
 

@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ok = __all_sync(0xffffffffu, ok && mbar_wait(acc_full, 0, abort_flag, p.status));
     if (ok) {
       tc_fence_after();
-      const float rs = rsqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / (float)p.K + p.eps);
+      const float rs = p.nonorm ? 1.f : rsqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / (float)p.K + p.eps);
       const int row_g = m0 + r;
       // RoPE table row of this token (rows are [batch, seq_len] flattened).
       const int pos = p.rope_cols > 0 ? row_g % p.seq_len : 0;
@@ -482,7 +482,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         __syncwarp();
       }
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&ss_full[sb], (bc >> 1) & 1, abort_flag, p.status)))) break;
-      const float rs = p.resid ? 1.f : rsqrtf(ss_s[sb * 128 + r] / (float)p.K + p.eps);
+      const float rs = (p.resid || p.nonorm) ? 1.f : rsqrtf(ss_s[sb * 128 + r] / (float)p.K + p.eps);
       const int row_g = rb * 128 + r;
       const int pos = p.rope_cols > 0 ? row_g % p.seq_len : 0;
       const float* crow = p.cos + (size_t)pos * p.cs_stride;

@@ -365,6 +365,33 @@ def rmsnorm_swiglu(x: Tensor, w_fused: Tensor, eps: float, out: Optional[Tensor]
     return out
 
 
+def qkv_rope(x: Tensor, w_cat: Tensor, cos: Tensor, sin: Tensor, rope_cols: int, head_dim: int,
+             out: Optional[Tensor] = None) -> Tensor:
+    """[q | k | v] = x @ w_cat^T with the rotate-half RoPE of the q and k heads
+    (the first rope_cols columns) in the GEMM epilogue, no norm: x [B, S, K]
+    16-bit, w_cat = [Wq; Wk; Wv] [N, K] -> y [B, S, N]; row (b, s) uses table
+    row s of cos / sin."""
+    _require_cuda(x, w_cat, cos, sin, out)
+    if x.dim() != 3:
+        raise ValueError("qkv_rope needs x of shape [B, S, K]")
+    K = x.shape[-1]
+    N = w_cat.shape[0]
+    if w_cat.shape[1] != K or w_cat.dtype != x.dtype or not w_cat.is_contiguous():
+        raise ValueError("w_cat must be a contiguous [N, K] tensor of x's dtype")
+    x2 = x.reshape(-1, K)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (N,), dtype=x.dtype, device=x.device)
+    o2 = out.view(-1, N)
+    cos, sin = _prep_tables(cos, sin)
+    rc = _lib.load().dt_qkv_rope(_ptr(x2), x2.stride(0), _ptr(w_cat), _ptr(o2), o2.stride(0), x2.shape[0], K, N,
+                                 _ptr(cos), _ptr(sin), cos.stride(0), cos.shape[0], x.shape[1], int(rope_cols),
+                                 int(head_dim), _dtype_code(x), _stream_ptr(x.device))
+    _lib.check("dt_qkv_rope", rc)
+    return out
+
+
 def gemm_residual_ok(x: Tensor, w: Tensor, y: Tensor) -> bool:
     """Whether gemm_residual takes these operands (16-bit CUDA tensors, row-major
     views with 16-byte aligned rows, N a multiple of 64)."""

@@ -189,3 +189,55 @@ def test_gemm_residual_rejects_bad_shapes():
     with pytest.raises(ValueError):
         gemm_residual(x, torch.zeros(100, 64, dtype=torch.bfloat16, device="cuda"),
                       torch.zeros(8, 100, dtype=torch.bfloat16, device="cuda"))  # N not a multiple of 64
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,S,K,Hq,Hkv,D", [(3, 48, 256, 8, 2, 32), (2, 300, 768, 12, 4, 64), (5, 21, 128, 4, 1, 32)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_qkv_rope_matches_projections_then_rope(B, S, K, Hq, Hkv, D, dtype):
+    """q | k | v projections with the RoPE of q and k in the GEMM epilogue, no norm
+    (the drop-in module's path on an already-normalised input)."""
+    from oracle import apply_rotary_pos_emb, precompute_freqs_cis
+    from rl_for_mario_b200.kernels import device_status, qkv_rope
+
+    g = torch.Generator().manual_seed(B * S + K + D)
+    x = torch.randn(B, S, K, generator=g).to(dtype)
+    wq, wk, wv = ((torch.randn(h * D, K, generator=g) / K ** 0.5).to(dtype) for h in (Hq, Hkv, Hkv))
+    cos, sin = precompute_freqs_cis(D, S + 3)
+    y = qkv_rope(x.cuda(), torch.cat([wq, wk, wv]).cuda(), cos[:S].cuda(), sin[:S].cuda(), (Hq + Hkv) * D, D)
+    assert device_status() == 0
+    xf = x.float()
+    q = (xf @ wq.float().t()).view(B, S, Hq, D)
+    k = (xf @ wk.float().t()).view(B, S, Hkv, D)
+    v = (xf @ wv.float().t()).view(B, S, Hkv, D)
+    q, k = apply_rotary_pos_emb(q, k, cos[:S], sin[:S])
+    ref = torch.cat([q, k, v], dim=2).reshape(B, S, -1)
+    err = (y.float().cpu() - ref).abs()
+    rel = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10  # one output rounding + fp32 accumulation
+    assert (err <= rel * ref.abs() + 1e-3).all(), f"max err {err.max().item():.3e}"
+
+
+@pytest.mark.gpu
+def test_dropin_module_uses_one_gemm_path_and_matches_unfused():
+    """FastDTAttention on 16-bit inputs takes the one-GEMM q | k | v + RoPE path; its output
+    matches the separate projections + in-kernel RoPE path within bf16 noise, at D = 32 and 64."""
+    from rl_for_mario_b200.attention import FastDTAttention
+    from rl_for_mario_b200.dt_model import rope_tables
+
+    for H, nh, nkv, S in ((256, 8, 2, 60), (768, 12, 4, 200)):
+        class _Cfg:
+            hidden_size, num_attention_heads, num_key_value_heads = H, nh, nkv
+            dropout, flash_attn = 0.0, True
+
+        torch.manual_seed(3)
+        m = FastDTAttention(_Cfg()).cuda().to(torch.bfloat16).eval()
+        with torch.no_grad():  # the one-GEMM path has no autograd: inference only
+            assert m._qkv_rope_ok(torch.zeros(2, S, H, dtype=torch.bfloat16, device="cuda"))
+        x = torch.randn(2, S, H, device="cuda").to(torch.bfloat16)
+        cos, sin = (t.cuda().to(torch.bfloat16) for t in rope_tables(H // nh, S, 1e4))
+        mask = (torch.arange(S, device="cuda")[None] >= torch.tensor([0, S // 3], device="cuda")[:, None]).float()
+        with torch.no_grad():
+            y1, _ = m(x, (cos, sin), attention_mask=mask)
+            m.rope_rounding = "reference"  # separate projections, RoPE inside the attention kernel
+            y2, _ = m(x, (cos, sin), attention_mask=mask)
+        assert (y1.float() - y2.float()).abs().max().item() < 5e-2
