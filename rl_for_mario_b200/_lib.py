@@ -47,6 +47,7 @@ SIGNATURES = {
     "dt_frames_to_blocks": (_I, [_P, _P, _L, _I, _I, _I, _P, _I, _P]),
     "dt_rmsnorm": (_I, [_P, _L, _P, _P, _L, _I, _I, _F, _I, _P]),
     "dt_frames_conv1": (_I, [_P, _L, _I, _I, _I, _P, _P, _P, _P, _I, _I, _P]),
+    "dt_encoder_conv23": (_I, [_P, _L, _P, _P, _P, _P, _P, _P, _I, _P]),
     "dt_frames_conv1_noalloc": (_I, [_P, _L, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
 }
 
