@@ -319,6 +319,7 @@ def run_ours(args):
             line["prefill_long"]["rmsnorm_qkv_kernel"] = bench_rmsnorm_qkv_cfg4(dev, peaks)
             line["prefill_long"]["rmsnorm_swiglu_kernel"] = bench_rmsnorm_swiglu_cfg4(dev, peaks)
             line["prefill_long"]["encoder_conv1_kernel"] = bench_conv1_cfg4(dev, peaks)
+            line["prefill_long"]["encoder_conv23_kernels"] = bench_conv23_cfg4(dev, peaks)
             line["prefill_long"]["residual_gemms"] = bench_gemm_residual_cfg4(dev, peaks)
         line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg, cpu=cpu)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -923,6 +924,61 @@ def bench_conv1_cfg4(dev, peaks, batch=None):
                          "peak_source": peaks["source"]}}
 
 
+def bench_conv23_cfg4(dev, peaks, batch=None):
+    """The state encoder's second and third layers at cfg4's shape (batch x 256
+    frames of the first layer's 32 x 20 x 20 output): dt_encoder_conv23 (two
+    TMA-fed tcgen05 kernels) against cuDNN's fused convolution + bias + ReLU on
+    the same channels-last bf16 tensors."""
+    from rl_for_mario_b200.kernels import device_status, encoder_conv23
+
+    C = PREFILL_LONG_CFG
+    n = (batch or C["batch"]) * C["timesteps"]
+    g = torch.Generator(device=dev).manual_seed(8)
+    cl = torch.channels_last
+    x1 = torch.relu(torch.randn(n, 32, 20, 20, device=dev, generator=g)).to(torch.bfloat16).contiguous(memory_format=cl)
+    w2 = (torch.randn(64, 32, 4, 4, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    b2 = (torch.randn(64, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    w3 = (torch.randn(64, 64, 3, 3, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    b3 = (torch.randn(64, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    w2c, w3c = w2.contiguous(memory_format=cl), w3.contiguous(memory_format=cl)
+
+    def ours():
+        return encoder_conv23(x1, w2, b2, w3, b3)
+
+    def cudnn():
+        y2 = torch.cudnn_convolution_relu(x1, w2c, b2, (2, 2), (0, 0), (1, 1), 1)
+        return y2, torch.cudnn_convolution_relu(y2, w3c, b3, (1, 1), (0, 0), (1, 1), 1)
+
+    res = {}
+    for name, fn in (("ours", ours), ("cudnn", cudnn)):
+        for _ in range(3):
+            out = fn()
+        del out
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            out = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        del out
+        res[name] = e0.elapsed_time(e1) / reps
+    if device_status() != 0:
+        raise SystemExit("device status error in the encoder-conv benchmark")
+    flops = 2 * n * (81 * 64 * 512 + 49 * 64 * 576)
+    byts = n * (32 * 400 + 2 * 64 * 81 + 64 * 49) * 2  # x1 in, y2 out and in again, y3 out
+    ms = res["ours"]
+    gbs = byts / (ms * 1e-3) / 1e9
+    del x1
+    torch.cuda.empty_cache()
+    return {"kernel": "encoder_conv_kernel<2>, <3>", "frames": n, "ms": ms, "cudnn_ms": res["cudnn"],
+            "tflops": flops / (ms * 1e-3) / 1e12,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": byts,
+                         "peak_source": peaks["source"]}}
+
+
 def bench_rollout_cfg5(dev, world, rank, pg, cpu: bool = False):
     """8,192 environments per GPU, 64 cached steps, CNN on synthetic frames, all-gather of logits.
 
@@ -1026,8 +1082,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode / rollout sub-benchmarks")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
-    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "conv1", "rollout",
-                                       "gemm_residual"],
+    ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "conv1", "conv23",
+                                       "rollout", "gemm_residual"],
                     default=None,
                     help="run one sub-benchmark alone and print its JSON (profiling)")
     ap.add_argument("--long-batch", type=int, default=None,
@@ -1045,6 +1101,8 @@ def main():
             emit({"only": "rmsnorm_qkv", **bench_rmsnorm_qkv_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "conv1":
             emit({"only": "conv1", **bench_conv1_cfg4(dev, _peaks(), batch=args.long_batch)})
+        elif args.only == "conv23":
+            emit({"only": "conv23", **bench_conv23_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "gemm_residual":
             emit({"only": "gemm_residual", **bench_gemm_residual_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "rollout":

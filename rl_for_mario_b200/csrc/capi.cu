@@ -597,8 +597,9 @@ extern "C" int dt_encoder_conv23(const void* x1, int64_t N, const void* w2, cons
     if ((rc = encode_nd(&m2, y2, bf16, 4, dims, strides, box, "y2"))) return rc;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = dtk::launch_encoder_conv_sm100(2, m1, w2, b2, y2, N, bf16, g_num_sms[dev], status, st);
-  if (e == cudaSuccess) e = dtk::launch_encoder_conv_sm100(3, m2, w3, b3, y3, N, bf16, g_num_sms[dev], status, st);
+  cudaError_t e = dtk::launch_encoder_conv_sm100(2, m1, x1, w2, b2, y2, N, bf16, g_num_sms[dev], status, st);
+  if (e == cudaSuccess)
+    e = dtk::launch_encoder_conv_sm100(3, m2, y2, w3, b3, y3, N, bf16, g_num_sms[dev], status, st);
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
   return DT_OK;
 }

@@ -22,13 +22,16 @@
 //    columns, 7 rows, 2 frames] gives 98 rows (two frames' 49 positions).  9
 //    atoms, K = 576.
 //
-// Warps: 0 TMA producer (ring of 128-row stages), 1 TMEM owner + MMA issuer
+// Warps: 0 TMA producer (ring of stages; each unit's input bytes are also
+// pulled into L2 two units ahead with one bulk prefetch), 1 TMEM owner + MMA issuer
 // (M = 128, N = 64, K = 16 steps; two 64-column accumulators in TMEM), 2-5
 // epilogue (bias + ReLU in fp32, one rounding, 128 bytes of channels-last
 // output per position).  The weights of all atoms stay in shared memory,
-// staged once per CTA from the reference's [64, Cin, k, k] layout.  Rows of a
-// stage past the box (tile rows without a position) hold stale bytes; their
-// accumulator rows are never stored.
+// staged once per CTA from the reference's [64, Cin, k, k] layout.  Stages are
+// packed at the box size (81 or 98 rows, rounded up to 1 KB) so that more copies
+// are in flight; the MMA still reads 128 rows from a stage, so its rows past the
+// box read the next stage (or the weights behind the ring): those accumulator
+// rows belong to no position and are never stored.
 #include "dt_common.cuh"
 #include "dt_internal.h"
 
@@ -37,8 +40,6 @@ namespace dtk {
 namespace {
 
 constexpr int kCvThreads = 192;
-constexpr int kCvStages = 6;
-constexpr int kCvStage = 128 * 128;  // one atom of a 128-row tile
 constexpr int kCvBAtom = 64 * 128;   // one atom of the 64-row weight tile
 
 template <int LAYER>
@@ -47,6 +48,8 @@ template <>
 struct Cv<2> {
   static constexpr int NATOM = 8, FRAMES = 1, P = 81, CIN = 32, KS = 4;
   static constexpr int ROWS = FRAMES * P;
+  static constexpr int IN_BYTES = 20 * 20 * 32 * 2;  // one frame of input
+  static constexpr int STAGES = 14;
   // Weight value of atom a, output channel o, K-value e (o, c, ky, kx of the reference layout).
   __device__ static int w_index(int a, int o, int e) {
     const int dy = a >> 2, dx = (a >> 1) & 1, sy = a & 1, sx = e >> 5, c = e & 31;
@@ -57,6 +60,8 @@ template <>
 struct Cv<3> {
   static constexpr int NATOM = 9, FRAMES = 2, P = 49, CIN = 64, KS = 3;
   static constexpr int ROWS = FRAMES * P;
+  static constexpr int IN_BYTES = 9 * 9 * 64 * 2;
+  static constexpr int STAGES = 11;
   __device__ static int w_index(int a, int o, int e) {
     const int ky = a / 3, kx = a % 3;
     return ((o * CIN + e) * KS + ky) * KS + kx;
@@ -65,12 +70,15 @@ struct Cv<3> {
 
 template <int LAYER>
 struct CvShape {
+  static constexpr int STAGES = Cv<LAYER>::STAGES;
+  static constexpr int STAGE = (Cv<LAYER>::ROWS * 128 + 1023) & ~1023;  // box bytes, 1 KB aligned
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = kCvStages * kCvStage;
+  static constexpr int OFF_B = STAGES * STAGE;  // the last stage's 128-row read ends inside B
+  static_assert(OFF_B + kCvBAtom * Cv<LAYER>::NATOM >= (STAGES - 1) * STAGE + 128 * 128, "MMA overhang");
   static constexpr int OFF_BIAS = OFF_B + Cv<LAYER>::NATOM * kCvBAtom;
   static constexpr int OFF_BAR = OFF_BIAS + 64 * 4;
   // full[S], empty[S], acc_full[2], acc_empty[2], drain
-  static constexpr int NBAR = 2 * kCvStages + 5;
+  static constexpr int NBAR = 2 * STAGES + 5;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -99,8 +107,9 @@ __device__ __forceinline__ void cv_load(uint8_t* dst, const CUtensorMap* map, ui
 
 template <int LAYER, bool BF16>
 __global__ void __launch_bounds__(kCvThreads, 1)
-    encoder_conv_kernel(const __grid_constant__ CUtensorMap tmX, const uint16_t* __restrict__ w,
-                        const float* __restrict__ bias, uint16_t* __restrict__ y, long long n_frames, int* status) {
+    encoder_conv_kernel(const __grid_constant__ CUtensorMap tmX, const uint8_t* __restrict__ x,
+                        const uint16_t* __restrict__ w, const float* __restrict__ bias, uint16_t* __restrict__ y,
+                        long long n_frames, int* status) {
   using L = Cv<LAYER>;
   using SH = CvShape<LAYER>;
   using E = Elem<BF16>;
@@ -109,9 +118,10 @@ __global__ void __launch_bounds__(kCvThreads, 1)
   uint8_t* a_s = smem + SH::OFF_A;
   uint8_t* b_s = smem + SH::OFF_B;
   float* bias_s = reinterpret_cast<float*>(smem + SH::OFF_BIAS);
+  constexpr int NST = SH::STAGES;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + SH::OFF_BAR);
-  uint64_t* empty = full + kCvStages;
-  uint64_t* acc_full = empty + kCvStages;
+  uint64_t* empty = full + NST;
+  uint64_t* acc_full = empty + NST;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
@@ -121,7 +131,7 @@ __global__ void __launch_bounds__(kCvThreads, 1)
   const long long units = (n_frames + L::FRAMES - 1) / L::FRAMES;
 
   if (tid == 0) {
-    for (int s = 0; s < kCvStages; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -162,17 +172,28 @@ __global__ void __launch_bounds__(kCvThreads, 1)
       prefetch_tmap(&tmX);
       int cnt = 0;
       bool ok = true;
-      for (long long u = blockIdx.x; u < units && ok; u += gridDim.x)
+      // The input bytes of unit v (FRAMES whole frames, contiguous) into L2.
+      auto prefetch_unit = [&](long long v) {
+        if (v >= units) return;
+        const long long f0 = v * L::FRAMES;
+        const long long nf = n_frames - f0 < L::FRAMES ? n_frames - f0 : L::FRAMES;
+        bulk_prefetch_l2(x + f0 * L::IN_BYTES, (uint32_t)(nf * L::IN_BYTES));
+      };
+      prefetch_unit(blockIdx.x);
+      prefetch_unit(blockIdx.x + (long long)gridDim.x);
+      for (long long u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        prefetch_unit(u + 2LL * gridDim.x);
         for (int a = 0; a < L::NATOM; ++a, ++cnt) {
-          const int s = cnt % kCvStages;
-          if (!(ok = mbar_wait(&empty[s], ((cnt / kCvStages) & 1) ^ 1, abort_flag, status))) break;
+          const int s = cnt % NST;
+          if (!(ok = mbar_wait(&empty[s], ((cnt / NST) & 1) ^ 1, abort_flag, status))) break;
           mbar_arrive_expect_tx(&full[s], (uint32_t)(L::ROWS * 128));
-          cv_load<LAYER>(a_s + s * kCvStage, &tmX, &full[s], a, (int)u);
+          cv_load<LAYER>(a_s + s * SH::STAGE, &tmX, &full[s], a, (int)u);
         }
+      }
       if (!ok) {
         // Let every copy already issued land before the CTA can exit.
-        for (int s = 0; s < kCvStages; ++s) {
-          const int uses = cnt / kCvStages + (s < cnt % kCvStages ? 1 : 0);
+        for (int s = 0; s < NST; ++s) {
+          const int uses = cnt / NST + (s < cnt % NST ? 1 : 0);
           if (uses > 0) mbar_wait(&full[s], (uses - 1) & 1, nullptr, nullptr);
         }
       }
@@ -187,10 +208,10 @@ __global__ void __launch_bounds__(kCvThreads, 1)
         const int buf = i & 1;
         if (!(ok = mbar_wait(&acc_empty[buf], ((i >> 1) & 1) ^ 1, abort_flag, status))) break;
         for (int a = 0; a < L::NATOM; ++a, ++cnt) {
-          const int s = cnt % kCvStages;
-          if (!(ok = mbar_wait(&full[s], (cnt / kCvStages) & 1, abort_flag, status))) break;
+          const int s = cnt % NST;
+          if (!(ok = mbar_wait(&full[s], (cnt / NST) & 1, abort_flag, status))) break;
           tc_fence_after();
-          const uint64_t ad = umma_smem_desc(smem_u32(a_s + s * kCvStage), 16, 1024, kSw128);
+          const uint64_t ad = umma_smem_desc(smem_u32(a_s + s * SH::STAGE), 16, 1024, kSw128);
           const uint64_t bd = umma_smem_desc(smem_u32(b_s + a * kCvBAtom), 16, 1024, kSw128);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)  // 32 bytes per K step inside the 128-byte atom
@@ -246,8 +267,9 @@ __global__ void __launch_bounds__(kCvThreads, 1)
 
 }  // namespace
 
-cudaError_t launch_encoder_conv_sm100(int layer, const CUtensorMap& x, const void* w, const float* bias, void* y,
-                                      long long n_frames, bool bf16, int num_sms, int* status, cudaStream_t st) {
+cudaError_t launch_encoder_conv_sm100(int layer, const CUtensorMap& x, const void* xp, const void* w,
+                                      const float* bias, void* y, long long n_frames, bool bf16, int num_sms,
+                                      int* status, cudaStream_t st) {
   const long long units = layer == 2 ? n_frames : (n_frames + 1) / 2;
   const unsigned grid = (unsigned)(units < num_sms ? units : num_sms);
   const void* fn;
@@ -263,18 +285,19 @@ cudaError_t launch_encoder_conv_sm100(int layer, const CUtensorMap& x, const voi
   }
   cudaError_t e = smem_limit_once(fn, smem);
   if (e != cudaSuccess) return e;
+  const uint8_t* xb = static_cast<const uint8_t*>(xp);
   const uint16_t* wp = static_cast<const uint16_t*>(w);
   uint16_t* yp = static_cast<uint16_t*>(y);
   if (layer == 2) {
     if (bf16)
-      encoder_conv_kernel<2, true><<<grid, kCvThreads, smem, st>>>(x, wp, bias, yp, n_frames, status);
+      encoder_conv_kernel<2, true><<<grid, kCvThreads, smem, st>>>(x, xb, wp, bias, yp, n_frames, status);
     else
-      encoder_conv_kernel<2, false><<<grid, kCvThreads, smem, st>>>(x, wp, bias, yp, n_frames, status);
+      encoder_conv_kernel<2, false><<<grid, kCvThreads, smem, st>>>(x, xb, wp, bias, yp, n_frames, status);
   } else {
     if (bf16)
-      encoder_conv_kernel<3, true><<<grid, kCvThreads, smem, st>>>(x, wp, bias, yp, n_frames, status);
+      encoder_conv_kernel<3, true><<<grid, kCvThreads, smem, st>>>(x, xb, wp, bias, yp, n_frames, status);
     else
-      encoder_conv_kernel<3, false><<<grid, kCvThreads, smem, st>>>(x, wp, bias, yp, n_frames, status);
+      encoder_conv_kernel<3, false><<<grid, kCvThreads, smem, st>>>(x, xb, wp, bias, yp, n_frames, status);
   }
   return cudaGetLastError();
 }

@@ -367,6 +367,22 @@ __device__ __forceinline__ void tmem_wait_ld3(uint32_t (&a)[32], uint32_t (&b)[3
                : "memory");
 }
 
+// Named barrier over `count` threads that also ANDs a predicate across them
+// (bar.red.and): every participant gets true only if all passed true.  Memory
+// accesses before the barrier are visible to all participants after it.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %3, 0;\n\t"
+      "bar.red.and.pred p, %1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(count), "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
+}
+
 // Named barrier over `count` threads (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

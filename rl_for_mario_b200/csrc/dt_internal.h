@@ -162,9 +162,10 @@ cudaError_t launch_frames_to_blocks_sm100(const void* frames, void* out, long lo
 // round_input: frames / 255 rounded to the output dtype before the
 // convolution (the reference's 16-bit rounding) instead of exact pixels.
 // The state encoder's second (layer 2) or third (layer 3) convolution + ReLU;
-// x is the layer's input tensor map (encoder_conv23 in capi.cu).
-cudaError_t launch_encoder_conv_sm100(int layer, const CUtensorMap& x, const void* w, const float* bias, void* y,
-                                      long long n_frames, bool bf16, int num_sms, int* status, cudaStream_t st);
+// x is the layer's input tensor map (encoder_conv23 in capi.cu), xp its base.
+cudaError_t launch_encoder_conv_sm100(int layer, const CUtensorMap& x, const void* xp, const void* w,
+                                      const float* bias, void* y, long long n_frames, bool bf16, int num_sms,
+                                      int* status, cudaStream_t st);
 
 cudaError_t launch_frames_conv1_sm100(const void* frames, long long N, int H, int W, const void* w,
                                       const float* bias, unsigned int* frame_max, void* y, bool bf16,

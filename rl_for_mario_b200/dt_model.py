@@ -243,8 +243,13 @@ class MarioStateEncoder(nn.Module):
                 x = torch.empty(s.shape, dtype=dt, device=s.device, memory_format=cl)
                 x.copy_(s)
                 x = self._conv_relu(x, w0.contiguous(memory_format=cl), conv0.bias, conv0.stride)
-        x = self._conv_relu(x, conv1.weight.contiguous(memory_format=cl), conv1.bias, conv1.stride)
-        x = self._conv_relu(x, conv2.weight.contiguous(memory_format=cl), conv2.bias, conv2.stride)
+        if self._tc_conv23 and self._conv23_shapes(x, conv1, conv2):
+            # Layers 2 and 3 (:322-325) on the tensor cores, their A tiles single TMA
+            # copies of the channels-last activations.
+            _, x = kernels.encoder_conv23(x, conv1.weight, conv1.bias, conv2.weight, conv2.bias)
+        else:
+            x = self._conv_relu(x, conv1.weight.contiguous(memory_format=cl), conv1.bias, conv1.stride)
+            x = self._conv_relu(x, conv2.weight.contiguous(memory_format=cl), conv2.bias, conv2.stride)
         if x.dim() == 4 and x.is_contiguous(memory_format=cl):
             # The reference flattens in (C, H, W) order; channels-last
             # activations are (H, W, C) in memory, so the Linear's input
@@ -255,6 +260,23 @@ class MarioStateEncoder(nn.Module):
         return lin(x.contiguous().flatten(1)).reshape(B, T, -1)
 
     _fused_conv = True
+    # True: layers 2 and 3 on the library's tensor-core kernel (dt_encoder_conv23) when
+    # the shapes are the Nature-DQN ones on 84 x 84 frames.  Off by default: its A
+    # tiles are TMA copies that re-read every input pixel once per kernel offset
+    # using it, and that copy volume makes it slower than cuDNN's fused
+    # convolution (7.0 vs 4.8 ms at 262,144 frames, 0.28 vs 0.17 ms at 8,192).
+    _tc_conv23 = False
+
+    @staticmethod
+    def _conv23_shapes(x: Tensor, c2: nn.Conv2d, c3: nn.Conv2d) -> bool:
+        return (x.is_cuda and x.dim() == 4 and tuple(x.shape[1:]) == (32, 20, 20)
+                and x.dtype in (torch.bfloat16, torch.float16) and x.is_contiguous(memory_format=torch.channels_last)
+                and x.data_ptr() % 16 == 0
+                and c2.in_channels == 32 and c2.out_channels == 64 and c2.kernel_size == (4, 4)
+                and c2.stride == (2, 2) and c2.padding == (0, 0) and c2.bias is not None
+                and c3.in_channels == 64 and c3.out_channels == 64 and c3.kernel_size == (3, 3)
+                and c3.stride == (1, 1) and c3.padding == (0, 0) and c3.bias is not None
+                and c2.weight.dtype == x.dtype and c3.weight.dtype == x.dtype)
     # True: frames / 255 rounded to the model dtype before the first convolution,
     # as the reference's 16-bit model does (:338); False: exact pixels, 1/255 on
     # the fp32 accumulator.

@@ -84,3 +84,24 @@ def test_encoder_conv23_rejects_bad_arguments():
         encoder_conv23(x1, w2.float(), b2, w3, b3)
     with pytest.raises(ValueError):
         encoder_conv23(x1, w3, b2, w2, b3)
+
+
+@pytest.mark.gpu
+def test_encoder_conv23_in_the_model_encoder():
+    """The DT's state encoder with layers 2 and 3 routed through dt_encoder_conv23
+    equals its default path (cuDNN's fused convolution) within the 16-bit bound."""
+    from rl_for_mario_b200.dt_model import MarioStateEncoder
+
+    torch.manual_seed(0)
+    enc = MarioStateEncoder((4, 84, 84), 256).cuda().to(torch.bfloat16).eval()
+    g = torch.Generator(device="cuda").manual_seed(2)
+    frames = torch.randint(0, 256, (3, 5, 4, 84, 84), device="cuda", generator=g, dtype=torch.uint8)
+    with torch.no_grad():
+        base = enc(frames)
+        MarioStateEncoder._tc_conv23 = True
+        try:
+            ours = enc(frames)
+        finally:
+            MarioStateEncoder._tc_conv23 = False
+    err = (ours.float() - base.float()).abs()
+    assert (err - 2e-2 - 2.0 ** -7 * base.float().abs()).max().item() <= 0, f"max err {err.max().item():.3e}"
