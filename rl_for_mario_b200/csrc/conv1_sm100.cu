@@ -477,11 +477,12 @@ __global__ void __launch_bounds__(kB1Threads, 1)
             if (lane == 0) mbar_arrive(&acc_empty[ab]);
           }
           // Row r + 1 of the dx = 1 accumulator: the next lane, or for lane 31 the next
-          // quarter's lane 0 through shared memory.
+          // quarter's lane 0 through shared memory (16-byte accesses).
           float* xw = xch_s + ((g * 2 + (j & 1)) * 4 + wq) * kC1N;
           if (lane == 0 && okw) {
 #pragma unroll
-            for (int c = 0; c < kC1N; ++c) xw[c] = v1[c];
+            for (int c = 0; c < kC1N; c += 4)
+              *reinterpret_cast<float4*>(xw + c) = make_float4(v1[c], v1[c + 1], v1[c + 2], v1[c + 3]);
           }
           // All four epilogue warps pass here every tile; the barrier also agrees on
           // their waits' outcomes, so they leave together.
@@ -491,20 +492,27 @@ __global__ void __launch_bounds__(kB1Threads, 1)
           const int oyl = r / 24, ox = r - oyl * 24;
           const bool valid = r < 120 && ox < 20;
 #pragma unroll
-          for (int c = 0; c < kC1N; ++c) {
-            const float nb = __shfl_down_sync(0xffffffffu, v1[c], 1);
-            v0[c] += lane == 31 ? xn[c] : nb;
+          for (int c = 0; c < kC1N; ++c) v1[c] = __shfl_down_sync(0xffffffffu, v1[c], 1);
+          if (lane == 31) {
+#pragma unroll
+            for (int c = 0; c < kC1N; c += 4) {
+              const float4 x4 = *reinterpret_cast<const float4*>(xn + c);
+              v1[c] = x4.x, v1[c + 1] = x4.y, v1[c + 2] = x4.z, v1[c + 3] = x4.w;
+            }
           }
           if (valid) {
             uint4* dst = reinterpret_cast<uint4*>(y + ((size_t)(n * 20 + 10 * h + 5 * t + oyl) * 20 + ox) * kC1N);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
+              const float4 b0 = *reinterpret_cast<const float4*>(bias_s + q * 8);
+              const float4 b1 = *reinterpret_cast<const float4*>(bias_s + q * 8 + 4);
+              const float bq[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
               uint32_t o[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const int jj = q * 8 + 2 * e;
-                o[e] = E::from_f2(fmaxf(fmaf(v0[jj], s, bias_s[jj]), 0.f),
-                                  fmaxf(fmaf(v0[jj + 1], s, bias_s[jj + 1]), 0.f));
+                o[e] = E::from_f2(fmaxf(fmaf(v0[jj] + v1[jj], s, bq[2 * e]), 0.f),
+                                  fmaxf(fmaf(v0[jj + 1] + v1[jj + 1], s, bq[2 * e + 1]), 0.f));
               }
               dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
             }
@@ -524,9 +532,11 @@ __global__ void __launch_bounds__(kB1Threads, 1)
         const int hb = k & 1;
         if (!(ok = mbar_wait(&arr_empty[hb], ((k >> 1) & 1) ^ 1, abort_flag, status))) break;
         uint8_t* arr = arr_s + hb * SH::ARR;
-        // items: (local block row 0..10, block column 0..20, channel 0..3)
+        // items: (channel 0..3, local block row 0..10, block column 0..20), the column
+        // fastest: a warp's 32-bit loads then cover consecutive words of a frame row
+        // (and the next block row's, 20 banks further), nearly free of bank conflicts.
         for (int it = ct; it < 11 * 21 * 4; it += kB1Conv * 32) {
-          const int c = it & 3, rest = it >> 2, bx = rest % 21, byl = rest / 21;
+          const int bx = it % 21, rest = it / 21, byl = rest % 11, c = rest / 11;
           const int by = 10 * h + byl;
           const uint8_t* src = raw + c * 7056 + (4 * by) * 84 + 4 * bx;
           uint32_t px[4];
