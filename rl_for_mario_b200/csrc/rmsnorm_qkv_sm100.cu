@@ -329,7 +329,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
   if (tid == 0) {
     for (int s = 0; s < kPStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 5);  // MMA commit + one arrival per sum-of-squares warp
+      // MMA commit + one arrival per sum-of-squares warp; without a norm (resid /
+      // nonorm) those warps read no stage, so the commit alone frees it.
+      mbar_init(&empty[s], (p.resid || p.nonorm) ? 1 : 5);
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(&acc_full[j], 1);
@@ -684,6 +686,17 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     const int rr = (warp - 6) * 32 + lane;  // row of the block
     int cnt = 0, bc = 0;
     bool ok = true;
+    if (p.resid || p.nonorm) {
+      // No norm: only the per-block handshake the epilogue waits on (the value is unused).
+      for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++bc) {
+        const int sb = bc & 1;
+        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&ss_empty[sb], ((bc >> 1) & 1) ^ 1, abort_flag, p.status))))
+          break;
+        ss_s[sb * 128 + rr] = 0.f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ss_full[sb]);
+      }
+    } else
     for (int rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++bc) {
       const int sb = bc & 1;
       float ss0 = 0.f, ss1 = 0.f;
@@ -692,7 +705,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
           const int s = cnt % kPStages;
           if (!(ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (cnt / kPStages) & 1, abort_flag, p.status))))
             break;
-          if (ct == 0 && !p.resid) {  // (resid mode applies no norm: only the stage releases)
+          if (ct == 0) {
             // Row rr of the chunk is the RB bytes at rr * RB (the swizzle
             // permutes 16-byte pieces inside the row); start each lane at a
             // different piece to spread a quarter warp over the banks.
