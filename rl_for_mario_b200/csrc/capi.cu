@@ -439,6 +439,21 @@ int rmsnorm_qkv_impl(const char* fn, const void* x, int64_t x_row_stride, const 
   if (rc) return rc;
   if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
   const bool bf16 = dtype == DT_DTYPE_BF16;
+  if (resid && N % 256 == 0 && g_num_sms[dev] >= 2 &&
+      (long long)((M + 255) / 256) * (N / 256) >= 2LL * g_num_sms[dev]) {
+    // Residual GEMM on CTA pairs (256 x 256 tiles, each CTA stages half of the
+    // tile's x rows and half of its W rows per K chunk), for problems with at
+    // least four tiles per pair; smaller ones (a rollout step's 24,576 rows) run
+    // faster on the single-CTA kernel below, measured.
+    CUtensorMap px, pw, py;
+    if ((rc = encode_2d(&px, x, bf16, (uint64_t)K, (uint64_t)M, (uint64_t)x_row_stride, 64, 128, "x", 128))) return rc;
+    if ((rc = encode_2d(&pw, w_fused, bf16, (uint64_t)K, (uint64_t)N, (uint64_t)K, 64, 128, "w", 128))) return rc;
+    if ((rc = encode_2d(&py, y, bf16, (uint64_t)N, (uint64_t)M, (uint64_t)y_row_stride, 64, 32, "y", 128))) return rc;
+    cudaError_t e = dtk::launch_gemm_residual_pair_sm100(px, pw, py, M, N, K, bf16, g_num_sms[dev], status,
+                                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
+    return DT_OK;
+  }
   // 0: persistent kernel, 256-column tiles (the only one with the SwiGLU epilogue)
   const int ncta = (swiglu || resid) ? 0 : dtk::rmsnorm_qkv_ncta(N);
   const int nsub = ncta == 0 ? 256 : (ncta <= 256 ? ncta : ncta / 2);

@@ -161,6 +161,11 @@ cudaError_t launch_frames_to_blocks_sm100(const void* frames, void* out, long lo
                                           unsigned int* frame_max, cudaStream_t st);
 // round_input: frames / 255 rounded to the output dtype before the
 // convolution (the reference's 16-bit rounding) instead of exact pixels.
+// Residual GEMM y += x W^T on CTA pairs (N a multiple of 256; x, w maps with
+// 64 x 128 boxes, y map with 64 x 32 boxes, all 128-byte swizzle).
+cudaError_t launch_gemm_residual_pair_sm100(const CUtensorMap& x, const CUtensorMap& w, const CUtensorMap& y, int M,
+                                            int N, int K, bool bf16, int num_sms, int* status, cudaStream_t st);
+
 // The state encoder's second (layer 2) or third (layer 3) convolution + ReLU;
 // x is the layer's input tensor map (encoder_conv23 in capi.cu), xp its base.
 cudaError_t launch_encoder_conv_sm100(int layer, const CUtensorMap& x, const void* xp, const void* w,

@@ -160,11 +160,15 @@ def test_rmsnorm_swiglu_rejects_bad_widths():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("M,K,N", [(300, 256, 256), (1000, 768, 768), (777, 2048, 768), (130, 704, 256),
-                                   (5000, 256, 256)])
+                                   (5000, 256, 256), (3000, 512, 512), (65536, 768, 768), (65536, 2048, 768),
+                                   (70000, 256, 512)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_gemm_residual_matches_fp32(M, K, N, dtype):
     """y += x @ w^T in place (the block's o_proj / down_proj with the residual add):
-    within one output rounding of the fp32 result."""
+    within one output rounding of the fp32 result.  N a multiple of 256 with at least
+    four 256 x 256 tiles per CTA pair runs on CTA pairs (the three large cases: each
+    pair gets about ten tiles, so its stage ring and both accumulators wrap; 70,000
+    rows end in a partial 256-row block); the others run on the single-CTA kernel."""
     from rl_for_mario_b200.kernels import device_status, gemm_residual
 
     g = torch.Generator(device="cuda").manual_seed(M + K + N)
