@@ -1088,6 +1088,8 @@ def main():
                     help="run one sub-benchmark alone and print its JSON (profiling)")
     ap.add_argument("--long-batch", type=int, default=None,
                     help="with --only prefill_long: batch of the attention-kernel case, model forward skipped")
+    ap.add_argument("--with-model", action="store_true",
+                    help="with --only prefill_long --long-batch: run the model forward at that batch too")
     args = ap.parse_args()
     if args.only:
         if not torch.cuda.is_available():
@@ -1111,7 +1113,7 @@ def main():
             emit({"only": "rmsnorm_swiglu", **bench_rmsnorm_swiglu_cfg4(dev, _peaks(), batch=args.long_batch)})
         else:
             emit({"only": "prefill_long", **bench_prefill_cfg4(dev, _peaks(), batch=args.long_batch,
-                                                                model=args.long_batch is None)})
+                                                                model=args.long_batch is None or args.with_model)})
         return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

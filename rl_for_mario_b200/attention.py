@@ -230,9 +230,13 @@ class FastDTAttention(nn.Module):
             o2 = out.reshape(-1, out.shape[-1])
             if not (residual_inplace and r2.data_ptr() == residual.data_ptr() and r2.is_contiguous()):
                 r2 = r2.clone()  # the caller keeps its residual: accumulate into a copy
-            # o_proj with the residual as the GEMM's accumulator input.  cuBLAS's
-            # addmm_ here: measured faster than dt_gemm_residual at these shapes.
-            r2.addmm_(o2, w.t())
+            # o_proj with the residual as the GEMM's accumulator input: the
+            # library's CTA-pair GEMM at prefill sizes, cuBLAS's addmm_ for a
+            # rollout step's small, latency-bound GEMM (measured faster there).
+            if kernels.gemm_residual_on_pairs(o2, w, r2):
+                kernels.gemm_residual(o2, w, r2)
+            else:
+                r2.addmm_(o2, w.t())
             return r2.view(residual.shape), past_kv
         return residual + self.resid_dropout(self.o_proj(out)), past_kv
 

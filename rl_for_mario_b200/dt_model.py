@@ -8,9 +8,9 @@ so a reference state_dict loads unchanged (checkpoint compatibility).  With
 ``fuse_norms()`` a block runs as: RMSNorm + Q/K/V + RoPE kernel, attention
 kernel, o_proj GEMM with the residual as accumulator input, RMSNorm + gate/up
 + SwiGLU kernel, down_proj GEMM with the residual (the two residual GEMMs on
-cuBLAS, which measures faster than the library's dt_gemm_residual at these
-shapes); the rest (CNN encoder past its first layer, embeddings, final norm,
-heads) runs as PyTorch on the GPU.
+the library's CTA-pair GEMM at prefill sizes, on cuBLAS for a rollout step's
+small, latency-bound ones); the rest (CNN encoder past its first layer,
+embeddings, final norm, heads) runs as PyTorch on the GPU.
 """
 from __future__ import annotations
 
@@ -151,9 +151,14 @@ class DTBlock(nn.Module):
             if self._fused_mlp_ok(h):
                 a = kernels.rmsnorm_swiglu(h, self._swiglu_weight(h.dtype), self.post_attention_layernorm.eps)
                 # h is this block's own intermediate: the down projection
-                # accumulates into it in place (no copy of the residual).
-                # (cuBLAS's addmm_: measured faster than dt_gemm_residual here)
-                h.view(-1, h.shape[-1]).addmm_(a.reshape(-1, a.shape[-1]), self.mlp.down_proj.weight.t())
+                # accumulates into it in place (no copy of the residual), on the
+                # library's CTA-pair GEMM at prefill sizes; a rollout step's small
+                # GEMM is latency-bound and faster on cuBLAS's addmm_ (measured).
+                h2, a2, wd = h.view(-1, h.shape[-1]), a.reshape(-1, a.shape[-1]), self.mlp.down_proj.weight
+                if kernels.gemm_residual_on_pairs(a2, wd, h2):
+                    kernels.gemm_residual(a2, wd, h2)
+                else:
+                    h2.addmm_(a2, wd.t())
             else:
                 h = h + self.mlp(self.post_attention_layernorm(h))
             return h, present

@@ -433,6 +433,24 @@ def gemm_residual_ok(x: Tensor, w: Tensor, y: Tensor) -> bool:
     return x.shape[0] == y.shape[0]
 
 
+_NUM_SMS: dict = {}
+
+
+def gemm_residual_on_pairs(x: Tensor, w: Tensor, y: Tensor) -> bool:
+    """Whether gemm_residual runs these operands on CTA pairs: N a multiple of 256 and
+    at least four 256 x 256 tiles per pair of SMs, the sizes at which it matches
+    cuBLAS's addmm (cfg4's o_proj / down_proj, measured).  Smaller, latency-bound
+    problems (a rollout step's GEMMs) fall to the single-CTA kernel, which is slower
+    than cuBLAS there."""
+    if not gemm_residual_ok(x, w, y):
+        return False
+    M, N = y.shape
+    dev = y.device.index if y.device.index is not None else torch.cuda.current_device()
+    if dev not in _NUM_SMS:
+        _NUM_SMS[dev] = torch.cuda.get_device_properties(dev).multi_processor_count
+    return N % 256 == 0 and ((M + 255) // 256) * (N // 256) >= 2 * _NUM_SMS[dev]
+
+
 def gemm_residual(x: Tensor, w: Tensor, y: Tensor) -> Tensor:
     """y += x @ w^T in place (fp32 accumulation, one rounding of the sum): the
     block's o_proj / down_proj with its residual add.  x [M, K], w [N, K],
