@@ -245,3 +245,72 @@ def test_dropin_module_uses_one_gemm_path_and_matches_unfused():
             m.rope_rounding = "reference"  # separate projections, RoPE inside the attention kernel
             y2, _ = m(x, (cos, sin), attention_mask=mask)
         assert (y1.float() - y2.float()).abs().max().item() < 5e-2
+
+
+# Whole-size rows (38,227 rows: an odd number of 128-row blocks, the last one
+# mostly past the end; 65,536 rows: cfg4's per-layer batch of 128 x 512 rows
+# over the persistent CTAs, several blocks each).  A row's result depends on its
+# block only through its row index modulo 32 (the lane that sums its squares
+# starts at a lane-dependent 16-byte piece), so the first 16 sequences and the
+# last ones from a sequence whose first row is a multiple of 32, run alone, must
+# come out bit-identical; the whole output is also checked against fp32.
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["qkv", "qkv_rope", "swiglu", "nonorm_rope"])
+@pytest.mark.parametrize("B,S", [(127, 301), (128, 512)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_large_row_counts_match_reference(mode, B, S, dtype):
+    import torch.nn.functional as Fn
+    from oracle import apply_rotary_pos_emb, precompute_freqs_cis
+    from rl_for_mario_b200.kernels import (device_status, fold_norm_weight, fold_swiglu_weight, qkv_rope,
+                                           rmsnorm_qkv, rmsnorm_swiglu)
+
+    M, K, Hq, Hkv, D, F = B * S, 768, 12, 4, 64, 2048
+    b_tail = 32 * ((B - 16) // 32)  # b_tail * S is a multiple of 32
+    g = torch.Generator(device="cuda").manual_seed(M + len(mode))
+    x = (torch.randn(B, S, K, generator=g, device="cuda") * 2).to(dtype)
+    wn = 1 + 0.1 * torch.randn(K, generator=g, device="cuda")
+    xn = x.float() if mode == "nonorm_rope" else rmsnorm_ref(x.float(), wn)
+    cos, sin = (t.cuda() for t in precompute_freqs_cis(D, S))
+    tab = 0.0
+    if mode == "swiglu":
+        wg, wu = (torch.randn(F, K, generator=g, device="cuda") / K ** 0.5 for _ in range(2))
+        wf = fold_swiglu_weight(wg, wu, wn, dtype)
+        run = lambda xs: rmsnorm_swiglu(xs.reshape(-1, K), wf, 1e-5)
+        ref = (Fn.silu(xn @ wg.t()) * (xn @ wu.t())).view(M, F)
+    else:
+        wq, wk, wv = ((torch.randn(h * D, K, generator=g, device="cuda") / K ** 0.5).to(dtype)
+                      for h in (Hq, Hkv, Hkv))
+        rope = (cos, sin, (Hq + Hkv) * D, D)
+        if mode == "qkv":
+            wf = fold_norm_weight(wq, wk, wv, wn, dtype)
+            run = lambda xs: rmsnorm_qkv(xs.reshape(-1, K), wf, 1e-5)
+        elif mode == "qkv_rope":
+            wf = fold_norm_weight(wq, wk, wv, wn, dtype)
+            run = lambda xs: rmsnorm_qkv(xs, wf, 1e-5, rope=rope)
+        else:
+            wc = torch.cat([wq, wk, wv])
+            run = lambda xs: qkv_rope(xs, wc, *rope)
+        q, k, v = (xn @ w.float().t() for w in (wq, wk, wv))
+        if mode != "qkv":
+            # the kernel holds cos / sin as fp16 (relative rounding 2^-11): that
+            # moves a rotated value by at most 2^-11 (|x[d]| + |x[d +- D/2]|)
+            qk = torch.cat([q.reshape(M, -1), k.reshape(M, -1)], dim=1).view(M, -1, D).abs()
+            tab = 2.0 ** -11 * (qk + torch.cat([qk[..., D // 2:], qk[..., :D // 2]], dim=-1)).view(M, -1)
+            tab = torch.cat([tab, torch.zeros(M, Hkv * D, device="cuda")], dim=1)
+            q, k = apply_rotary_pos_emb(q.view(B, S, Hq, D), k.view(B, S, Hkv, D), cos, sin)
+        ref = torch.cat([t.reshape(M, -1) for t in (q, k, v)], dim=1)
+    y = run(x).reshape(B, S, -1)
+    assert device_status() == 0
+    for part in (slice(0, 16), slice(b_tail, B)):
+        assert torch.equal(y[part], run(x[part].contiguous()).reshape(part.stop - part.start, S, -1))
+    err = (y.float().reshape(M, -1) - ref).abs()
+    if mode == "nonorm_rope":
+        rel = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
+        bound = rel * ref.abs() + 1e-3 + tab
+    else:
+        # SwiGLU multiplies two projections, each with the folded norm weight
+        # rounded to 16 bits, so its relative error is about twice the others'
+        # (134 M outputs at 128 x 512 rows reach past the 2e-2 bf16 bound).
+        tol = (3e-2 if mode == "swiglu" else 2e-2) if dtype == torch.bfloat16 else 4e-3
+        bound = tol + tol * ref.abs()
+    assert bool((err <= bound).all()), f"max excess {(err - bound).max().item():.3e}"
