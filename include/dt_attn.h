@@ -256,6 +256,85 @@ int dt_frames_to_blocks(const void* frames, void* out, int64_t N, int C, int H, 
                         int dtype, void* stream);
 
 /*
+ * ---- Batched NES emulation: the Mario environment step (scope row f4) ----
+ *
+ * Replaces the reference's GPU emulator class NESBatchGpu and its kernels
+ * (nes_emulator_gpu/src/cuda/host/nes_batch_gpu.{h,cu}, src/cuda/kernels/
+ * nes_batch_kernel.cu) and the bookkeeping of GpuMarioVecEnv.step
+ * (scripts/mario/gpu_vec_env.py:271-404), with the same results (the same
+ * instructions, cycle counts, PPU model, frame loop and observation).  The
+ * caller owns every buffer; nothing here allocates.  Instances are grouped 32
+ * to a group; buffers hold n_pad = n rounded up to 32 instances:
+ *   regs        [n_pad][48]  packed registers, little-endian: A X Y SP, PC(16)
+ *               P nmi_pending, irq_pending joypad1 joypad_shift joypad_strobe,
+ *               PPUCTRL PPUMASK PPUSTATUS OAMADDR, v(16) t(16), fine_x w
+ *               read_buffer mirroring, scanline(16) cycle(16), frame_ready 0
+ *               active_sprite_count far_dma_count, total_cycles(64),
+ *               sprite-0-in-list flag, 0 (16-byte aligned)
+ *   ram, vram   [n_pad/32][2048][32]   byte a of instance i at
+ *                                       ((i/32)*2048 + a)*32 + i%32
+ *   oam         [n_pad/32][256][32],  palette [n_pad/32][32][32]
+ *   framebuffer [n_pad/32][240][32][32][8] palette values; pixel (y, x) of
+ *               instance i at (((i/32)*240 + y)*32 + x/8)*256 + (i%32)*8 + x%8;
+ *               NULL renders nothing (and, as in the reference, then never
+ *               sets the sprite 0 hit flag)
+ * PRG ROM 16 or 32 KB, CHR ROM 8 KB (NROM), device memory.
+ * Defined where the reference is not: an OAM DMA from page >= 8 copies from
+ * the RAM mirror (pages < 0x20), PRG ROM (pages >= 0x80) or zeros (the
+ * reference reads past the instance's RAM); reset clears the controller latch.
+ */
+typedef struct DtNesState {
+  uint8_t* regs;
+  uint8_t* ram;
+  uint8_t* vram;
+  uint8_t* oam;
+  uint8_t* palette;
+  uint8_t* framebuffer;
+} DtNesState;
+
+/* Power-on reset (NESBatchGpu::reset_all / reset_selected,
+ * nes_batch_kernel.cu:86-110, :231-254) of every instance, or of those with
+ * mask[i] != 0 (device, nullable).  mirroring 0..4 sets it (MIRROR_*); -1 keeps
+ * each instance's. */
+int dt_nes_reset(const DtNesState* s, int n, const uint8_t* mask, int mirroring, const uint8_t* prg,
+                 uint32_t prg_size, const uint8_t* chr, uint32_t chr_size, void* stream);
+
+/* num_frames frames of every instance, all but the last without background
+ * rendering (NESBatchGpu::run_frames_all, nes_batch_kernel.cu:116-160;
+ * num_frames = 1 is run_frame_all, :46-80). */
+int dt_nes_run_frames(const DtNesState* s, int n, int num_frames, const uint8_t* prg, uint32_t prg_size,
+                      const uint8_t* chr, uint32_t chr_size, void* stream);
+
+/* Controller bytes (device [n]) and a fresh serial latch
+ * (NESBatchGpu::set_buttons_batch, nes_batch_gpu.cu:424-430). */
+int dt_nes_set_buttons(const DtNesState* s, int n, const uint8_t* buttons, void* stream);
+
+/* Controller bytes from SIMPLE_MOVEMENT action indices (device int64 [n],
+ * 0..6), overridden during the boot sequence (boot[i] > boot_settle: START;
+ * 0 < boot[i] <= boot_settle: none) as GpuMarioVecEnv.step does
+ * (gpu_vec_env.py:300-320).  An index out of 0..6 sets the device status. */
+int dt_nes_set_actions(const DtNesState* s, int n, const int64_t* actions, const int32_t* boot,
+                       int boot_settle, void* stream);
+
+/* 84 x 84 grayscale observation of every framebuffer (palette -> luma,
+ * bilinear; nes_batch_kernel.cu:180-216) into obs [n][84][84] (nullable) and,
+ * when stacked [n][stack][84][84] is given, shifts each instance's stack by one
+ * frame (oldest first) and appends it (the frame ring of gpu_vec_env.py:
+ * 250-267). */
+int dt_nes_observe(const DtNesState* s, int n, uint8_t* obs, uint8_t* stacked, int stack, void* stream);
+
+/* The rest of GpuMarioVecEnv.step (gpu_vec_env.py:325-404) after the frames and
+ * the observation: x position ($006D * 256 + $0086), lives ($075A) and the
+ * stage-clear flag ($07D7 == 0x80) from RAM; boot counters (boot[i] -= frame_skip
+ * while > 0); reward = clip(dx / 40, -1, 1), -1 on a lost life, +1 on the
+ * flag; done; and, for done instances, a reset and boot[i] = boot_total.  All
+ * arrays are device [n] and updated in place. */
+int dt_nes_env_update(const DtNesState* s, int n, int frame_skip, int boot_total, int32_t* boot, int32_t* prev_x,
+                      int32_t* init_lives, float* reward, uint8_t* done, int32_t* x_pos, int32_t* lives,
+                      uint8_t* flag_get, const uint8_t* prg, uint32_t prg_size, const uint8_t* chr,
+                      uint32_t chr_size, void* stream);
+
+/*
  * Synchronises `stream`, then returns and clears the device status word that
  * the kernels of this library write when a bounded wait runs out or a
  * device-side check fails (0 = no error).  Used by tests and debugging.

@@ -26,6 +26,7 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _L = ctypes.c_int64
 _F = ctypes.c_float
+_U = ctypes.c_uint32
 
 # Exported symbol -> (restype, argtypes).  Kept in the order of include/dt_attn.h.
 SIGNATURES = {
@@ -49,6 +50,12 @@ SIGNATURES = {
     "dt_frames_conv1": (_I, [_P, _L, _I, _I, _I, _P, _P, _P, _P, _I, _I, _P]),
     "dt_encoder_conv23": (_I, [_P, _L, _P, _P, _P, _P, _P, _P, _I, _P]),
     "dt_frames_conv1_noalloc": (_I, [_P, _L, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
+    "dt_nes_reset": (_I, [_P, _I, _P, _I, _P, _U, _P, _U, _P]),
+    "dt_nes_run_frames": (_I, [_P, _I, _I, _P, _U, _P, _U, _P]),
+    "dt_nes_set_buttons": (_I, [_P, _I, _P, _P]),
+    "dt_nes_set_actions": (_I, [_P, _I, _P, _P, _I, _P]),
+    "dt_nes_observe": (_I, [_P, _I, _P, _P, _I, _P]),
+    "dt_nes_env_update": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _U, _P, _U, _P]),
 }
 
 

@@ -677,3 +677,120 @@ extern "C" int dt_rmsnorm_swiglu(const void* x, int64_t x_row_stride, const void
   return rmsnorm_qkv_impl(fn, x, x_row_stride, w_fused, y, y_row_stride, M, K, 2 * N, eps, nullptr, nullptr, 0, 0, 1,
                           0, 0, dtype, stream, 1);
 }
+
+// ------------------------------------------------------------------ NES emulation
+namespace {
+int nes_check(const char* fn, const DtNesState* s, int n, const uint8_t* prg, uint32_t prg_size, const uint8_t* chr,
+              uint32_t chr_size, bool need_rom) {
+  if (!s || !s->regs || !s->ram || !s->vram || !s->oam || !s->palette)
+    return fail(DT_ERR_INVALID, "%s: null state pointer", fn);
+  if (reinterpret_cast<uintptr_t>(s->regs) & 15) return fail(DT_ERR_INVALID, "%s: regs must be 16-byte aligned", fn);
+  if (s->framebuffer && (reinterpret_cast<uintptr_t>(s->framebuffer) & 7))
+    return fail(DT_ERR_INVALID, "%s: framebuffer must be 8-byte aligned", fn);
+  if (n < 1) return fail(DT_ERR_INVALID, "%s: n must be >= 1", fn);
+  if (need_rom) {
+    if (!prg || !chr) return fail(DT_ERR_INVALID, "%s: null ROM pointer", fn);
+    if (prg_size != 0x4000u && prg_size != 0x8000u)
+      return fail(DT_ERR_UNSUPPORTED, "%s: PRG ROM must be 16 or 32 KB (got %u bytes)", fn, prg_size);
+    if (chr_size != 0x2000u) return fail(DT_ERR_UNSUPPORTED, "%s: CHR ROM must be 8 KB (got %u bytes)", fn, chr_size);
+  }
+  return DT_OK;
+}
+dtk::NesLaunch nes_launch(const DtNesState* s, int n, const uint8_t* prg, uint32_t prg_size, const uint8_t* chr) {
+  dtk::NesLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.regs = s->regs; L.ram = s->ram; L.vram = s->vram; L.oam = s->oam; L.pal = s->palette; L.fb = s->framebuffer;
+  L.prg = prg; L.prg_size = prg_size; L.chr = chr; L.n = n;
+  return L;
+}
+int nes_run(const char* fn, int op, dtk::NesLaunch& L, void* stream) {
+  int dev = 0;
+  int* status = nullptr;
+  int rc = device_setup(&dev, &status);
+  if (rc) return rc;
+  L.status = status;
+  cudaError_t e = dtk::launch_nes(op, L, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
+  return DT_OK;
+}
+}  // namespace
+
+extern "C" int dt_nes_reset(const DtNesState* s, int n, const uint8_t* mask, int mirroring, const uint8_t* prg,
+                            uint32_t prg_size, const uint8_t* chr, uint32_t chr_size, void* stream) {
+  const char* fn = "dt_nes_reset";
+  if (int rc = nes_check(fn, s, n, prg, prg_size, chr, chr_size, true)) return rc;
+  if (mirroring < -1 || mirroring > 4) return fail(DT_ERR_INVALID, "%s: mirroring must be -1..4", fn);
+  dtk::NesLaunch L = nes_launch(s, n, prg, prg_size, chr);
+  L.mask = mask;
+  L.mirroring = mirroring;
+  return nes_run(fn, 1, L, stream);
+}
+
+extern "C" int dt_nes_run_frames(const DtNesState* s, int n, int num_frames, const uint8_t* prg, uint32_t prg_size,
+                                 const uint8_t* chr, uint32_t chr_size, void* stream) {
+  const char* fn = "dt_nes_run_frames";
+  if (int rc = nes_check(fn, s, n, prg, prg_size, chr, chr_size, true)) return rc;
+  if (num_frames < 1) return fail(DT_ERR_INVALID, "%s: num_frames must be >= 1", fn);
+  dtk::NesLaunch L = nes_launch(s, n, prg, prg_size, chr);
+  L.num_frames = num_frames;
+  return nes_run(fn, 0, L, stream);
+}
+
+extern "C" int dt_nes_set_buttons(const DtNesState* s, int n, const uint8_t* buttons, void* stream) {
+  const char* fn = "dt_nes_set_buttons";
+  if (int rc = nes_check(fn, s, n, nullptr, 0, nullptr, 0, false)) return rc;
+  if (!buttons) return fail(DT_ERR_INVALID, "%s: null buttons", fn);
+  dtk::NesLaunch L = nes_launch(s, n, nullptr, 0, nullptr);
+  L.buttons = buttons;
+  return nes_run(fn, 2, L, stream);
+}
+
+extern "C" int dt_nes_set_actions(const DtNesState* s, int n, const int64_t* actions, const int32_t* boot,
+                                  int boot_settle, void* stream) {
+  const char* fn = "dt_nes_set_actions";
+  if (int rc = nes_check(fn, s, n, nullptr, 0, nullptr, 0, false)) return rc;
+  if (!actions) return fail(DT_ERR_INVALID, "%s: null actions", fn);
+  dtk::NesLaunch L = nes_launch(s, n, nullptr, 0, nullptr);
+  L.actions = actions;
+  L.boot = const_cast<int32_t*>(boot);
+  L.boot_settle = boot_settle;
+  return nes_run(fn, 2, L, stream);
+}
+
+extern "C" int dt_nes_observe(const DtNesState* s, int n, uint8_t* obs, uint8_t* stacked, int stack, void* stream) {
+  const char* fn = "dt_nes_observe";
+  if (int rc = nes_check(fn, s, n, nullptr, 0, nullptr, 0, false)) return rc;
+  if (!s->framebuffer) return fail(DT_ERR_INVALID, "%s: rendering is off (no framebuffer)", fn);
+  if (!obs && !stacked) return fail(DT_ERR_INVALID, "%s: no output", fn);
+  if (stacked && (stack < 1 || stack > 64)) return fail(DT_ERR_INVALID, "%s: stack must be 1..64", fn);
+  if ((obs && (reinterpret_cast<uintptr_t>(obs) & 3)) || (stacked && (reinterpret_cast<uintptr_t>(stacked) & 3)))
+    return fail(DT_ERR_INVALID, "%s: outputs must be 4-byte aligned", fn);
+  dtk::NesLaunch L = nes_launch(s, n, nullptr, 0, nullptr);
+  L.obs = obs;
+  L.stacked = stacked;
+  L.stack = stack;
+  return nes_run(fn, 3, L, stream);
+}
+
+extern "C" int dt_nes_env_update(const DtNesState* s, int n, int frame_skip, int boot_total, int32_t* boot,
+                                 int32_t* prev_x, int32_t* init_lives, float* reward, uint8_t* done, int32_t* x_pos,
+                                 int32_t* lives, uint8_t* flag_get, const uint8_t* prg, uint32_t prg_size,
+                                 const uint8_t* chr, uint32_t chr_size, void* stream) {
+  const char* fn = "dt_nes_env_update";
+  if (int rc = nes_check(fn, s, n, prg, prg_size, chr, chr_size, true)) return rc;
+  if (!boot || !prev_x || !init_lives || !reward || !done || !x_pos || !lives || !flag_get)
+    return fail(DT_ERR_INVALID, "%s: null pointer", fn);
+  if (frame_skip < 1 || boot_total < 0) return fail(DT_ERR_INVALID, "%s: frame_skip >= 1, boot_total >= 0", fn);
+  dtk::NesLaunch L = nes_launch(s, n, prg, prg_size, chr);
+  L.frame_skip = frame_skip;
+  L.boot_total = boot_total;
+  L.boot = boot;
+  L.prev_x = prev_x;
+  L.init_lives = init_lives;
+  L.reward = reward;
+  L.done = done;
+  L.x_pos = x_pos;
+  L.lives = lives;
+  L.flag = flag_get;
+  return nes_run(fn, 4, L, stream);
+}

@@ -186,4 +186,39 @@ cudaError_t launch_kv_write_sm100(const KvWriteParams& prm, int D, int dtype, in
 cudaError_t launch_decode_sm100(const DecodeParams& prm, const CUtensorMap& kmap, const CUtensorMap& vmap, int D,
                                 bool bf16, int grid, cudaStream_t stream);
 
+
+// Batched NES emulation (nes_sm100.cu).  op: 0 run frames, 1 reset, 2 buttons,
+// 3 observation, 4 environment bookkeeping.  Unused fields may be left zero.
+struct NesLaunch {
+  uint8_t* regs;
+  uint8_t* ram;
+  uint8_t* vram;
+  uint8_t* oam;
+  uint8_t* pal;
+  uint8_t* fb;
+  const uint8_t* prg;
+  uint32_t prg_size;
+  const uint8_t* chr;
+  int n;
+  int num_frames;
+  const uint8_t* mask;
+  int mirroring;
+  const uint8_t* buttons;
+  const int64_t* actions;
+  int32_t* boot;
+  int boot_settle, boot_total, frame_skip;
+  int* status;
+  uint8_t* obs;
+  uint8_t* stacked;
+  int stack;
+  int32_t* prev_x;
+  int32_t* init_lives;
+  float* reward;
+  uint8_t* done;
+  int32_t* x_pos;
+  int32_t* lives;
+  uint8_t* flag;
+};
+cudaError_t launch_nes(int op, const NesLaunch& L, cudaStream_t st);
+
 }  // namespace dtk
