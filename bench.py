@@ -27,6 +27,7 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
 import torch
 
 REPO = Path(__file__).resolve().parent
@@ -979,6 +980,139 @@ def bench_conv23_cfg4(dev, peaks, batch=None):
                          "peak_source": peaks["source"]}}
 
 
+
+NES_ENV_CFG = {"envs": 65536, "frame_skip": 4, "frame_stack": 4,
+               "cartridge": "nes_roms.demo_rom(): synthetic 32 KB NROM (the SMB ROM is not shipped)"}
+
+
+def _nes_cpu_baseline(seconds: float = 8.0) -> dict:
+    """The C oracle (one host thread) on a bounded sample: 8 environments,
+    4-frame steps after the boot sequence, until `seconds` have passed."""
+    from oracle.nes import OracleEnv
+    from rl_for_mario_b200.nes_roms import demo_rom
+
+    env = OracleEnv(8, *demo_rom())
+    env.reset()
+    rng = np.random.default_rng(0)
+    t0, steps = time.perf_counter(), 0
+    while time.perf_counter() - t0 < seconds:
+        env.step(rng.integers(0, 7, 8))
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {"value": 8 * steps / dt, "unit": "env_steps/s", "cores": 1, "kind": "port",
+            "sample": f"oracle/nes_oracle.c, 8 environments x {steps} steps of 4 frames after the boot sequence"}
+
+
+def bench_nes_env(dev, peaks, envs=None, cpu: bool = True) -> dict:
+    """Mario environment step (scope row f4) on the batched NES kernels:
+    GpuMarioVecEnv.step_device at 65,536 environments, 4 frames per step (the
+    last one rendered), the 84 x 84 observation into the 4-frame stack, and the
+    reward / done / auto-reset bookkeeping, all on the device.  Inputs: random
+    SIMPLE_MOVEMENT actions resident on the device.  e2e: the reference-facing
+    step(actions) with numpy actions in and numpy rewards / dones / infos out."""
+    from rl_for_mario_b200.kernels import device_status
+    from rl_for_mario_b200.nes import GpuMarioVecEnv
+    from rl_for_mario_b200.nes_roms import demo_rom
+
+    n = envs or NES_ENV_CFG["envs"]
+    env = GpuMarioVecEnv(n, rom=demo_rom(), device=dev)
+    t0 = time.perf_counter()
+    env.reset()
+    torch.cuda.synchronize(dev)
+    boot_s = time.perf_counter() - t0
+    g = torch.Generator(device=dev).manual_seed(5)
+    acts = [torch.randint(0, 7, (n,), device=dev, generator=g) for _ in range(8)]
+
+    def timed(fn, reps):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    steps = 10
+    ms = timed(lambda i: env.step_device(acts[i % 8]), steps)
+    b = env._batch
+    frames_ms = timed(lambda i: b.run_frames_all(4), 5)
+    frame1_ms = timed(lambda i: b.run_frames_all(1), 5)
+    obs_out = torch.empty(n, 84, 84, dtype=torch.uint8, device=dev)
+    obs_ms = timed(lambda i: b.obs_device(obs_out), 10)
+    acts_np = [a.cpu().numpy() for a in acts]
+    e2e_ms = timed(lambda i: env.step(acts_np[i % 8]), steps)
+    if device_status() != 0:
+        raise SystemExit("device status error in the NES benchmark")
+    fb_bytes = n * 240 * 256
+    obs_bytes = fb_bytes + n * 84 * 84  # read every framebuffer, write the observation
+    gbs = obs_bytes / (obs_ms * 1e-3) / 1e9
+    out = {"metric": "env_steps_per_s", "value": n / (ms * 1e-3), "unit": "env_steps/s", "ms_per_step": ms,
+           "config": {"workload": f"Mario environment step, {n} environments, frame skip 4, frame stack 4",
+                      **NES_ENV_CFG, "envs": n},
+           "data": "synthetic cartridge, random actions",
+           "kernels_ms": {"nes_frames_kernel x4 frames (last rendered)": frames_ms,
+                          "nes_frames_kernel x1 rendered frame": frame1_ms,
+                          "nes_observe_kernel": obs_ms},
+           "env_frames_per_s": 4 * n / (frames_ms * 1e-3),
+           "boot_s": boot_s,
+           "e2e": {"value": n / (e2e_ms * 1e-3), "unit": "env_steps/s",
+                   "h2d_bytes_per_step": n * 8, "d2h_bytes_per_step": n * (4 + 1 + 4 + 4 + 1)},
+           "roofline_observe": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": obs_bytes,
+                                "peak_source": peaks["source"]}}
+    del env
+    torch.cuda.empty_cache()
+    if cpu:
+        out["cpu_baseline"] = _nes_cpu_baseline()
+    return out
+
+
+def bench_nes_reference(envs=None) -> dict:
+    """The reference's own NESBatchGpu (its kernels, built from its sources)
+    at the same size: per step, set_buttons_batch (host buttons), run_frames_all(4),
+    get_obs_batch and get_ram_batch (host copies), as GpuMarioVecEnv.step calls
+    them; and run_frames_all(4) alone.  Wall clock (its calls synchronise)."""
+    from oracle.nes import RefNESBatch
+    from rl_for_mario_b200.nes_roms import demo_rom
+
+    n = envs or NES_ENV_CFG["envs"]
+    prg, chr_rom, mir = demo_rom()
+    ref = RefNESBatch(n)
+    ref.load_rom(prg, chr_rom)
+    ref.reset_all(mir)
+    ref.set_buttons_batch(np.zeros(n, np.uint8))
+    t0 = time.perf_counter()
+    ref.run_frames_all(286)  # the boot sequence's frame count
+    boot_s = time.perf_counter() - t0
+    rng = np.random.default_rng(5)
+    bits = np.array([0x00, 0x80, 0x81, 0x82, 0x83, 0x01, 0x40], np.uint8)
+
+    def step():
+        ref.set_buttons_batch(bits[rng.integers(0, 7, n)])
+        ref.run_frames_all(4)
+        ref.get_obs_batch()
+        ref.get_ram_batch()
+
+    for _ in range(2):
+        step()
+    t0, k = time.perf_counter(), 5
+    for _ in range(k):
+        step()
+    step_s = (time.perf_counter() - t0) / k
+    t0 = time.perf_counter()
+    for _ in range(k):
+        ref.run_frames_all(4)
+    frames_s = (time.perf_counter() - t0) / k
+    return {"impl": "reference", "metric": "env_steps_per_s", "value": n / step_s, "unit": "env_steps/s",
+            "ms_per_step": step_s * 1e3, "run_frames_all_4_ms": frames_s * 1e3,
+            "env_frames_per_s": 4 * n / frames_s, "boot_286_frames_s": boot_s,
+            "config": {"workload": f"Mario environment step, {n} environments, frame skip 4", **NES_ENV_CFG,
+                       "envs": n}}
+
+
 def bench_rollout_cfg5(dev, world, rank, pg, cpu: bool = False):
     """8,192 environments per GPU, 64 cached steps, CNN on synthetic frames, all-gather of logits.
 
@@ -1083,7 +1217,7 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="override the batch (profiling of small cases only; the bench line is B=4096)")
     ap.add_argument("--only", choices=["decode", "prefill_long", "rmsnorm_qkv", "rmsnorm_swiglu", "conv1", "conv23",
-                                       "rollout", "gemm_residual"],
+                                       "rollout", "gemm_residual", "nes"],
                     default=None,
                     help="run one sub-benchmark alone and print its JSON (profiling)")
     ap.add_argument("--long-batch", type=int, default=None,
@@ -1109,6 +1243,12 @@ def main():
             emit({"only": "gemm_residual", **bench_gemm_residual_cfg4(dev, _peaks(), batch=args.long_batch)})
         elif args.only == "rollout":
             emit({"only": "rollout", **bench_rollout_cfg5(dev, 1, 0, None)})
+        elif args.only == "nes":
+            if args.impl == "reference":
+                emit(bench_nes_reference(envs=args.batch))
+            else:
+                emit({"only": "nes", **bench_nes_env(dev, _peaks(), envs=args.batch,
+                                                     cpu=not args.no_cpu_baseline)})
         elif args.only == "rmsnorm_swiglu":
             emit({"only": "rmsnorm_swiglu", **bench_rmsnorm_swiglu_cfg4(dev, _peaks(), batch=args.long_batch)})
         else:

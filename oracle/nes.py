@@ -198,3 +198,86 @@ class OracleEnv:
         active = ~booting & ~dones
         self.prev_x[active] = cur_x[active]
         return self.stacked(), rew, dones, info
+
+
+# ---------------------------------------------------------------- the reference
+_REF = _DIR / "_ref" / "libnes_ref.so"
+
+
+class RefNESBatch:
+    """The reference's own NESBatchGpu (built from its sources into
+    oracle/_ref/libnes_ref.so by oracle/build_ref.py), through the extern "C"
+    shim oracle/nes_ref_shim.cu.  Host numpy arrays in and out, as its pybind
+    module takes them."""
+
+    def __init__(self, n: int):
+        if not _REF.exists():
+            raise FileNotFoundError(f"{_REF} is not built (python oracle/build_ref.py)")
+        self.lib = ctypes.CDLL(str(_REF))
+        P, I, U = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32
+        sig = {"ref_nes_create": (P, [I]), "ref_nes_destroy": (None, [P]),
+               "ref_nes_load_rom": (I, [P, P, U, P, U]), "ref_nes_reset_all": (I, [P, I]),
+               "ref_nes_run_frame_all": (I, [P]), "ref_nes_run_frames_all": (I, [P, I]),
+               "ref_nes_set_buttons": (I, [P, P, I]), "ref_nes_get_ram": (I, [P, P]),
+               "ref_nes_get_obs": (I, [P, P]), "ref_nes_get_framebuffers": (I, [P, P]),
+               "ref_nes_reset_selected": (I, [P, P, I]), "ref_nes_get_scalars": (I, [P, I, P])}
+        for k, (r, a) in sig.items():
+            getattr(self.lib, k).restype, getattr(self.lib, k).argtypes = r, a
+        self.n = n
+        self.h = self.lib.ref_nes_create(n)
+        if not self.h:
+            raise RuntimeError("NESBatchGpu construction failed")
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.lib.ref_nes_destroy(self.h)
+            self.h = None
+
+    def _ok(self, rc, what):
+        if rc != 0:
+            raise RuntimeError(f"reference {what} failed")
+
+    def load_rom(self, prg: bytes, chr_rom: bytes):
+        self._prg = np.frombuffer(prg, np.uint8).copy()
+        self._chr = np.frombuffer(chr_rom, np.uint8).copy()
+        self._ok(self.lib.ref_nes_load_rom(self.h, _ptr(self._prg), len(prg), _ptr(self._chr), len(chr_rom)),
+                 "load_rom")
+
+    def reset_all(self, mirroring: int = 0):
+        self._ok(self.lib.ref_nes_reset_all(self.h, mirroring), "reset_all")
+
+    def run_frame_all(self):
+        self._ok(self.lib.ref_nes_run_frame_all(self.h), "run_frame_all")
+
+    def run_frames_all(self, k: int):
+        self._ok(self.lib.ref_nes_run_frames_all(self.h, k), "run_frames_all")
+
+    def set_buttons_batch(self, buttons):
+        b = np.ascontiguousarray(buttons, np.uint8)
+        self._ok(self.lib.ref_nes_set_buttons(self.h, _ptr(b), len(b)), "set_buttons_batch")
+
+    def get_ram_batch(self) -> np.ndarray:
+        out = np.empty((self.n, 2048), np.uint8)
+        self._ok(self.lib.ref_nes_get_ram(self.h, _ptr(out)), "get_ram_batch")
+        return out
+
+    def get_obs_batch(self) -> np.ndarray:
+        out = np.empty((self.n, 84, 84), np.uint8)
+        self._ok(self.lib.ref_nes_get_obs(self.h, _ptr(out)), "get_obs_batch")
+        return out
+
+    def get_framebuffers(self) -> np.ndarray:
+        out = np.empty((self.n, 240, 256), np.uint32)
+        self._ok(self.lib.ref_nes_get_framebuffers(self.h, _ptr(out)), "get_framebuffers")
+        return out
+
+    def reset_selected(self, mask):
+        m = np.ascontiguousarray(mask, np.uint8)
+        self._ok(self.lib.ref_nes_reset_selected(self.h, _ptr(m), len(m)), "reset_selected")
+
+    def scalars(self) -> np.ndarray:
+        """[n, 27] in the order of SCALARS[:27] (the controller fields read 0)."""
+        out = np.empty((self.n, 27), np.int64)
+        for i in range(self.n):
+            self._ok(self.lib.ref_nes_get_scalars(self.h, i, _ptr(out[i])), "get_state")
+        return out

@@ -16,7 +16,6 @@ those in dma_far.
 """
 from __future__ import annotations
 
-import ctypes
 import hashlib
 import sys
 from pathlib import Path
@@ -26,7 +25,7 @@ import numpy as np
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
 
-from oracle.nes import OracleNES, SCALARS, palette_rgba  # noqa: E402
+from oracle.nes import OracleNES, RefNESBatch, SCALARS, palette_rgba  # noqa: E402
 from rl_for_mario_b200.nes_roms import demo_rom, random_rom  # noqa: E402
 
 N = 6
@@ -53,64 +52,31 @@ def fb_sha(rgba: np.ndarray) -> np.ndarray:
     return np.array([int.from_bytes(hashlib.sha256(f.tobytes()).digest()[:8], "little") for f in rgba], np.uint64)
 
 
-class Ref:
-    def __init__(self, path: Path):
-        self.lib = ctypes.CDLL(str(path))
-        P, I, U = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32
-        sig = {"ref_nes_create": (P, [I]), "ref_nes_destroy": (None, [P]), "ref_nes_load_rom": (I, [P, P, U, P, U]),
-               "ref_nes_reset_all": (I, [P, I]), "ref_nes_run_frame_all": (I, [P]),
-               "ref_nes_run_frames_all": (I, [P, I]), "ref_nes_set_buttons": (I, [P, P, I]),
-               "ref_nes_get_ram": (I, [P, P]), "ref_nes_get_obs": (I, [P, P]),
-               "ref_nes_get_framebuffers": (I, [P, P]), "ref_nes_reset_selected": (I, [P, P, I]),
-               "ref_nes_get_scalars": (I, [P, I, P])}
-        for k, (r, a) in sig.items():
-            getattr(self.lib, k).restype, getattr(self.lib, k).argtypes = r, a
-
-    def call(self, name, *args):
-        rc = getattr(self.lib, name)(*args)
-        if rc != 0:
-            raise RuntimeError(f"{name} failed")
-
-
-def _p(a):
-    return a.ctypes.data_as(ctypes.c_void_p)
-
-
 def run(out_path: Path) -> int:
-    ref = Ref(ROOT / "oracle" / "_ref" / "libnes_ref.so")
     pal = palette_rgba()
     golden, bad = {}, 0
     for ci, (name, make) in enumerate(CARTS.items()):
         prg, chr_rom, mir = make()
-        prg_a, chr_a = np.frombuffer(prg, np.uint8).copy(), np.frombuffer(chr_rom, np.uint8).copy()
-        h = ref.lib.ref_nes_create(N)
-        ref.call("ref_nes_load_rom", h, _p(prg_a), len(prg_a), _p(chr_a), len(chr_a))
-        ref.call("ref_nes_reset_all", h, mir)
+        ref = RefNESBatch(N)
+        ref.load_rom(prg, chr_rom)
+        ref.reset_all(mir)
         ora = OracleNES(N, prg, chr_rom, mir)
         ora.reset()
         for op, arg in schedule(ci):
             if op == "b":
-                ref.call("ref_nes_set_buttons", h, _p(arg), N)
+                ref.set_buttons_batch(arg)
                 ora.set_buttons(arg)
             elif op == "f":
-                ref.call("ref_nes_run_frame_all", h)
+                ref.run_frame_all()
                 ora.run_frames(1)
             elif op == "k":
-                ref.call("ref_nes_run_frames_all", h, arg)
+                ref.run_frames_all(arg)
                 ora.run_frames(arg)
             else:
-                ref.call("ref_nes_reset_selected", h, _p(arg), N)
+                ref.reset_selected(arg)
                 ora.reset(arg)
-        ram = np.empty((N, 2048), np.uint8)
-        ref.call("ref_nes_get_ram", h, _p(ram))
-        obs = np.empty((N, 84, 84), np.uint8)
-        ref.call("ref_nes_get_obs", h, _p(obs))
-        rgba = np.empty((N, 240, 256), np.uint32)
-        ref.call("ref_nes_get_framebuffers", h, _p(rgba))
-        sc = np.empty((N, 27), np.int64)
-        for i in range(N):
-            ref.call("ref_nes_get_scalars", h, i, _p(sc[i]))
-        ref.lib.ref_nes_destroy(h)
+        ram, obs, rgba, sc = ref.get_ram_batch(), ref.get_obs_batch(), ref.get_framebuffers(), ref.scalars()
+        del ref
         os_ = ora.scalars()
         keep = os_["dma_far"] == 0
         o_sc = np.stack([os_[k] for k in SCALARS[:27]], 1)
