@@ -97,6 +97,8 @@ struct NesCpu {
   uint32_t ctrl, mask, status, oam_addr, v, t, fine_x, w, rbuf, mir;
   int scanline, cycle;
   uint32_t frame_ready, count, s0, dma_far, headless;
+  uint32_t spr_tiles;  // tiles of this line that some listed sprite covers (bit per 8-pixel tile)
+  uint32_t tile_done;  // the current tile was finished at its first pixel (no sprite over it)
   unsigned long long total;
   unsigned long long tbuf;  // background tile being rendered (8 palette values)
 };
@@ -165,23 +167,40 @@ __device__ __forceinline__ void sprite_pixel(NesCpu& s, const NesMem& m, int x) 
     return;
   }
 }
-// Pixels [xa, xb) of the current visible line.
+// Pixels [xa, xb) of the current visible line.  A tile that no listed sprite
+// covers is final once its background is drawn at its first pixel (nothing
+// else can change it), so it is stored then and its other pixels are skipped;
+// covered tiles take every pixel.  Headless frames only look for sprite 0 hits,
+// so they visit only sprite 0's 8 pixels.
 __device__ __forceinline__ void render_range(NesCpu& s, const NesMem& m, int xa, int xb) {
-  const bool spr = (s.mask & 0x10u) && s.count;
   if (s.headless) {
-    if (!spr) return;
-    for (int x = xa; x < xb; ++x) sprite_pixel(s, m, x);
+    if (!s.count || !(s.mask & 0x10u)) return;  // (headless lists hold sprite 0 only)
+    const int sx = (int)(m.spr[0] & 0xFFu);
+    const int lo = max(xa, sx), hi = min(xb, sx + 8);
+    for (int x = lo; x < hi; ++x) sprite_pixel(s, m, x);
     return;
   }
-  for (int x = xa; x < xb; ++x) {
-    if ((x & 7) == 0) bg_tile(s, m, x >> 3);
-    if (spr) sprite_pixel(s, m, x);
-    if ((x & 7) == 7) flush_tile(s, m, x >> 3);
+  int x = xa;
+  while (x < xb) {
+    const int tx = x >> 3;
+    if ((x & 7) == 0) {
+      bg_tile(s, m, tx);
+      s.tile_done = !((s.spr_tiles >> tx) & 1u);
+      if (s.tile_done) flush_tile(s, m, tx);
+    }
+    if (s.tile_done) {
+      x = (x | 7) + 1;  // next tile
+      continue;
+    }
+    if (s.mask & 0x10u) sprite_pixel(s, m, x);
+    if ((x & 7) == 7) flush_tile(s, m, tx);
+    ++x;
   }
 }
 __device__ __forceinline__ void eval_sprites(NesCpu& s, const NesMem& m) {
   s.count = 0;
   s.s0 = 0;
+  s.spr_tiles = 0;
   const int n = s.headless ? 1 : 64;
   for (int i = 0; i < n; ++i) {
     const int row = s.scanline - ((int)m.oam[(4 * i) * kNesThreads] + 1);
@@ -196,6 +215,7 @@ __device__ __forceinline__ void eval_sprites(NesCpu& s, const NesMem& m) {
     const uint32_t a = ((s.ctrl & 0x08u) ? 0x1000u : 0u) + tile * 16u + fy;
     const uint32_t pat = (chr_byte(m, a) << 8) | chr_byte(m, a + 8);
     m.spr[s.count * kNesThreads] = x | (attr << 8) | (pat << 16);
+    s.spr_tiles |= (1u << (x >> 3)) | ((x + 7) < 256 ? (1u << ((x + 7) >> 3)) : 0u);
     if (i == 0) s.s0 = 1;
     s.count++;
   }
@@ -570,6 +590,8 @@ __device__ __forceinline__ void load_regs(NesCpu& s, const uint8_t* regs) {
   s.s0 = c.z & 1u;
   s.headless = 0;
   s.tbuf = 0;
+  s.spr_tiles = 0;
+  s.tile_done = 0;
 }
 __device__ __forceinline__ void store_regs(const NesCpu& s, uint8_t* regs) {
   uint4 a, b, c;
