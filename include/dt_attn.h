@@ -312,7 +312,7 @@ int dt_nes_set_buttons(const DtNesState* s, int n, const uint8_t* buttons, void*
 /* Controller bytes from SIMPLE_MOVEMENT action indices (device int64 [n],
  * 0..6), overridden during the boot sequence (boot[i] > boot_settle: START;
  * 0 < boot[i] <= boot_settle: none) as GpuMarioVecEnv.step does
- * (gpu_vec_env.py:300-320).  An index out of 0..6 sets the device status. */
+ * (gpu_vec_env.py:327-342).  An index out of 0..6 sets the device status. */
 int dt_nes_set_actions(const DtNesState* s, int n, const int64_t* actions, const int32_t* boot,
                        int boot_settle, void* stream);
 
@@ -323,7 +323,7 @@ int dt_nes_set_actions(const DtNesState* s, int n, const int64_t* actions, const
  * 250-267). */
 int dt_nes_observe(const DtNesState* s, int n, uint8_t* obs, uint8_t* stacked, int stack, void* stream);
 
-/* The rest of GpuMarioVecEnv.step (gpu_vec_env.py:325-404) after the frames and
+/* The rest of GpuMarioVecEnv.step (gpu_vec_env.py:344-404) after the frames and
  * the observation: x position ($006D * 256 + $0086), lives ($075A) and the
  * stage-clear flag ($07D7 == 0x80) from RAM; boot counters (boot[i] -= frame_skip
  * while > 0); reward = clip(dx / 40, -1, 1), -1 on a lost life, +1 on the
