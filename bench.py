@@ -322,6 +322,7 @@ def run_ours(args):
             line["prefill_long"]["encoder_conv1_kernel"] = bench_conv1_cfg4(dev, peaks)
             line["prefill_long"]["encoder_conv23_kernels"] = bench_conv23_cfg4(dev, peaks)
             line["prefill_long"]["residual_gemms"] = bench_gemm_residual_cfg4(dev, peaks)
+            line["nes_env"] = bench_nes_env(dev, peaks, cpu=cpu)
         line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg, cpu=cpu)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
