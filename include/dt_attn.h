@@ -198,11 +198,11 @@ int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int W, const vo
 /*
  * The state encoder's second and third layers: Conv2d(32, 64, 4, stride 2) +
  * ReLU on the first layer's 20 x 20 output, then Conv2d(64, 64, 3, stride 1) +
- * ReLU (model_decision_transformer.py:322-325), each as an implicit GEMM on
- * the tensor cores whose A tiles are single TMA copies of the channels-last
- * input (no im2col pass).  x1 [N, 20, 20, 32], y2 [N, 9, 9, 64] and y3
- * [N, 7, 7, 64] channels-last 16-bit tensors (16-byte aligned); y2 is an
- * output too (conv2 + ReLU) and the third layer's input.  w2 [64, 32, 4, 4],
+ * ReLU (model_decision_transformer.py:322-325), fused in one tensor-core
+ * kernel that keeps the second layer's output in shared memory.  x1
+ * [N, 20, 20, 32] and y3 [N, 7, 7, 64] channels-last 16-bit tensors (16-byte
+ * aligned); y2 [N, 9, 9, 64] (nullable) also receives the second layer's
+ * output (conv2 + ReLU) when given.  w2 [64, 32, 4, 4],
  * w3 [64, 64, 3, 3] 16-bit in the reference's own layout; b2, b3 [64] fp32.
  * Products accumulate in fp32, the bias is added in fp32 and each output is
  * rounded once.  bf16 or fp16.

@@ -581,11 +581,11 @@ extern "C" int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int 
 extern "C" int dt_encoder_conv23(const void* x1, int64_t N, const void* w2, const float* b2, void* y2, const void* w3,
                                  const float* b3, void* y3, int dtype, void* stream) {
   const char* fn = "dt_encoder_conv23";
-  if (!x1 || !w2 || !b2 || !y2 || !w3 || !b3 || !y3) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
+  if (!x1 || !w2 || !b2 || !w3 || !b3 || !y3) return fail(DT_ERR_INVALID, "%s: null pointer", fn);
   if (N < 1 || N > 0x3fffffffLL) return fail(DT_ERR_INVALID, "%s: N must be in [1, 2^30)", fn);
   if (dtype != DT_DTYPE_BF16 && dtype != DT_DTYPE_FP16)
     return fail(DT_ERR_UNSUPPORTED, "%s: dtype %d not supported (bf16 / fp16)", fn, dtype);
-  if (!aligned16(x1) || !aligned16(y2) || !aligned16(y3) || (reinterpret_cast<uintptr_t>(w2) & 1) ||
+  if (!aligned16(x1) || (y2 && !aligned16(y2)) || !aligned16(y3) || (reinterpret_cast<uintptr_t>(w2) & 1) ||
       (reinterpret_cast<uintptr_t>(w3) & 1) || (reinterpret_cast<uintptr_t>(b2) & 3) ||
       (reinterpret_cast<uintptr_t>(b3) & 3))
     return fail(DT_ERR_INVALID, "%s: x1, y2 and y3 must be 16-byte aligned", fn);
@@ -594,27 +594,8 @@ extern "C" int dt_encoder_conv23(const void* x1, int64_t N, const void* w2, cons
   int rc = device_setup(&dev, &status);
   if (rc) return rc;
   if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
-  const bool bf16 = dtype == DT_DTYPE_BF16;
-  // conv2 input [N, 20, 20, 32] as (64 values = a pixel pair, block column, block-row
-  // parity, block row, frame); box = one atom's 81 positions of a frame.
-  CUtensorMap m1, m2;
-  {
-    const cuuint64_t dims[5] = {64, 10, 2, 10, (cuuint64_t)N};
-    const cuuint64_t strides[4] = {128, 1280, 2560, 25600};
-    const cuuint32_t box[5] = {64, 9, 1, 9, 1};
-    if ((rc = encode_nd(&m1, x1, bf16, 5, dims, strides, box, "x1"))) return rc;
-  }
-  // conv3 input [N, 9, 9, 64] as (64 channels, column, row, frame); box = 49 positions of two frames.
-  {
-    const cuuint64_t dims[4] = {64, 9, 9, (cuuint64_t)N};
-    const cuuint64_t strides[3] = {128, 1152, 10368};
-    const cuuint32_t box[4] = {64, 7, 7, 2};
-    if ((rc = encode_nd(&m2, y2, bf16, 4, dims, strides, box, "y2"))) return rc;
-  }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = dtk::launch_encoder_conv_sm100(2, m1, x1, w2, b2, y2, N, bf16, g_num_sms[dev], status, st);
-  if (e == cudaSuccess)
-    e = dtk::launch_encoder_conv_sm100(3, m2, y2, w3, b3, y3, N, bf16, g_num_sms[dev], status, st);
+  cudaError_t e = dtk::launch_encoder_conv23_sm100(x1, w2, b2, y2, w3, b3, y3, N, dtype == DT_DTYPE_BF16,
+                                                   g_num_sms[dev], status, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
   return DT_OK;
 }

@@ -168,9 +168,9 @@ cudaError_t launch_gemm_residual_pair_sm100(const CUtensorMap& x, const CUtensor
 
 // The state encoder's second (layer 2) or third (layer 3) convolution + ReLU;
 // x is the layer's input tensor map (encoder_conv23 in capi.cu), xp its base.
-cudaError_t launch_encoder_conv_sm100(int layer, const CUtensorMap& x, const void* xp, const void* w,
-                                      const float* bias, void* y, long long n_frames, bool bf16, int num_sms,
-                                      int* status, cudaStream_t st);
+cudaError_t launch_encoder_conv23_sm100(const void* x1, const void* w2, const float* b2, void* y2, const void* w3,
+                                        const float* b3, void* y3, long long n_frames, bool bf16, int num_sms,
+                                        int* status, cudaStream_t st);
 
 cudaError_t launch_frames_conv1_sm100(const void* frames, long long N, int H, int W, const void* w,
                                       const float* bias, unsigned int* frame_max, void* y, bool bf16,

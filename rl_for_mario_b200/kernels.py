@@ -311,12 +311,14 @@ def frames_conv1(frames: Tensor, weight: Tensor, bias: Tensor, round_input: bool
     return out, fmax
 
 
-def encoder_conv23(x1: Tensor, w2: Tensor, b2: Tensor, w3: Tensor, b3: Tensor) -> Tuple[Tensor, Tensor]:
+def encoder_conv23(x1: Tensor, w2: Tensor, b2: Tensor, w3: Tensor, b3: Tensor,
+                   keep_y2: bool = True) -> Tuple[Optional[Tensor], Tensor]:
     """relu(conv2d(x1, w2, b2, stride 2)) and relu(conv2d(that, w3, b3)) for the
     state encoder's second and third layers: x1 a channels-last [N, 32, 20, 20]
     16-bit tensor (the first layer's output), w2 [64, 32, 4, 4], w3 [64, 64, 3, 3]
     of x1's dtype.  Returns both outputs as channels-last tensors ([N, 64, 9, 9],
-    [N, 64, 7, 7])."""
+    [N, 64, 7, 7]); with keep_y2=False the second layer's output is not written
+    to memory at all (None is returned in its place)."""
     _require_cuda(x1, w2, b2, w3, b3)
     if x1.dim() != 4 or tuple(x1.shape[1:]) != (32, 20, 20) or not x1.is_contiguous(memory_format=torch.channels_last):
         raise ValueError("x1 must be a channels-last [N, 32, 20, 20] tensor")
@@ -328,7 +330,7 @@ def encoder_conv23(x1: Tensor, w2: Tensor, b2: Tensor, w3: Tensor, b3: Tensor) -
     w2c, w3c = w2.contiguous(), w3.contiguous()
     b2f, b3f = b2.float().contiguous(), b3.float().contiguous()
     cl = torch.channels_last
-    y2 = torch.empty((N, 64, 9, 9), dtype=x1.dtype, device=x1.device, memory_format=cl)
+    y2 = torch.empty((N, 64, 9, 9), dtype=x1.dtype, device=x1.device, memory_format=cl) if keep_y2 else None
     y3 = torch.empty((N, 64, 7, 7), dtype=x1.dtype, device=x1.device, memory_format=cl)
     rc = _lib.load().dt_encoder_conv23(_ptr(x1), N, _ptr(w2c), _ptr(b2f), _ptr(y2), _ptr(w3c), _ptr(b3f), _ptr(y3),
                                        _dtype_code(x1), _stream_ptr(x1.device))

@@ -2,12 +2,11 @@
 (dt_encoder_conv23) against PyTorch's fp32 convolution of the same 16-bit
 values (reference model/model_decision_transformer.py:322-325).
 
-Frame counts cover one frame, odd counts (the third layer's boxes hold two
-frames; the last box of an odd count reads past the tensor and is zero-filled),
-and counts that give every persistent CTA several tiles, so the stage ring and
-the accumulator double buffer wrap their barrier phases.  Tolerance: the
-output's own 16-bit rounding (2^-8 relative) plus 2e-3 absolute for fp32
-accumulation order.
+Frame counts cover one frame, counts below and above the number of SMs (the
+persistent CTAs take one frame at a time, loading the next one into the other
+input buffer, so 300 and 1001 frames wrap both buffers and the accumulator
+barrier's phase many times).  Tolerance: the output's own 16-bit rounding
+(2^-8 relative) plus 2e-3 absolute for fp32 accumulation order.
 """
 import pytest
 import torch
@@ -105,3 +104,18 @@ def test_encoder_conv23_in_the_model_encoder():
             MarioStateEncoder._tc_conv23 = False
     err = (ours.float() - base.float()).abs()
     assert (err - 2e-2 - 2.0 ** -7 * base.float().abs()).max().item() <= 0, f"max err {err.max().item():.3e}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_encoder_conv23_without_storing_y2(dtype):
+    """keep_y2=False: the second layer's output stays in shared memory; the
+    third layer's output is bit-identical to the run that also stores y2."""
+    from rl_for_mario_b200.kernels import device_status, encoder_conv23
+
+    x1, w2, b2, w3, b3 = _inputs(333, dtype, seed=5)
+    y2, y3 = encoder_conv23(x1, w2, b2, w3, b3)
+    none, y3b = encoder_conv23(x1, w2, b2, w3, b3, keep_y2=False)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    assert none is None and torch.equal(y3, y3b)
