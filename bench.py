@@ -323,6 +323,7 @@ def run_ours(args):
             line["prefill_long"]["encoder_conv23_kernels"] = bench_conv23_cfg4(dev, peaks)
             line["prefill_long"]["residual_gemms"] = bench_gemm_residual_cfg4(dev, peaks)
             line["nes_env"] = bench_nes_env(dev, peaks, cpu=cpu)
+            line["nes_env"]["policy_loop"] = bench_nes_policy(dev)
         line["rollout"] = bench_rollout_cfg5(dev, world, rank, pg, cpu=cpu)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, info = cpu_oracle_rate(budget_s=12.0, sample_b=256, threads=len(os.sched_getaffinity(0)))
@@ -1075,6 +1076,46 @@ def bench_nes_env(dev, peaks, envs=None, cpu: bool = True) -> dict:
     return out
 
 
+
+def bench_nes_policy(dev, envs: int = 8192, steps: int = 16) -> dict:
+    """The closed loop of row f4 feeding the decode: the repo-default DT (bf16,
+    fused blocks, CUDA-graph rollout) reads the NES environments' stacked
+    frames and its actions step the emulators (nes.run_policy), 8,192
+    environments (the rollout's per-GPU count) on the synthetic cartridge, for
+    `steps` steps after the boot sequence; no host round trip inside a step."""
+    from rl_for_mario_b200.dt_model import DTConfig, MarioDT
+    from rl_for_mario_b200.kernels import device_status
+    from rl_for_mario_b200.nes import GpuMarioVecEnv, run_policy
+    from rl_for_mario_b200.nes_roms import demo_rom
+    from rl_for_mario_b200.rollout import DTRollout
+
+    C = ROLLOUT_CFG
+    cfg = DTConfig(hidden_size=C["hidden"], num_hidden_layers=C["layers"], num_attention_heads=C["q_heads"],
+                   num_key_value_heads=C["kv_heads"], context_len=C["context_len"], dropout=0.0)
+    model = MarioDT(cfg).to(dev, torch.bfloat16).eval().fuse_norms()
+    env = GpuMarioVecEnv(envs, rom=demo_rom(), device=dev)
+    ro = DTRollout(model, num_envs=envs, max_steps=steps, page_size=64, device=dev, graphs=True)
+    obs0 = env.reset().clone()
+    run_policy(env, ro, steps, start_obs=obs0)      # eager episode (initialises the kernels)
+    run_policy(env, ro, steps, start_obs=obs0)      # captures the step graphs
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    acts, _, _ = run_policy(env, ro, steps, start_obs=obs0)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    if device_status() != 0:
+        raise SystemExit("device status error in the NES policy benchmark")
+    ms = e0.elapsed_time(e1) / steps
+    out = {"metric": "env_steps_per_s (policy + environment)", "value": envs / (ms * 1e-3), "unit": "env_steps/s",
+           "ms_per_step": ms, "envs": envs, "steps": steps,
+           "config": "repo-default DT bf16 (fused blocks, graph-replayed cached rollout) + 4 NES frames per step, "
+                     "synthetic cartridge; the episode's reset is outside the timed steps",
+           "distinct_actions": len(set(acts.flatten().tolist()))}
+    del env, ro, model
+    torch.cuda.empty_cache()
+    return out
+
 def bench_nes_reference(envs=None) -> dict:
     """The reference's own NESBatchGpu (its kernels, built from its sources)
     at the same size: per step, set_buttons_batch (host buttons), run_frames_all(4),
@@ -1252,8 +1293,9 @@ def main():
             if args.impl == "reference":
                 emit(bench_nes_reference(envs=args.batch))
             else:
-                emit({"only": "nes", **bench_nes_env(dev, _peaks(), envs=args.batch,
-                                                     cpu=not args.no_cpu_baseline)})
+                line = bench_nes_env(dev, _peaks(), envs=args.batch, cpu=not args.no_cpu_baseline)
+                line["policy_loop"] = bench_nes_policy(dev)
+                emit({"only": "nes", **line})
         elif args.only == "rmsnorm_swiglu":
             emit({"only": "rmsnorm_swiglu", **bench_rmsnorm_swiglu_cfg4(dev, _peaks(), batch=args.long_batch)})
         else:

@@ -290,3 +290,33 @@ class GpuMarioVecEnv:
 
     def close(self) -> None:
         del self._batch
+
+
+@torch.no_grad()
+def run_policy(env: GpuMarioVecEnv, rollout, steps: int, target_return: float = 1.0,
+               deterministic: bool = True, start_obs: Optional[torch.Tensor] = None):
+    """Closed loop on the device, as the reference's batched rollout
+    (trainer/train_ppo_finetune.py:397-437: policy -> actions for all
+    environments -> environment step): the Decision Transformer's cached
+    rollout (``rollout.DTRollout``) reads the environment's stacked frames,
+    its actions step the emulators (``step_device``), and the new frames feed
+    the next policy step -- no host round trip in between.  Returns device
+    tensors (actions, rewards, dones), each [steps, N]; the return-to-go
+    falls by each step's reward, the timestep counts steps.  ``start_obs``:
+    the frames of the first step (default: ``env.reset()``)."""
+    n = env.num_envs
+    dev = env._device
+    obs = env.reset() if start_obs is None else start_obs
+    rtg = torch.full((n,), float(target_return), dtype=torch.float32, device=dev)
+    ts = torch.zeros(n, dtype=torch.long, device=dev)
+    acts = torch.empty(steps, n, dtype=torch.long, device=dev)
+    rews = torch.empty(steps, n, dtype=torch.float32, device=dev)
+    dones = torch.empty(steps, n, dtype=torch.uint8, device=dev)
+    rollout.reset()
+    for t in range(steps):
+        a, _ = rollout.step(obs, rtg, ts, deterministic=deterministic)
+        obs, r, d, _ = env.step_device(a)
+        acts[t], rews[t], dones[t] = a, r, d
+        rtg -= r
+        ts += 1
+    return acts, rews, dones

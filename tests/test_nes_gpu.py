@@ -216,3 +216,56 @@ def test_bad_arguments_are_rejected():
     env.reset()
     env.step_device(torch.tensor([0, 1, 9, 2], device="cuda"))
     assert device_status() != 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("graphs", [False, True])
+def test_policy_loop_on_device_matches_oracle_env(graphs):
+    """run_policy: the Decision Transformer's cached rollout reads the
+    environment's frames and its actions step the emulators, all on the
+    device.  The same policy driven by the oracle's environment (frames copied
+    from the host) sees bit-identical frames, so it chooses the same actions at
+    every step, and rewards and dones agree."""
+    from oracle.dt_ref import dt_param_shapes
+    from oracle.nes import OracleEnv
+    from oracle.seeded import seeded_state_dict
+    from rl_for_mario_b200.dt_model import DTConfig, MarioDT
+    from rl_for_mario_b200.nes import GpuMarioVecEnv, run_policy
+    from rl_for_mario_b200.nes_roms import demo_rom
+    from rl_for_mario_b200.rollout import DTRollout
+
+    cfg = DTConfig(hidden_size=256, num_hidden_layers=4, num_attention_heads=8, num_key_value_heads=2,
+                   context_len=32, dropout=0.0)
+    cfgd = {k: getattr(cfg, k) for k in ("state_shape", "act_dim", "max_ep_len", "context_len", "hidden_size",
+                                         "num_hidden_layers", "num_attention_heads", "num_key_value_heads",
+                                         "intermediate_size")}
+    model = MarioDT(cfg)
+    model.load_state_dict(seeded_state_dict(dt_param_shapes(cfgd), 4), strict=True)
+    model = model.cuda().to(torch.bfloat16).eval()
+    n, T = 16, 24
+    rom = demo_rom()
+    env = GpuMarioVecEnv(n, rom=rom)
+    policy = DTRollout(model, n, T, page_size=16, graphs=graphs)
+    acts, rews, dones = run_policy(env, policy, T, target_return=2.0)
+    assert acts.is_cuda and rews.is_cuda and dones.is_cuda
+    if graphs:
+        # episode 2 captures one graph per step, episode 3 replays them: same decisions
+        for _ in range(2):
+            a2, r2, d2 = run_policy(env, policy, T, target_return=2.0)
+            assert torch.equal(a2, acts) and torch.equal(r2, rews) and torch.equal(d2, dones)
+
+    ora = OracleEnv(n, *rom)
+    ro = DTRollout(model, n, T, page_size=16, graphs=graphs)
+    obs = torch.from_numpy(ora.reset()).cuda()
+    rtg = torch.full((n,), 2.0, device="cuda")
+    ts = torch.zeros(n, dtype=torch.long, device="cuda")
+    with torch.no_grad():
+        for t in range(T):
+            a, _ = ro.step(obs, rtg, ts)
+            assert torch.equal(a, acts[t]), t
+            o, r, d, _ = ora.step(a.cpu().numpy())
+            assert np.array_equal(r, rews[t].cpu().numpy()) and np.array_equal(d, dones[t].cpu().numpy().astype(bool))
+            obs = torch.from_numpy(o).cuda()
+            rtg -= torch.from_numpy(r).cuda()
+            ts += 1
+    assert len(set(acts.flatten().tolist())) > 1  # the policy does not collapse to one action
