@@ -405,8 +405,22 @@ __device__ __forceinline__ int cpu_step(NesCpu& s, const NesMem& m) {
     s.total += 7;
     return 7;
   }
-  const uint32_t op = rd(s, m, s.PC);
-  s.PC = (s.PC + 1) & 0xFFFFu;
+  // In PRG ROM (no read side effects) the two bytes after the opcode are read
+  // with it, so the operand fetch does not wait for the decode; the values are
+  // the bus reads the instruction makes at PC + 1 and PC + 2.
+  const uint32_t pc0 = s.PC;
+  const bool fast = pc0 >= 0x8000u && pc0 <= 0xFFFDu;
+  uint32_t op, p1 = 0, p2 = 0;
+  if (fast) {
+    op = prg_byte(m, pc0);
+    p1 = prg_byte(m, pc0 + 1);
+    p2 = prg_byte(m, pc0 + 2);
+  } else {
+    op = rd(s, m, pc0);
+  }
+  s.PC = (pc0 + 1) & 0xFFFFu;
+  auto opb = [&]() -> uint32_t { return fast ? p1 : rd(s, m, s.PC); };
+  auto opw = [&]() -> uint32_t { return fast ? (p1 | (p2 << 8)) : rd16(s, m, s.PC); };
   const uint32_t d = m.dec[op];
   const uint32_t mode = d & 15u, kind = (d >> 4) & 63u;
   int cyc = (int)((d >> 10) & 15u);
@@ -414,35 +428,35 @@ __device__ __forceinline__ int cpu_step(NesCpu& s, const NesMem& m) {
   bool crossed = false;
   switch (mode) {
     case NM_IMM: a = s.PC; s.PC = (s.PC + 1) & 0xFFFFu; break;
-    case NM_ZP: a = rd(s, m, s.PC); s.PC = (s.PC + 1) & 0xFFFFu; break;
-    case NM_ZPX: a = (rd(s, m, s.PC) + s.X) & 0xFFu; s.PC = (s.PC + 1) & 0xFFFFu; break;
-    case NM_ZPY: a = (rd(s, m, s.PC) + s.Y) & 0xFFu; s.PC = (s.PC + 1) & 0xFFFFu; break;
-    case NM_ABS: a = rd16(s, m, s.PC); s.PC = (s.PC + 2) & 0xFFFFu; break;
+    case NM_ZP: a = opb(); s.PC = (s.PC + 1) & 0xFFFFu; break;
+    case NM_ZPX: a = (opb() + s.X) & 0xFFu; s.PC = (s.PC + 1) & 0xFFFFu; break;
+    case NM_ZPY: a = (opb() + s.Y) & 0xFFu; s.PC = (s.PC + 1) & 0xFFFFu; break;
+    case NM_ABS: a = opw(); s.PC = (s.PC + 2) & 0xFFFFu; break;
     case NM_ABX:
     case NM_ABY: {
-      const uint32_t b = rd16(s, m, s.PC);
+      const uint32_t b = opw();
       s.PC = (s.PC + 2) & 0xFFFFu;
       a = (b + (mode == NM_ABX ? s.X : s.Y)) & 0xFFFFu;
       crossed = (a ^ b) & 0xFF00u;
       break;
     }
     case NM_IZX: {
-      const uint32_t zp = (rd(s, m, s.PC) + s.X) & 0xFFu;
+      const uint32_t zp = (opb() + s.X) & 0xFFu;
       s.PC = (s.PC + 1) & 0xFFFFu;
       a = rd16(s, m, zp);
       break;
     }
     case NM_IZY: {
-      const uint32_t zp = rd(s, m, s.PC);
+      const uint32_t zp = opb();
       s.PC = (s.PC + 1) & 0xFFFFu;
       const uint32_t b = rd16(s, m, zp);
       a = (b + s.Y) & 0xFFFFu;
       crossed = (a ^ b) & 0xFF00u;
       break;
     }
-    case NM_REL: a = rd(s, m, s.PC); s.PC = (s.PC + 1) & 0xFFFFu; break;
+    case NM_REL: a = opb(); s.PC = (s.PC + 1) & 0xFFFFu; break;
     case NM_IND: {
-      const uint32_t p = rd16(s, m, s.PC);
+      const uint32_t p = opw();
       s.PC = (s.PC + 2) & 0xFFFFu;
       const uint32_t lo = rd(s, m, p);
       a = lo | (rd(s, m, (p & 0xFF00u) | ((p + 1) & 0xFFu)) << 8);
@@ -453,19 +467,22 @@ __device__ __forceinline__ int cpu_step(NesCpu& s, const NesMem& m) {
     default: break;
   }
   if (crossed && (d & 0x4000u)) ++cyc;
+  // data operand of the read kinds: the immediate byte comes from the prefetch
+  const bool imm_fast = fast && mode == NM_IMM;
+  auto rdv = [&]() -> uint32_t { return imm_fast ? p1 : rd(s, m, a); };
   switch (kind) {
-    case NK_LDA: s.A = rd(s, m, a); zn(s, s.A); break;
-    case NK_LDX: s.X = rd(s, m, a); zn(s, s.X); break;
-    case NK_LDY: s.Y = rd(s, m, a); zn(s, s.Y); break;
+    case NK_LDA: s.A = rdv(); zn(s, s.A); break;
+    case NK_LDX: s.X = rdv(); zn(s, s.X); break;
+    case NK_LDY: s.Y = rdv(); zn(s, s.Y); break;
     case NK_STA: wr(s, m, a, s.A); break;
     case NK_STX: wr(s, m, a, s.X); break;
     case NK_STY: wr(s, m, a, s.Y); break;
-    case NK_ORA: s.A |= rd(s, m, a); zn(s, s.A); break;
-    case NK_AND: s.A &= rd(s, m, a); zn(s, s.A); break;
-    case NK_EOR: s.A ^= rd(s, m, a); zn(s, s.A); break;
+    case NK_ORA: s.A |= rdv(); zn(s, s.A); break;
+    case NK_AND: s.A &= rdv(); zn(s, s.A); break;
+    case NK_EOR: s.A ^= rdv(); zn(s, s.A); break;
     case NK_ADC:
     case NK_SBC: {
-      uint32_t v = rd(s, m, a);
+      uint32_t v = rdv();
       // A - v - !C == A + ~v + C (8 bits): one adder for both
       if (kind == NK_SBC) v ^= 0xFFu;
       const uint32_t sum = s.A + v + (s.P & FC);
@@ -479,7 +496,7 @@ __device__ __forceinline__ int cpu_step(NesCpu& s, const NesMem& m) {
     case NK_CPX:
     case NK_CPY: {
       const uint32_t reg = kind == NK_CMP ? s.A : kind == NK_CPX ? s.X : s.Y;
-      const uint32_t v = rd(s, m, a);
+      const uint32_t v = rdv();
       setc(s, reg >= v);
       zn(s, (reg - v) & 0xFFu);
       break;
