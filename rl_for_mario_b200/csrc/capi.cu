@@ -113,20 +113,6 @@ int encode_bshd(CUtensorMap* map, const void* base, bool is16, int B, int S, int
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Tensor map of `rank` dims (innermost first; byte strides of dims 1..rank-1),
-// 128-byte swizzle, zero fill outside the tensor.
-int encode_nd(CUtensorMap* map, const void* base, bool is16, int rank, const cuuint64_t* dims,
-              const cuuint64_t* strides, const cuuint32_t* box, const char* name) {
-  EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
-  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = enc(map, is16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank,
-                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(DT_ERR_INVALID, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name, (int)r);
-  return DT_OK;
-}
-
 // 2-D map over the rows of a paged cache ([num_pages * Hkv * page_size, D]),
 // box = one page of one KV head, swizzled like the decode kernel's rows.
 int encode_pages(CUtensorMap* map, const void* base, bool is16, int D, uint64_t rows, uint32_t page_size,

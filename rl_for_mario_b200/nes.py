@@ -95,7 +95,6 @@ class NESBatchGpu:
         self.chr: Optional[torch.Tensor] = None
         self._state = _State()
         self._sync_state()
-        self._obs: Optional[torch.Tensor] = None
 
     # ------------------------------------------------------------------ plumbing
     def _sync_state(self):
