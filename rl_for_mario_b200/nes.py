@@ -299,8 +299,11 @@ def run_policy(env: GpuMarioVecEnv, rollout, steps: int, target_return: float = 
     environments -> environment step): the Decision Transformer's cached
     rollout (``rollout.DTRollout``) reads the environment's stacked frames,
     its actions step the emulators (``step_device``), and the new frames feed
-    the next policy step -- no host round trip in between.  Returns device
-    tensors (actions, rewards, dones), each [steps, N]; the return-to-go
+    the next policy step -- no host round trip in between.  With the
+    environments sharded over ranks (``env`` holds this rank's slice, the
+    rollout gathers every rank's logits), each rank steps its emulators with
+    its slice of the gathered actions.  Returns device tensors (actions,
+    rewards, dones), each [steps, N] for this rank's N environments; the return-to-go
     falls by each step's reward, the timestep counts steps.  ``start_obs``:
     the frames of the first step (default: ``env.reset()``)."""
     n = env.num_envs
@@ -314,6 +317,7 @@ def run_policy(env: GpuMarioVecEnv, rollout, steps: int, target_return: float = 
     rollout.reset()
     for t in range(steps):
         a, _ = rollout.step(obs, rtg, ts, deterministic=deterministic)
+        a = a[rollout.lo:rollout.hi]
         obs, r, d, _ = env.step_device(a)
         acts[t], rews[t], dones[t] = a, r, d
         rtg -= r
