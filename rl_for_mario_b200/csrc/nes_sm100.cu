@@ -85,6 +85,7 @@ struct NesMem {
   uint8_t* oam;   // shared: [256][kNesThreads] (column tid)
   uint8_t* pal;   // shared: [32][kNesThreads]
   uint32_t* spr;  // shared: [8][kNesThreads]: x | attr << 8 | pattern << 16
+  uint8_t* ntc;   // shared: [40][kNesThreads]: the current tile row's 32 tile indices and 8 attribute bytes
   uint8_t* fbrow; // this instance's tile words of row 0: [group][240][32 tiles][32][8 B] or null
   const uint8_t* prg;
   uint32_t prg_mask;
@@ -99,6 +100,7 @@ struct NesCpu {
   uint32_t frame_ready, count, s0, dma_far, headless;
   uint32_t spr_tiles;  // tiles of this line that some listed sprite covers (bit per 8-pixel tile)
   uint32_t tile_done;  // the current tile was finished at its first pixel (no sprite over it)
+  uint32_t nt_key;     // (nametable select, tile row) held in ntc; ~0 after any VRAM write
   unsigned long long total;
   unsigned long long tbuf;  // background tile being rendered (8 palette values)
 };
@@ -129,8 +131,27 @@ __device__ __forceinline__ void bg_tile(NesCpu& s, const NesMem& m, int tx) {
   }
   const int y = s.scanline, ty = y >> 3, fy = y & 7;
   const uint32_t base = 0x2000u | ((s.ctrl & 3u) << 10);
-  const uint32_t tile = m.vram[nt_index(s.mir, base + ty * 32 + tx) * kG];
-  const uint32_t attr = m.vram[nt_index(s.mir, base + 0x3C0u + (ty >> 2) * 8 + (tx >> 2)) * kG];
+  // The 8 lines of a tile row read the same 32 tile indices and 8 attribute
+  // bytes: read them once, all at once, into shared memory (VRAM only changes
+  // through PPUDATA writes, which drop this copy).
+  const uint32_t key = ((s.ctrl & 3u) << 8) | (uint32_t)ty;
+  if (key != s.nt_key) {
+    // a row's tiles (and its attribute bytes) are consecutive bytes of one nametable
+    const uint8_t* row = m.vram + nt_index(s.mir, base + ty * 32) * kG;
+    const uint8_t* att = m.vram + nt_index(s.mir, base + 0x3C0u + (ty >> 2) * 8) * kG;
+#pragma unroll 1
+    for (int b = 0; b < 5; ++b) {
+      const uint8_t* src = b < 4 ? row + b * 8 * kG : att;
+      uint32_t v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = src[i * kG];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m.ntc[(b * 8 + i) * kNesThreads] = (uint8_t)v[i];
+    }
+    s.nt_key = key;
+  }
+  const uint32_t tile = m.ntc[tx * kNesThreads];
+  const uint32_t attr = m.ntc[(32 + (tx >> 2)) * kNesThreads];
   const uint32_t pal = (attr >> ((((ty & 3) >> 1) * 2 + ((tx & 3) >> 1)) * 2)) & 3u;
   const uint32_t pa = ((s.ctrl & 0x10u) ? 0x1000u : 0u) + tile * 16u + fy;
   const uint32_t lo = chr_byte(m, pa), hi = chr_byte(m, pa + 8);
@@ -315,8 +336,13 @@ __device__ __forceinline__ void ppu_reg_write(NesCpu& s, const NesMem& m, uint32
     case 7: {
       const uint32_t a = s.v & 0x3FFFu;
       if (a >= 0x2000u) {
-        if (a < 0x3F00u) m.vram[nt_index(s.mir, a) * kG] = (uint8_t)val;
-        else m.pal[pal_index(a - 0x3F00u) * kNesThreads] = (uint8_t)val;
+        if (a < 0x3F00u) {
+          m.vram[nt_index(s.mir, a) * kG] = (uint8_t)val;
+          s.nt_key = ~0u;
+        }
+        else {
+          m.pal[pal_index(a - 0x3F00u) * kNesThreads] = (uint8_t)val;
+        }
       }
       inc_v(s);
       break;
@@ -609,6 +635,7 @@ __device__ __forceinline__ void load_regs(NesCpu& s, const uint8_t* regs) {
   s.tbuf = 0;
   s.spr_tiles = 0;
   s.tile_done = 0;
+  s.nt_key = ~0u;
 }
 __device__ __forceinline__ void store_regs(const NesCpu& s, uint8_t* regs) {
   uint4 a, b, c;
@@ -651,6 +678,7 @@ __global__ void __launch_bounds__(kNesThreads) nes_frames_kernel(NesArgs g, int 
   __shared__ uint8_t oam_s[256 * kNesThreads];
   __shared__ uint8_t pal_s[32 * kNesThreads];
   __shared__ uint32_t spr_s[8 * kNesThreads];
+  __shared__ uint8_t ntc_s[40 * kNesThreads];
   const int tid = threadIdx.x;
   for (int i = tid; i < 256; i += kNesThreads) dec_s[i] = kNesDecode[i];
   const int inst = blockIdx.x * kNesThreads + tid;
@@ -659,6 +687,7 @@ __global__ void __launch_bounds__(kNesThreads) nes_frames_kernel(NesArgs g, int 
   m.oam = oam_s + tid;
   m.pal = pal_s + tid;
   m.spr = spr_s + tid;
+  m.ntc = ntc_s + tid;
   m.dec = dec_s;
   m.prg = g.prg;
   m.prg_mask = g.prg_size - 1;
