@@ -650,11 +650,12 @@ def bench_prefill_cfg4(dev, peaks, batch=None, model=True, cpu: bool = False):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n = 10
-    e0.record()
-    for _ in range(n):
-        attn_prefill(q, k, v, cos, sin, pad, out=out, apply_rope=False)
-    e1.record()
-    torch.cuda.synchronize()
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        e0.record()
+        for _ in range(n):
+            attn_prefill(q, k, v, cos, sin, pad, out=out, apply_rope=False)
+        e1.record()
+        torch.cuda.synchronize()
     if device_status() != 0:
         raise SystemExit("device status error in the long-prefill benchmark")
     kms = e0.elapsed_time(e1) / n
@@ -667,11 +668,19 @@ def bench_prefill_cfg4(dev, peaks, batch=None, model=True, cpu: bool = False):
     # byte time at the HBM peak (per launch); frac = that lower bound / the time.
     t_flop = flops / (peaks["bf16_tflops"] * 1e12)
     t_byte = byts / (peaks["hbm_gbs"] * 1e9)
-    bound = "tensor" if t_flop >= t_byte else "hbm"
+    # One exponential per attended score on the MUFU unit, 16 per clock per SM
+    # (measured 15.99 on this part), at the SM clock the timed region ran at.
+    exps = Hq * _attended_pairs(S, pad.cpu().tolist())
+    props = torch.cuda.get_device_properties(dev)
+    sm_hz = (clk.summary().get("sm_mhz") or 1965) * 1e6
+    t_exp = exps / (16 * props.multi_processor_count * sm_hz)
+    bound = max((t_flop, "tensor"), (t_byte, "hbm"), (t_exp, "mufu (exp2)"))[1]
     kernel_res = {"kernel": "dt_prefill_long_kernel", "inputs": "q / k rotated upstream", "batch": B, "ms": kms,
                   "tokens_per_s": B * S / (kms * 1e-3),
-                  "roofline": {"bound": bound, "lower_bound_ms": max(t_flop, t_byte) * 1e3,
-                               "frac": max(t_flop, t_byte) / (kms * 1e-3),
+                  "roofline": {"bound": bound, "lower_bound_ms": max(t_flop, t_byte, t_exp) * 1e3,
+                               "frac": max(t_flop, t_byte, t_exp) / (kms * 1e-3),
+                               "exp_lower_bound_ms": t_exp * 1e3, "exps_per_launch": exps,
+                               "exp_frac": t_exp / (kms * 1e-3),
                                "achieved_tflops": tflops, "peak_tflops": peaks["bf16_tflops"],
                                "tensor_frac": tflops / peaks["bf16_tflops"], "flops_per_launch": flops,
                                "achieved_gbs": byts / (kms * 1e-3) / 1e9, "peak_gbs": peaks["hbm_gbs"],
