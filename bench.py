@@ -938,9 +938,10 @@ def bench_conv1_cfg4(dev, peaks, batch=None):
 
 def bench_conv23_cfg4(dev, peaks, batch=None):
     """The state encoder's second and third layers at cfg4's shape (batch x 256
-    frames of the first layer's 32 x 20 x 20 output): dt_encoder_conv23 (two
-    TMA-fed tcgen05 kernels) against cuDNN's fused convolution + bias + ReLU on
-    the same channels-last bf16 tensors."""
+    frames of the first layer's 32 x 20 x 20 output): dt_encoder_conv23 (one
+    fused tcgen05 kernel; ms with layer 2's output stored, ms_without_y2 as the
+    model runs it) against cuDNN's fused convolution + bias + ReLU, one call
+    per layer, on the same channels-last bf16 tensors."""
     from rl_for_mario_b200.kernels import device_status, encoder_conv23
 
     C = PREFILL_LONG_CFG

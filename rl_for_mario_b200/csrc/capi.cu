@@ -580,7 +580,24 @@ extern "C" int dt_encoder_conv23(const void* x1, int64_t N, const void* w2, cons
   int rc = device_setup(&dev, &status);
   if (rc) return rc;
   if (g_cc_major[dev] != 10) return fail(DT_ERR_UNSUPPORTED, "%s: needs an sm_100 GPU", fn);
-  cudaError_t e = dtk::launch_encoder_conv23_sm100(x1, w2, b2, y2, w3, b3, y3, N, dtype == DT_DTYPE_BF16,
+  // x1 [N, 20, 20, 32] as (channel, x, y, frame), walked with a stride of 2
+  // pixels in x and y: a box of 8 channels x 20 x 20 pixels from (8 cg, sx,
+  // sy, f) holds the 10 x 10 pixels (2 bx + sx, 2 by + sy), i.e. one K group
+  // of the 2 x 2 space-to-depth blocks, 1,600 bytes in block order.
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(DT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  CUtensorMap mx;
+  {
+    const cuuint64_t dims[4] = {32, 20, 20, (cuuint64_t)N};
+    const cuuint64_t strides[3] = {64, 1280, 25600};
+    const cuuint32_t box[4] = {8, 20, 20, 1};
+    const cuuint32_t estr[4] = {1, 2, 2, 1};
+    CUresult r = enc(&mx, dtype == DT_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                     4, const_cast<void*>(x1), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(DT_ERR_INVALID, "%s: cuTensorMapEncodeTiled(x1) failed with CUresult %d", fn, (int)r);
+  }
+  cudaError_t e = dtk::launch_encoder_conv23_sm100(mx, w2, b2, y2, w3, b3, y3, N, dtype == DT_DTYPE_BF16,
                                                    g_num_sms[dev], status, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DT_ERR_CUDA, "%s launch: %s", fn, cudaGetErrorString(e));
   return DT_OK;

@@ -166,9 +166,11 @@ cudaError_t launch_frames_to_blocks_sm100(const void* frames, void* out, long lo
 cudaError_t launch_gemm_residual_pair_sm100(const CUtensorMap& x, const CUtensorMap& w, const CUtensorMap& y, int M,
                                             int N, int K, bool bf16, int num_sms, int* status, cudaStream_t st);
 
-// The state encoder's second (layer 2) or third (layer 3) convolution + ReLU;
-// x is the layer's input tensor map (encoder_conv23 in capi.cu), xp its base.
-cudaError_t launch_encoder_conv23_sm100(const void* x1, const void* w2, const float* b2, void* y2, const void* w3,
+// The state encoder's second and third convolutions + ReLU, fused; x1 is the
+// map of the [N, 20, 20, 32] input as (channel, x, y, frame) with traversal
+// strides (1, 2, 2, 1) and 8 x 20 x 20 x 1 boxes (one K group of the
+// space-to-depth operand per box; encoded in capi.cu).
+cudaError_t launch_encoder_conv23_sm100(const CUtensorMap& x1, const void* w2, const float* b2, void* y2, const void* w3,
                                         const float* b3, void* y3, long long n_frames, bool bf16, int num_sms,
                                         int* status, cudaStream_t st);
 
