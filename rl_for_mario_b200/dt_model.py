@@ -271,8 +271,9 @@ class MarioStateEncoder(nn.Module):
     # 262,144 frames, same fp32 accumulation and single rounding.  Off by
     # default: with it, the cfg1-shape bf16 DT's largest logit error against the
     # fp32 reference measured 1.29x the reference's own bf16 run (0.0566 vs
-    # 0.0438; mean error within 1.1x), above the 1.25x bound the parity tests
-    # hold the default path to; cuDNN's rounding pattern stays inside it.
+    # 0.0438), above the 1.25x bound the parity tests hold the default path to,
+    # although its mean error and argmax agreement over the bf16 golden cases
+    # match cuDNN's.
     _tc_conv23 = False
 
     @staticmethod
