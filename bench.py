@@ -936,6 +936,22 @@ def bench_conv1_cfg4(dev, peaks, batch=None):
                          "peak_source": peaks["source"]}}
 
 
+# Shared-memory operand bytes the fused layer-2/3 kernel's MMAs read per frame:
+# conv2 2 x 8 MMAs of 128 x 128 x 16 (4 KB of A + 4 KB of B each), conv3 3 x 4 of
+# 128 x 192 x 16 (4 KB + 6 KB); the tensor core reads them at up to 128 bytes
+# per clock per SM.
+CONV23_OPERAND_BYTES_PER_FRAME = 16 * (4096 + 4096) + 12 * (4096 + 6144)
+
+
+def conv23_bound(n_frames: int, ms: float, sm_mhz: float, n_sms: int) -> dict:
+    """The fused layer-2/3 kernel's binding resource, the shared-memory operand
+    path: its floor (operand bytes at 128 B per clock per SM, at the given SM
+    clock) and the fraction of it that `ms` reaches."""
+    floor_s = n_frames * CONV23_OPERAND_BYTES_PER_FRAME / (128.0 * n_sms * sm_mhz * 1e6)
+    return {"bound": "shared-memory operand reads", "operand_bytes_per_frame": CONV23_OPERAND_BYTES_PER_FRAME,
+            "lower_bound_ms": floor_s * 1e3, "frac": floor_s / (ms * 1e-3), "sm_mhz": sm_mhz}
+
+
 def bench_conv23_cfg4(dev, peaks, batch=None):
     """The state encoder's second and third layers at cfg4's shape (batch x 256
     frames of the first layer's 32 x 20 x 20 output): dt_encoder_conv23 (one
@@ -965,7 +981,7 @@ def bench_conv23_cfg4(dev, peaks, batch=None):
         y2 = torch.cudnn_convolution_relu(x1, w2c, b2, (2, 2), (0, 0), (1, 1), 1)
         return y2, torch.cudnn_convolution_relu(y2, w3c, b3, (1, 1), (0, 0), (1, 1), 1)
 
-    res = {}
+    res, mhz = {}, None
     for name, fn in (("ours", ours), ("ours_no_y2", ours_no_y2), ("cudnn", cudnn)):
         for _ in range(3):
             out = fn()
@@ -973,11 +989,14 @@ def bench_conv23_cfg4(dev, peaks, batch=None):
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 5
-        e0.record()
-        for _ in range(reps):
-            out = fn()
-        e1.record()
-        torch.cuda.synchronize()
+        with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+            e0.record()
+            for _ in range(reps):
+                out = fn()
+            e1.record()
+            torch.cuda.synchronize()
+        if name == "ours_no_y2":
+            mhz = clk.summary().get("sm_mhz")
         del out
         res[name] = e0.elapsed_time(e1) / reps
     if device_status() != 0:
@@ -988,8 +1007,10 @@ def bench_conv23_cfg4(dev, peaks, batch=None):
     gbs = byts / (ms * 1e-3) / 1e9
     del x1
     torch.cuda.empty_cache()
+    n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
     return {"kernel": "encoder_conv23_kernel (conv2 + conv3 fused)", "frames": n, "ms": ms,
             "ms_without_y2": res["ours_no_y2"], "cudnn_ms": res["cudnn"],
+            "roofline_operands": conv23_bound(n, res["ours_no_y2"], mhz or 1965.0, n_sms),
             "tflops": flops / (ms * 1e-3) / 1e12,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes_per_launch": byts,
