@@ -282,13 +282,23 @@ __global__ void __launch_bounds__(kC23Threads, 1)
       const uint32_t ph = (uint32_t)i & 1u;
       if (!__all_sync(0xffffffffu, mbar_wait(c3_full, ph, abort_flag, status))) return false;
       tc_fence_after();
+      // E_0, E_1, E_2 of this row and channel half: three loads in flight, one wait
+      uint32_t r0[32], r1[32], r2[32];
+      tmem_ld32_async(t_row + kTmemC3 + 32u * h, r0);
+      tmem_ld32_async(t_row + kTmemC3 + 64u + 32u * h, r1);
+      tmem_ld32_async(t_row + kTmemC3 + 128u + 32u * h, r2);
+      tmem_wait_ld3(r0, r1, r2);
+      float v[32], e1[32], e2[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        v[c] = __uint_as_float(r0[c]);
+        e1[c] = __uint_as_float(r1[c]);
+        e2[c] = __uint_as_float(r2[c]);
+      }
       if (wq == 1) {
         // publish E_1 of row 32 and E_2 of rows 32, 33 for the rows 30, 31 above
-        float e[32];
-        tmem_ld32(t_row + kTmemC3 + 64u + 32u * h, e);
-        if (lane == 0) store_row(x3s + 32 * h, e);
-        tmem_ld32(t_row + kTmemC3 + 128u + 32u * h, e);
-        if (lane < 2) store_row(x3s + (1 + lane) * 64 + 32 * h, e);
+        if (lane == 0) store_row(x3s + 32 * h, e1);
+        if (lane < 2) store_row(x3s + (1 + lane) * 64 + 32 * h, e2);
         __syncwarp();
         if (lane == 0) mbar_arrive(x3_full);
       }
@@ -297,12 +307,8 @@ __global__ void __launch_bounds__(kC23Threads, 1)
       const int oy = m / 9, ox = m - 9 * (m / 9);
       const bool valid = m < 63 && ox < 7;
       {
-        float v[32], e[32];
-        tmem_ld32(t_row + kTmemC3 + 32u * h, v);
-        tmem_ld32(t_row + kTmemC3 + 64u + 32u * h, e);
-        add_shifted<1>(v, e, lane, wq == 0 ? x3s + 32 * h : nullptr);
-        tmem_ld32(t_row + kTmemC3 + 128u + 32u * h, e);
-        add_shifted<2>(v, e, lane, wq == 0 ? x3s + 64 + 32 * h : nullptr);
+        add_shifted<1>(v, e1, lane, wq == 0 ? x3s + 32 * h : nullptr);
+        add_shifted<2>(v, e2, lane, wq == 0 ? x3s + 64 + 32 * h : nullptr);
         uint4 p[4];
         relu_pieces<BF16>(v, bias + 64 + 32 * h, p);
         if (valid) {
@@ -323,11 +329,21 @@ __global__ void __launch_bounds__(kC23Threads, 1)
       // conv3's operand buffer b is free once frame i - 2's conv3 MMAs are done
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&a3_empty[b], ph ^ 1u, abort_flag, status)))) break;
       tc_fence_after();
+      // E_0, E_1 of this row and channel half: both loads in flight, one wait
+      uint32_t r0[32], r1[32];
+      tmem_ld32_async(t_row + (uint32_t)(kN2 * b) + 32u * h, r0);
+      tmem_ld32_async(t_row + (uint32_t)(kN2 * b) + 64u + 32u * h, r1);
+      tmem_wait_ld(r0);
+      tmem_wait_ld(r1);
+      float v[32], e[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        v[c] = __uint_as_float(r0[c]);
+        e[c] = __uint_as_float(r1[c]);
+      }
       float* xb = x2s + b * 128;
       if (wq == 1 || wq == 2) {
         // publish E_1 of row 32 (warp quarter 1) / row 64 (quarter 2)
-        float e[32];
-        tmem_ld32(t_row + (uint32_t)(kN2 * b) + 64u + 32u * h, e);
         if (lane == 0) store_row(xb + (wq - 1) * 64 + 32 * h, e);
         __syncwarp();
         if (lane == 0) mbar_arrive(&x2_full[b]);
@@ -339,9 +355,6 @@ __global__ void __launch_bounds__(kC23Threads, 1)
       const int q = oy * 9 + ox;
       uint8_t* a3 = smem + kOffA3 + b * kA3Bytes;
       {
-        float v[32], e[32];
-        tmem_ld32(t_row + (uint32_t)(kN2 * b) + 32u * h, v);
-        tmem_ld32(t_row + (uint32_t)(kN2 * b) + 64u + 32u * h, e);
         add_shifted<1>(v, e, lane, wq <= 1 ? xb + wq * 64 + 32 * h : nullptr);
         uint4 p[4];
         relu_pieces<BF16>(v, bias + 32 * h, p);
