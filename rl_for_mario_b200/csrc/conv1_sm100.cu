@@ -302,6 +302,7 @@ __global__ void __launch_bounds__(kC1Threads, 1)
 constexpr int kB1Threads = 480;
 constexpr int kB1Conv = 4;          // converter warps
 constexpr int kB1Raw = 4;           // frame buffers
+constexpr int kB1Batch = 4;         // converter items per thread with loads in flight together
 constexpr int kB1FrameBytes = 4 * 84 * 84;
 constexpr int kB1ArrRows = 272;     // 11 block rows x 24 and the rows the second tile's dy = 1 atoms read past them
 
@@ -535,33 +536,48 @@ __global__ void __launch_bounds__(kB1Threads, 1)
         // items: (channel 0..3, local block row 0..10, block column 0..20), the column
         // fastest: a warp's 32-bit loads then cover consecutive words of a frame row
         // (and the next block row's, 20 banks further), nearly free of bank conflicts.
-        for (int it = ct; it < 11 * 21 * 4; it += kB1Conv * 32) {
-          const int bx = it % 21, rest = it / 21, byl = rest % 11, c = rest / 11;
-          const int by = 10 * h + byl;
-          const uint8_t* src = raw + c * 7056 + (4 * by) * 84 + 4 * bx;
-          uint32_t px[4];
+        // A thread takes kB1Batch items at a time with all their loads issued before
+        // any conversion, so that one warp per scheduler keeps several shared-memory
+        // loads in flight.
+        constexpr int kItems = 11 * 21 * 4, kStride = kB1Conv * 32;
+        for (int it0 = ct; it0 < kItems; it0 += kB1Batch * kStride) {
+          uint32_t px[kB1Batch][4];
+          int rows[kB1Batch], chans[kB1Batch];
 #pragma unroll
-          for (int ry = 0; ry < 4; ++ry) px[ry] = *reinterpret_cast<const uint32_t*>(src + ry * 84);
-          uint32_t o[8];
+          for (int u = 0; u < kB1Batch; ++u) {
+            const int it = it0 + u * kStride;
+            const int bx = it % 21, rest = it / 21, byl = rest % 11, c = rest / 11;
+            rows[u] = byl * 24 + bx;
+            chans[u] = c;
+            if (it < kItems) {
+              const uint8_t* src = raw + c * 7056 + (4 * (10 * h + byl)) * 84 + 4 * bx;
 #pragma unroll
-          for (int ry = 0; ry < 4; ++ry) {
-            if (ROUND) {
-              o[2 * ry] = E::from_f2(byte_f(px[ry], 0) * in_scale, byte_f(px[ry], 1) * in_scale);
-              o[2 * ry + 1] = E::from_f2(byte_f(px[ry], 2) * in_scale, byte_f(px[ry], 3) * in_scale);
-            } else {
-              // fp16 pairs (1024 + b0, 1024 + b1) and (1024 + b2, 1024 + b3), minus 1024: exact
-              const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
-              uint32_t lo = __byte_perm(px[ry], 0x64646464u, 0x5140);
-              uint32_t hi = __byte_perm(px[ry], 0x64646464u, 0x7362);
-              const __half2 l2 = __hsub2(*reinterpret_cast<const __half2*>(&lo), k1024);
-              const __half2 h2 = __hsub2(*reinterpret_cast<const __half2*>(&hi), k1024);
-              o[2 * ry] = *reinterpret_cast<const uint32_t*>(&l2);
-              o[2 * ry + 1] = *reinterpret_cast<const uint32_t*>(&h2);
+              for (int ry = 0; ry < 4; ++ry) px[u][ry] = *reinterpret_cast<const uint32_t*>(src + ry * 84);
             }
           }
-          const int row = byl * 24 + bx;
-          *reinterpret_cast<uint4*>(arr + sw128_off(row, 2 * c)) = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(arr + sw128_off(row, 2 * c + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+#pragma unroll
+          for (int u = 0; u < kB1Batch; ++u) {
+            if (it0 + u * kStride >= kItems) break;
+            uint32_t o[8];
+#pragma unroll
+            for (int ry = 0; ry < 4; ++ry) {
+              if (ROUND) {
+                o[2 * ry] = E::from_f2(byte_f(px[u][ry], 0) * in_scale, byte_f(px[u][ry], 1) * in_scale);
+                o[2 * ry + 1] = E::from_f2(byte_f(px[u][ry], 2) * in_scale, byte_f(px[u][ry], 3) * in_scale);
+              } else {
+                // fp16 pairs (1024 + b0, 1024 + b1) and (1024 + b2, 1024 + b3), minus 1024: exact
+                const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
+                uint32_t lo = __byte_perm(px[u][ry], 0x64646464u, 0x5140);
+                uint32_t hi = __byte_perm(px[u][ry], 0x64646464u, 0x7362);
+                const __half2 l2 = __hsub2(*reinterpret_cast<const __half2*>(&lo), k1024);
+                const __half2 h2 = __hsub2(*reinterpret_cast<const __half2*>(&hi), k1024);
+                o[2 * ry] = *reinterpret_cast<const uint32_t*>(&l2);
+                o[2 * ry + 1] = *reinterpret_cast<const uint32_t*>(&h2);
+              }
+            }
+            *reinterpret_cast<uint4*>(arr + sw128_off(rows[u], 2 * chans[u])) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(arr + sw128_off(rows[u], 2 * chans[u] + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
         }
         fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
         __syncwarp();
