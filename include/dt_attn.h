@@ -205,7 +205,7 @@ int dt_frames_conv1(const void* frames, int64_t N, int C, int H, int W, const vo
  * output (conv2 + ReLU) when given.  w2 [64, 32, 4, 4],
  * w3 [64, 64, 3, 3] 16-bit in the reference's own layout; b2, b3 [64] fp32.
  * Products accumulate in fp32, the bias is added in fp32 and each output is
- * rounded once.  bf16 or fp16.
+ * rounded once.  bf16 or fp16; N in [1, 2^30).
  */
 int dt_encoder_conv23(const void* x1, int64_t N, const void* w2, const float* b2, void* y2, const void* w3,
                       const float* b3, void* y3, int dtype, void* stream);
